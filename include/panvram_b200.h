@@ -1,0 +1,136 @@
+/* panvram_b200.h - the C ABI of panvram_b200: a B200-native decoder for panvram's refrel3 v1 random-access window
+ * path. Plain pointers and sizes; no torch types. Every entry point names the reference interface it replaces
+ * (panvram 1.0.1, paths inside that project). Device pointers are CUDA device addresses on the current device.
+ *
+ * Error convention: functions return PV_OK (0) or a PV_E* code; pv_last_error() gives the message of the calling
+ * thread's last failure. Format refusals carry the reference's text ("<path>: refused: <why>", pv_v1.h:101). */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PV_OK 0
+#define PV_EFORMAT 1      /* archive / reference refused (the reference's FormatError, pv_core.cpp:196) */
+#define PV_EARG 2         /* argument error (the reference's TORCH_CHECK -> RuntimeError, pv_cuda.cu:119-128) */
+#define PV_ECUDA 3        /* a CUDA runtime call failed */
+#define PV_EIO 4          /* file read error */
+
+/* status bits a window call ORs into its int32 status word (pv_cuda.cu:37) */
+#define PV_STATUS_DECODE 1    /* a touched block failed to decode (corrupt archive) */
+#define PV_STATUS_WAIT 4      /* a bounded wait inside a kernel expired */
+#define PV_STATUS_WINDOW 8    /* a window lies outside its assembly (or names no assembly) */
+
+#define PV_NCTX 61                 /* refrel3 model contexts (refrel3.h:24) */
+#define PV_TAB_BYTES 11264         /* per-assembly device decode table (see panvram_b200/csrc/pv_layout.h) */
+
+/* Per assembly, device record (64 bytes). */
+typedef struct pv_asm_rec {
+    uint64_t nbases;      /* bases of the assembly's stream (header offset 64) */
+    uint64_t blk_base;    /* its first entry in pv_dev_cohort.blocks */
+    uint64_t nb;          /* blocks = ceil(nbases / Q) */
+    uint64_t low_base;    /* its first lower-case run in pv_dev_cohort.low */
+    uint64_t low_cnt;     /* its lower-case run count */
+    uint64_t pad[3];
+} pv_asm_rec;
+
+/* The pooled cohort as the window kernel reads it (device addresses). Built on the host by pv_core_pools() and
+ * uploaded by the caller; it replaces the reference's pooled tensors P, pay_base, off, st, tab, blk_base, nbases,
+ * low_s, low_l, low_base, low_cnt, ref (pv_core.cpp:65-90) that windows_cuda takes (pv_cuda.cu:153-162). */
+typedef struct pv_dev_cohort {
+    const uint8_t* ref;          /* decoded reference, first base; 64 zero bytes readable on each side */
+    uint64_t ref_n;
+    const uint8_t* payload;      /* pooled rANS streams; 64 zero bytes readable after the end */
+    const uint64_t* blocks;      /* 2 words per block: payload offset | payload length << 40, start state c << 1 | dir */
+    const pv_asm_rec* asms;      /* [nasm] */
+    const uint8_t* tabs;         /* [nasm][PV_TAB_BYTES] decode tables */
+    const uint64_t* low;         /* pooled lower-case runs, [start, end) pairs, sorted per assembly */
+    int64_t nasm;
+    uint32_t Q;                  /* block size of the cohort: 1024, 2048, 4096 or 16384 */
+    uint32_t pad;
+} pv_dev_cohort;
+
+/* The host-side pooled arrays (pv_core_pools); byte sizes give the device allocation for each. The device `ref`
+ * pointer is (device copy of ref_padded) + 64. */
+typedef struct pv_host_pools {
+    const uint8_t* ref_padded; uint64_t ref_padded_bytes;
+    const uint8_t* payload; uint64_t payload_bytes;
+    const uint64_t* blocks; uint64_t blocks_bytes;
+    const pv_asm_rec* asms; uint64_t asms_bytes;
+    const uint8_t* tabs; uint64_t tabs_bytes;
+    const uint64_t* low; uint64_t low_bytes;
+    const int64_t* ctg_asm; const int64_t* ctg_local; const int64_t* ctg_boff; const int64_t* ctg_len; uint64_t ncontigs;
+} pv_host_pools;
+
+typedef struct pv_asm_info {
+    uint32_t Q; uint32_t block_hashes;
+    uint64_t bases, blocks, file_bytes, payload_bytes, contigs, lower_case_runs;
+    uint64_t fasta_xxh3, bases_xxh3;
+} pv_asm_info;
+
+typedef struct pv_core pv_core;
+
+const char* pv_last_error(void);
+
+/* ---- host: open, pool, describe (replaces panvram._C.Core, pv_core.cpp:23-183, 195-212) ---- */
+
+/* Core(reference, paths, threads, packed_reference, compact_blocks) (pv_core.cpp:32-50, bound at :198-199): read the
+ * reference FASTA (upper-cased, SHA-256), open every archive with all FORMAT section-5 checks (pv_v1.h:99-146),
+ * one block size per cohort, pool the arrays into the device layout. threads 0 = all host threads.
+ * packed_reference / compact_blocks: the reference's opt-in resident forms; refused (PV_EARG) in this build. */
+int pv_core_open(const char* reference, const char* const* paths, int64_t npaths, int threads, int packed_reference,
+                 int compact_blocks, pv_core** out);
+void pv_core_free(pv_core* c);
+int64_t pv_core_n(const pv_core* c);                    /* Core.n (pv_core.cpp:208) */
+uint32_t pv_core_q(const pv_core* c);                   /* Core.Q (:205) */
+uint64_t pv_core_ref_bases(const pv_core* c);           /* Core.ref_bases (:209) */
+void pv_core_ref_sha256(const pv_core* c, char hex[65]); /* Core.ref_sha256 (:210) */
+int pv_core_pools(const pv_core* c, pv_host_pools* out);/* Core.pools (pv_core.cpp:177-182) */
+int pv_core_info(const pv_core* c, int64_t asm_index, pv_asm_info* out);   /* Core.info (pv_core.cpp:161-163) */
+/* reference name and path strings of Core.info; NUL-terminated, truncated to cap */
+int pv_core_info_strings(const pv_core* c, int64_t asm_index, char* path, size_t path_cap, char* refname, size_t ref_cap);
+/* Core.contigs (pv_core.cpp:160): contig i of assembly a -> header, name, length, base offset, line width */
+int64_t pv_core_ncontigs(const pv_core* c, int64_t asm_index);
+int pv_core_contig(const pv_core* c, int64_t asm_index, int64_t i, char* hdr, size_t hdr_cap, char* name, size_t name_cap,
+                   uint64_t* len, uint64_t* boff, uint32_t* line_width);
+/* Core.fasta_xxh3 (pv_core.cpp:167-176): XXH3 of the FASTA rebuilt from a decoded base stream (case applied) */
+int pv_core_fasta_xxh3(const pv_core* c, int64_t asm_index, const uint8_t* bases, uint64_t nbases, uint64_t* out_hash);
+/* FASTA bytes rebuilt from a decoded base stream (case applied): size query with out == NULL; the rebuild half of
+ * Core.fasta (pv_core.cpp:138-159), whose decode half runs on the GPU here */
+int pv_core_fasta_write(const pv_core* c, int64_t asm_index, const uint8_t* bases, uint64_t nbases, uint8_t* out,
+                        uint64_t cap, uint64_t* size);
+/* block XXH3 check of a decoded upper-case stream (flag bit 0 archives; pv_v1.h:156): first bad block or -1 */
+int pv_core_check_block_hashes(const pv_core* c, int64_t asm_index, const uint8_t* upper_bases, uint64_t nbases,
+                               int64_t* first_bad);
+/* lower-case runs of assembly a applied in place to a decoded upper-case stream (pv_core.cpp:149) */
+int pv_core_apply_case(const pv_core* c, int64_t asm_index, uint8_t* bases, uint64_t nbases);
+/* sha256_file_bases (pv_core.cpp:211): SHA-256 of a FASTA's upper-cased base stream, as hex */
+int pv_sha256_file_bases(const char* path, char hex[65]);
+
+/* ---- device: the window decode (replaces windows_cuda / windows_cuda2, pv_cuda.cu:117-179) ---- */
+
+/* out[i, 0:W] = bases [start[i], start[i] + W) of assembly asm[i], lower-case runs applied (apply_case, skipped when
+ * tokens), reverse-complemented where rc[i] != 0 (rc may be NULL), then mapped to tokens A/a 0 C/c 1 G/g 2 T/t 3
+ * else 4 when tokens. asm, start: int64 [n] device; out: uint8 [n * W] device; status: int32 device word that the
+ * call ORs PV_STATUS_* bits into (the caller zeroes it). Launches on `stream` (a cudaStream_t), asynchronous.
+ * Same argument checks as pv_cuda.cu:119-128: W in [0, 2^31), n >= 0. */
+int pv_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
+               const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* stream);
+
+/* pv_windows with flags. PV_WIN_BLOCK_PATH routes every block through the general path (the whole block
+ * materialised in shared memory, ops executed in order) instead of only the blocks that need it; the output is the
+ * same, it is for testing that path on every input. */
+#define PV_WIN_BLOCK_PATH 1u
+int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
+                  const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, void* stream);
+
+/* number of kernel launches one pv_windows call with these sizes makes (0 for an empty call) */
+int pv_windows_launches(int64_t n, int64_t W);
+/* message of the calling thread's last pv_windows / pv_windows_ex argument or launch failure */
+const char* pv_kernels_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,247 @@
+"""panvram_b200._C - the binding of the native library (include/panvram_b200.h) under the names of the reference's
+extension module panvram._C (pv_core.cpp:195-220): Core, FormatError, with_cuda, sha256_file_bases, and the window
+launch that replaces windows_cuda / windows_cuda2 (pv_cuda.cu:153-179).
+
+The binding is ctypes over the C ABI: tensors cross as device pointers plus torch's current CUDA stream. There is no
+CPU decoder and no fallback: if the native library is missing, importing this module raises."""
+import ctypes
+import os
+
+import numpy as np
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libpanvram_b200.so")
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"panvram_b200 native library missing ({LIB_PATH}); build it: python panvram_b200/build.py")
+_lib = ctypes.CDLL(LIB_PATH)
+
+PV_OK, PV_EFORMAT, PV_EARG, PV_ECUDA, PV_EIO = 0, 1, 2, 3, 4
+PV_TAB_BYTES = 11264
+with_cuda = True
+
+
+class FormatError(ValueError):
+    """An archive or reference refused (the reference's panvram.FormatError, a ValueError)."""
+
+
+class AsmRec(ctypes.Structure):
+    _fields_ = [("nbases", ctypes.c_uint64), ("blk_base", ctypes.c_uint64), ("nb", ctypes.c_uint64), ("low_base", ctypes.c_uint64),
+                ("low_cnt", ctypes.c_uint64), ("pad", ctypes.c_uint64 * 3)]
+
+
+class DevCohort(ctypes.Structure):
+    _fields_ = [("ref", ctypes.c_void_p), ("ref_n", ctypes.c_uint64), ("payload", ctypes.c_void_p), ("blocks", ctypes.c_void_p),
+                ("asms", ctypes.c_void_p), ("tabs", ctypes.c_void_p), ("low", ctypes.c_void_p), ("nasm", ctypes.c_int64),
+                ("Q", ctypes.c_uint32), ("pad", ctypes.c_uint32)]
+
+
+class HostPools(ctypes.Structure):
+    _fields_ = [(k, t) for k, t in (
+        ("ref_padded", ctypes.c_void_p), ("ref_padded_bytes", ctypes.c_uint64), ("payload", ctypes.c_void_p), ("payload_bytes", ctypes.c_uint64),
+        ("blocks", ctypes.c_void_p), ("blocks_bytes", ctypes.c_uint64), ("asms", ctypes.c_void_p), ("asms_bytes", ctypes.c_uint64),
+        ("tabs", ctypes.c_void_p), ("tabs_bytes", ctypes.c_uint64), ("low", ctypes.c_void_p), ("low_bytes", ctypes.c_uint64),
+        ("ctg_asm", ctypes.c_void_p), ("ctg_local", ctypes.c_void_p), ("ctg_boff", ctypes.c_void_p), ("ctg_len", ctypes.c_void_p),
+        ("ncontigs", ctypes.c_uint64))]
+
+
+class AsmInfo(ctypes.Structure):
+    _fields_ = [("Q", ctypes.c_uint32), ("block_hashes", ctypes.c_uint32), ("bases", ctypes.c_uint64), ("blocks", ctypes.c_uint64),
+                ("file_bytes", ctypes.c_uint64), ("payload_bytes", ctypes.c_uint64), ("contigs", ctypes.c_uint64),
+                ("lower_case_runs", ctypes.c_uint64), ("fasta_xxh3", ctypes.c_uint64), ("bases_xxh3", ctypes.c_uint64)]
+
+
+_P, _I64, _U64, _I32, _U32, _SZ = ctypes.c_void_p, ctypes.c_int64, ctypes.c_uint64, ctypes.c_int, ctypes.c_uint32, ctypes.c_size_t
+for _name, _res, _args in (
+        ("pv_last_error", ctypes.c_char_p, []),
+        ("pv_kernels_last_error", ctypes.c_char_p, []),
+        ("pv_core_open", _I32, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p), _I64, _I32, _I32, _I32, ctypes.POINTER(_P)]),
+        ("pv_core_free", None, [_P]),
+        ("pv_core_n", _I64, [_P]), ("pv_core_q", _U32, [_P]), ("pv_core_ref_bases", _U64, [_P]),
+        ("pv_core_ref_sha256", None, [_P, ctypes.c_char_p]),
+        ("pv_core_pools", _I32, [_P, ctypes.POINTER(HostPools)]),
+        ("pv_core_info", _I32, [_P, _I64, ctypes.POINTER(AsmInfo)]),
+        ("pv_core_info_strings", _I32, [_P, _I64, ctypes.c_char_p, _SZ, ctypes.c_char_p, _SZ]),
+        ("pv_core_ncontigs", _I64, [_P, _I64]),
+        ("pv_core_contig", _I32, [_P, _I64, _I64, ctypes.c_char_p, _SZ, ctypes.c_char_p, _SZ, ctypes.POINTER(_U64), ctypes.POINTER(_U64),
+                                  ctypes.POINTER(_U32)]),
+        ("pv_core_fasta_xxh3", _I32, [_P, _I64, _P, _U64, ctypes.POINTER(_U64)]),
+        ("pv_core_fasta_write", _I32, [_P, _I64, _P, _U64, _P, _U64, ctypes.POINTER(_U64)]),
+        ("pv_core_check_block_hashes", _I32, [_P, _I64, _P, _U64, ctypes.POINTER(_I64)]),
+        ("pv_core_apply_case", _I32, [_P, _I64, _P, _U64]),
+        ("pv_sha256_file_bases", _I32, [ctypes.c_char_p, ctypes.c_char_p]),
+        ("pv_windows", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _P, _P, _P]),
+        ("pv_windows_ex", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _U32, _P, _P, _P]),
+        ("pv_windows_launches", _I32, [_I64, _I64])):
+    _f = getattr(_lib, _name)
+    _f.restype, _f.argtypes = _res, _args
+
+
+def _err(code):
+    msg = (_lib.pv_last_error() or b"").decode(errors="replace")
+    if code == PV_EFORMAT:
+        return FormatError(msg)
+    if code == PV_EARG:
+        return RuntimeError(msg)
+    return RuntimeError(f"panvram_b200: {msg or 'error ' + str(code)}")
+
+
+def _check(code):
+    if code:
+        raise _err(code)
+
+
+def _host_array(ptr, nbytes, dtype):
+    if not nbytes:
+        return np.zeros(0, dtype)
+    buf = (ctypes.c_uint8 * nbytes).from_address(ptr)
+    return np.frombuffer(buf, dtype=dtype)
+
+
+class Core:
+    """The opened cohort on the host (the reference's panvram._C.Core): reference + archives, every check done,
+    arrays pooled in the device layout (pools()) for the caller to move to its GPU."""
+
+    def __init__(self, reference, paths, threads=0, packed_reference=False, compact_blocks=False):
+        h = ctypes.c_void_p()
+        arr = (ctypes.c_char_p * len(paths))(*[os.fsencode(p) for p in paths])
+        _check(_lib.pv_core_open(os.fsencode(reference), arr, len(paths), int(threads), int(bool(packed_reference)),
+                                 int(bool(compact_blocks)), ctypes.byref(h)))
+        self._h, self._free = h, _lib.pv_core_free
+        self.packed_reference, self.compact_blocks = False, False
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            self._free(self._h)
+            self._h = None
+
+    Q = property(lambda self: int(_lib.pv_core_q(self._h)))
+    n = property(lambda self: int(_lib.pv_core_n(self._h)))
+    ref_bases = property(lambda self: int(_lib.pv_core_ref_bases(self._h)))
+
+    @property
+    def ref_sha256(self):
+        b = ctypes.create_string_buffer(65)
+        _lib.pv_core_ref_sha256(self._h, b)
+        return b.value.decode()
+
+    def pools(self):
+        """Host arrays in the device layout (numpy views of the core's memory), keyed by component."""
+        p = HostPools()
+        _check(_lib.pv_core_pools(self._h, ctypes.byref(p)))
+        n = p.ncontigs
+        return {
+            "ref_padded": _host_array(p.ref_padded, p.ref_padded_bytes, np.uint8),
+            "payload": _host_array(p.payload, p.payload_bytes, np.uint8),
+            "blocks": _host_array(p.blocks, p.blocks_bytes, np.uint64),
+            "asms": _host_array(p.asms, p.asms_bytes, np.uint8),
+            "tabs": _host_array(p.tabs, p.tabs_bytes, np.uint8),
+            "low": _host_array(p.low, p.low_bytes, np.uint64),
+            "ctg_asm": _host_array(p.ctg_asm, n * 8, np.int64), "ctg_local": _host_array(p.ctg_local, n * 8, np.int64),
+            "ctg_boff": _host_array(p.ctg_boff, n * 8, np.int64), "ctg_len": _host_array(p.ctg_len, n * 8, np.int64),
+        }
+
+    def _asm_check(self, i):
+        i = int(i)
+        if not 0 <= i < self.n:
+            raise FormatError("assembly index out of range")
+        return i
+
+    def info(self, i):
+        i = self._asm_check(i)
+        a = AsmInfo()
+        _check(_lib.pv_core_info(self._h, i, ctypes.byref(a)))
+        path, refname = ctypes.create_string_buffer(4096), ctypes.create_string_buffer(65536)
+        _check(_lib.pv_core_info_strings(self._h, i, path, 4096, refname, 65536))
+        return {"path": path.value.decode(), "Q": a.Q, "bases": a.bases, "blocks": a.blocks, "file_bytes": a.file_bytes,
+                "payload_bytes": a.payload_bytes, "block_hashes": bool(a.block_hashes), "fasta_xxh3": "%016x" % a.fasta_xxh3,
+                "contigs": a.contigs, "lower_case_runs": a.lower_case_runs, "reference_name": refname.value.decode()}
+
+    def contigs(self, i):
+        """[(name, header, length, offset in the base stream, line width)] (pv_core.cpp:160)."""
+        i = self._asm_check(i)
+        out = []
+        for k in range(_lib.pv_core_ncontigs(self._h, i)):
+            hdr, name = ctypes.create_string_buffer(1 << 16), ctypes.create_string_buffer(1 << 16)
+            ln, bo, lw = _U64(), _U64(), _U32()
+            _check(_lib.pv_core_contig(self._h, i, k, hdr, 1 << 16, name, 1 << 16, ctypes.byref(ln), ctypes.byref(bo), ctypes.byref(lw)))
+            out.append((name.value.decode(), hdr.value.decode(), ln.value, bo.value, lw.value))
+        return out
+
+    @staticmethod
+    def _host_u8(bases):
+        if not isinstance(bases, torch.Tensor) or bases.device.type != "cpu" or bases.dtype != torch.uint8:
+            raise FormatError("bases: uint8 CPU tensor of the assembly's length")
+        return bases.contiguous()
+
+    def fasta_xxh3(self, i, bases):
+        """XXH3 of the FASTA rebuilt from a decoded base stream (case applied), "%016x" (pv_core.cpp:167-176)."""
+        i, b = self._asm_check(i), self._host_u8(bases)
+        h = _U64()
+        code = _lib.pv_core_fasta_xxh3(self._h, i, b.data_ptr(), b.numel(), ctypes.byref(h))
+        if code:
+            raise FormatError((_lib.pv_last_error() or b"").decode())
+        return "%016x" % h.value
+
+    def fasta_bytes(self, i, bases):
+        """The FASTA file's bytes rebuilt from a decoded base stream (case applied) and the contig table."""
+        i, b = self._asm_check(i), self._host_u8(bases)
+        sz = _U64()
+        _check(_lib.pv_core_fasta_write(self._h, i, b.data_ptr(), b.numel(), None, 0, ctypes.byref(sz)))
+        buf = ctypes.create_string_buffer(max(1, sz.value))
+        _check(_lib.pv_core_fasta_write(self._h, i, b.data_ptr(), b.numel(), ctypes.cast(buf, ctypes.c_void_p), sz.value, ctypes.byref(sz)))
+        return buf.raw[:sz.value]
+
+    def first_bad_block(self, i, upper_bases):
+        i, b = self._asm_check(i), self._host_u8(upper_bases)
+        r = _I64()
+        _check(_lib.pv_core_check_block_hashes(self._h, i, b.data_ptr(), b.numel(), ctypes.byref(r)))
+        return r.value
+
+    def apply_case(self, i, bases):
+        i, b = self._asm_check(i), self._host_u8(bases)
+        if not b.is_contiguous():
+            raise FormatError("bases must be contiguous")
+        _check(_lib.pv_core_apply_case(self._h, i, b.data_ptr(), b.numel()))
+        return b
+
+
+def sha256_file_bases(path):
+    b = ctypes.create_string_buffer(65)
+    _check(_lib.pv_sha256_file_bases(os.fsencode(path), b))
+    return b.value.decode()
+
+
+PV_WIN_BLOCK_PATH = 1
+
+
+def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, out=None, status=None, flags=0):
+    """out uint8 [n, W], status int32 [1] on the cohort's device: the one-kernel window decode (pv_windows_ex).
+    dev: the DevCohort of device pointers; wasm / wstart: int64 device tensors [n]; rc: None or a [n] bool/uint8 device
+    tensor. Asynchronous on torch's current stream of that device."""
+    n, W = int(wasm.numel()), int(W)
+    if wstart.numel() != n:
+        raise RuntimeError("assembly and start counts differ")
+    if W < 0 or W >= (1 << 31):
+        raise RuntimeError("W")
+    device = wasm.device
+    if out is None:
+        out = torch.empty((n, W), dtype=torch.uint8, device=device)
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=device)
+    rp = None
+    if rc is not None:
+        if rc.numel() != n:
+            raise RuntimeError("reverse_complement mask size")
+        rp = rc.data_ptr()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    code = _lib.pv_windows_ex(ctypes.byref(dev), wasm.data_ptr(), wstart.data_ptr(), n, W, rp, int(bool(tokens)), int(bool(apply_case)),
+                              int(flags), out.data_ptr(), status.data_ptr(), stream)
+    if code:
+        msg = (_lib.pv_kernels_last_error() or b"").decode()
+        raise RuntimeError(f"panvram_b200 window launch: {msg}")
+    return out, status
+
+
+def launches_per_call(n, W):
+    return int(_lib.pv_windows_launches(int(n), int(W)))

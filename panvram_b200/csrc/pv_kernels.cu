@@ -1,0 +1,579 @@
+// pv_kernels.cu - the refrel3 v1 window decode on sm_100a (pv_windows of include/panvram_b200.h).
+//
+// Replaces the reference's three-kernel path (pv_queue_kernel -> pv_case_kernel -> pv_rc_tok_kernel,
+// pv_cuda.cu:38-147) with one kernel that writes every output byte once:
+//   * work item = (window, one block the window touches); a CTA takes `ipc` consecutive items.
+//   * phase 1, one thread per item: the block's rANS stream is decoded in full (every validity check of
+//     refrel3.h:114-160, so a corrupt block reports status 1 exactly as the reference does), keeping in shared memory
+//     only the ops and literal bytes that land inside the window.
+//   * phase 2, one warp per item: the item's output range is written in 16-byte vector stores; each lane gathers its
+//     16 bytes from the ops (reference copies realigned with funnel shifts, reverse-complement copies byte-reversed),
+//     then applies lower-case runs, reverse complement and the token map in registers.
+//   * heavy items (a self copy inside the window, or more ops / literals than a shared-memory slot holds) are
+//     decoded again by the whole CTA into a Q-byte shared block buffer, ops executed in order, then emitted the same
+//     way. Every access is bounds-checked by the decoder; the kernel has no spin waits.
+// Model tables are the compact per-assembly decode tables of pv_layout.h, read through the read-only path.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "pv_layout.h"
+
+namespace {
+
+using namespace pvb;
+
+constexpr int CTA = 128;
+constexpr int OPS_CAP = 40;    // ops inside the window per item (common path)
+constexpr int LIT_CAP = 48;    // literal bytes inside the window per item
+constexpr int RUN_CAP = 8;     // lower-case runs per item kept in shared memory
+constexpr int HOPS = 64;       // ops per chunk on the heavy path
+
+enum { ST_IDLE = 0, ST_OK = 1, ST_HEAVY = 2, ST_ERR = 3 };
+enum { DEC_DONE = 1, DEC_PAUSE = 0, DEC_ERR = -1, DEC_ABORT = -2 };
+
+struct Op { uint32_t src; uint16_t dk; uint16_t len; };   // dk: block offset | kind << 14
+__device__ __forceinline__ uint32_t op_dst(const Op& o) { return o.dk & 0x3FFFu; }
+__device__ __forceinline__ uint32_t op_kind(const Op& o) { return o.dk >> 14; }
+
+struct __align__(16) Item {
+    int64_t w;              // window index
+    uint64_t s;             // window start in the assembly's stream
+    uint64_t bst;           // block start in the stream
+    uint64_t gblk;          // pooled block index
+    int32_t a;              // assembly
+    uint32_t ox0, ox1, blen;
+    int32_t state;
+    uint16_t nops, nlits;
+    uint32_t run_first, run_cnt;
+    uint32_t pad[3];
+    Op ops[OPS_CAP];
+    uint8_t lits[LIT_CAP];
+    int32_t runs[2 * RUN_CAP];   // window-relative [start, end), clipped to the item's range
+};
+
+struct Params {
+    pv_dev_cohort C;
+    const int64_t* wasm; const int64_t* wstart; const uint8_t* rc;
+    uint8_t* out; int32_t* status;
+    uint64_t n, W, bpw, total;
+    uint32_t ipc; int tokens, apply_case, force_block;
+};
+
+// ---------------------------------------------------------------- rANS decoder (refrel3.h:69-109)
+struct Dec {
+    const uint8_t* p; const uint8_t* e;
+    uint32_t x; int bad;
+    uint32_t o, li; int prevk, nc;
+    uint64_t cc[4]; uint32_t cd[4];   // diagonal cache, most recent first
+};
+
+__device__ __forceinline__ uint32_t cum_at(uint4 r, uint32_t k) {
+    const uint32_t w = (k >> 1) == 0 ? r.x : (k >> 1) == 1 ? r.y : (k >> 1) == 2 ? r.z : r.w;
+    return (k & 1) ? (w >> 16) : (w & 0xFFFFu);
+}
+// false when the stream ran out (the reference then sets bad and returns at once, refrel3.h:80,87)
+__device__ __forceinline__ bool renorm(Dec& d) {
+    while (d.x < RANS_L) {
+        if (d.p >= d.e) { d.bad = 1; return false; }
+        d.x = (d.x << 8) | __ldg(d.p);
+        d.p++;
+    }
+    return true;
+}
+// one symbol of context c: the slot's symbol, state update, byte renormalisation (refrel3.h:76-82)
+__device__ __forceinline__ uint32_t dsym(Dec& d, const uint8_t* __restrict__ T, int c) {
+    const uint32_t slot = d.x & (MTOT - 1);
+    uint32_t s, f, cm;
+    const int bi = big_index(c);
+    if (bi < 0) {
+        const uint4 r = __ldg((const uint4*)(T + TAB_CUM8 + c * 16));
+        s = (uint32_t)((r.x >> 16) <= slot) + (uint32_t)((r.y & 0xFFFFu) <= slot) + (uint32_t)((r.y >> 16) <= slot) +
+            (uint32_t)((r.z & 0xFFFFu) <= slot) + (uint32_t)((r.z >> 16) <= slot);
+        cm = cum_at(r, s);
+        f = cum_at(r, s + 1) - cm;
+    } else {
+        const uint32_t* dn = (const uint32_t*)(T + TAB_DENSE) + bi * AB;
+        uint32_t u = __ldg(T + TAB_BIDX + bi * 256 + (slot >> 4));
+        uint32_t e = __ldg(dn + u);
+        while (dense_freq(e) && slot >= dense_cum(e) + dense_freq(e)) e = __ldg(dn + (++u));
+        s = dense_sym(e); f = dense_freq(e); cm = dense_cum(e);
+    }
+    if (!f) { d.bad = 1; return 0; }
+    d.x = f * (d.x >> PB) + slot - cm;
+    renorm(d);
+    return s;
+}
+// raw bits, at most 16 per step (refrel3.h:83-90)
+__device__ __forceinline__ uint64_t draw(Dec& d, uint32_t nb) {
+    uint64_t v = 0; uint32_t sh = 0;
+    while (nb) {
+        const uint32_t k = nb > 16 ? 16 : nb;
+        const uint32_t b = d.x & ((1u << k) - 1);
+        d.x >>= k;
+        if (!renorm(d)) return v;
+        v |= (uint64_t)b << sh; sh += k; nb -= k;
+    }
+    return v;
+}
+__device__ __forceinline__ uint64_t unbucket(uint32_t s, uint64_t extra) {
+    if (s < 16) return s;
+    const uint32_t e = (s - 16) / 4 + 4, m = (s - 16) & 3;
+    return (1ull << e) | ((uint64_t)m << (e - 2)) | extra;
+}
+__device__ __forceinline__ uint64_t dval(Dec& d, const uint8_t* T, int c) {
+    const uint32_t s = dsym(d, T, c);
+    return unbucket(s, draw(d, s < 16 ? 0 : (s - 16) / 4 + 2));
+}
+__device__ __forceinline__ int kclass(int k) { return k < 0 ? 0 : k == K_CONT ? 1 : (k == K_DELTA || k == K_REP || k == K_FLIP) ? 2 : 3; }
+__device__ __forceinline__ int llc(uint64_t ll) { return ll == 0 ? 0 : ll == 1 ? 1 : ll <= 8 ? 2 : 3; }
+__device__ __forceinline__ int64_t unzz(uint64_t z) { return (int64_t)(z >> 1) ^ -(int64_t)(z & 1); }
+__device__ __forceinline__ uint8_t comp_up(uint8_t c) { return c == 'A' ? 'T' : c == 'C' ? 'G' : c == 'G' ? 'C' : c == 'T' ? 'A' : c; }
+// the reference base the diagonal predicts at block offset o: 0..3, 4 = none (refrel3.h:104-109)
+__device__ __forceinline__ int refbase(const uint8_t* __restrict__ ref, uint64_t ref_n, uint64_t c, uint32_t dir, uint32_t o) {
+    const int64_t q = dir ? (int64_t)c - (int64_t)o : (int64_t)c + (int64_t)o;
+    if (q < 0 || (uint64_t)q >= ref_n) return 4;
+    uint8_t b = __ldg(ref + q);
+    if (dir) b = comp_up(b);
+    return b == 'A' ? 0 : b == 'C' ? 1 : b == 'G' ? 2 : b == 'T' ? 3 : 4;
+}
+__device__ __forceinline__ void dpush(Dec& d, uint64_t c, uint32_t dir) {
+    int j = 0;
+    while (j < d.nc && !(d.cc[j] == c && d.cd[j] == dir)) j++;
+    if (j == d.nc) { if (d.nc < 4) d.nc++; j = d.nc - 1; }
+    for (; j > 0; j--) { d.cc[j] = d.cc[j - 1]; d.cd[j] = d.cd[j - 1]; }
+    d.cc[0] = c; d.cd[0] = dir;
+}
+__device__ __forceinline__ void dec_init(Dec& d, const uint8_t* src, uint32_t n, int64_t st) {
+    d.p = src; d.e = src + n; d.bad = 0; d.x = 0;
+    d.o = 0; d.li = 0; d.prevk = -1; d.nc = 1;
+    d.cc[0] = (uint64_t)(st >> 1); d.cd[0] = (uint32_t)(st & 1);
+    if (n < 3) { d.bad = 1; return; }
+    d.x = (uint32_t)__ldg(src) | ((uint32_t)__ldg(src + 1) << 8) | ((uint32_t)__ldg(src + 2) << 16);
+    d.p += 3;
+}
+
+// The event loop of refrel3.h:114-160. Sinks: more() is asked before each event (false pauses, resumable),
+// lit()/op() returning false abort the decode (the caller takes another path). Returns DEC_*.
+template <class Sink>
+__device__ int decode_events(Dec& d, const uint8_t* __restrict__ T, const uint8_t* __restrict__ ref, uint64_t ref_n, uint32_t blen,
+                             Sink& sk) {
+    if (d.bad) return DEC_ERR;
+    while (d.o < blen) {
+        if (!sk.more()) return DEC_PAUSE;
+        const uint64_t ll = dval(d, T, C_LL + kclass(d.prevk));
+        if (d.bad || ll > blen - d.o) return DEC_ERR;
+        if (ll) {
+            uint32_t p1 = 16, p2 = 16;
+            for (uint32_t j = 0; j < (uint32_t)ll; j++) {
+                int c;
+                if (ll <= 8) c = C_LITR + refbase(ref, ref_n, d.cc[0], d.cd[0], d.o + j) * 2 + (j == 0 ? 1 : 0);
+                else c = C_LIT2 + (p1 == 16 ? 16 : (int)((p2 == 16 ? p1 : p2 * 4 + p1) % 16));
+                const uint32_t s = dsym(d, T, c);
+                const uint8_t byte = s == 0 ? 'A' : s == 1 ? 'C' : s == 2 ? 'G' : s == 3 ? 'T' : s == 4 ? 'N' : (uint8_t)draw(d, 8);
+                if (!sk.lit(d.o + j, byte)) return DEC_ABORT;
+                p2 = p1; p1 = s < 4 ? s : 0;
+            }
+            if (!sk.op(0, d.li, d.o, (uint32_t)ll)) return DEC_ABORT;
+            d.li += (uint32_t)ll; d.o += (uint32_t)ll;
+        }
+        if (d.o == blen) break;
+        const int kind = (int)dsym(d, T, C_KIND + llc(ll) * 4 + kclass(d.prevk));
+        uint64_t p = 0; uint32_t dir = 0; int ki = 0; int64_t dd = 0; uint64_t dist = 0;
+        if (kind == K_CONT || kind == K_DELTA) { if (kind == K_DELTA) dd = unzz(dval(d, T, C_DELTA + (ll == 0 ? 0 : 1))); }
+        else if (kind == K_REP) { ki = 1 + (int)dsym(d, T, C_REPK); dd = unzz(dval(d, T, C_REPD)); if (ki >= d.nc) return DEC_ERR; }
+        else if (kind == K_ABS) { dir = dsym(d, T, C_DIR); p = draw(d, 32); }
+        else if (kind == K_SELF) dist = dval(d, T, C_SELF);
+        else if (kind == K_FLIP) { ki = (int)dsym(d, T, C_FLIPK); dd = unzz(dval(d, T, C_FLIPD)); if (ki >= d.nc) return DEC_ERR; }
+        else return DEC_ERR;
+        const uint64_t L = dval(d, T, C_LEN + kind) + MINL;
+        if (d.bad || L > blen - d.o) return DEC_ERR;
+        uint32_t okind; uint64_t osrc;
+        if (kind == K_SELF) {
+            if (dist == 0 || dist > d.o) return DEC_ERR;
+            okind = 2; osrc = d.o - dist;
+        } else {
+            if (kind == K_FLIP) {
+                const uint64_t gc = d.cc[ki]; const uint32_t gd = d.cd[ki];
+                dir = gd ^ 1;
+                const int64_t e = (gd ? (int64_t)gc - (int64_t)d.o : (int64_t)gc + (int64_t)d.o) + dd;
+                if (e < 0) return DEC_ERR;
+                p = (uint64_t)e;
+            } else if (kind != K_ABS) {
+                const int k2 = kind == K_REP ? ki : 0;
+                const uint64_t gc = d.cc[k2]; const uint32_t gd = d.cd[k2];
+                dir = gd;
+                const int64_t e = (gd ? (int64_t)gc - (int64_t)d.o - (int64_t)L + 1 : (int64_t)gc + (int64_t)d.o) + dd;
+                if (e < 0) return DEC_ERR;
+                p = (uint64_t)e;
+            }
+            if (p > ref_n || L > ref_n - p) return DEC_ERR;
+            okind = dir ? 3 : 1; osrc = p;
+            dpush(d, dir ? (uint64_t)((int64_t)p + (int64_t)L - 1 + (int64_t)d.o) : (uint64_t)((int64_t)p - (int64_t)d.o), dir);
+        }
+        if (!sk.op(okind, osrc, d.o, (uint32_t)L)) return DEC_ABORT;
+        d.o += (uint32_t)L; d.prevk = kind;
+    }
+    if (d.bad || d.x != RANS_L || d.p != d.e) return DEC_ERR;
+    return DEC_DONE;
+}
+
+// keeps the ops and literals that fall inside [ox0, ox1) of the block
+struct WindowSink {
+    Op* ops; uint8_t* lits; uint32_t ox0, ox1, nops, nlits;
+    __device__ bool more() const { return true; }
+    __device__ bool lit(uint32_t o, uint8_t b) {
+        if (o < ox0 || o >= ox1) return true;
+        if (nlits >= LIT_CAP) return false;
+        lits[nlits++] = b;
+        return true;
+    }
+    __device__ bool op(uint32_t kind, uint64_t src, uint32_t dst, uint32_t len) {
+        if (dst >= ox1 || dst + len <= ox0) return true;
+        if (kind == 2 || nops >= OPS_CAP) return false;
+        const uint32_t lo = dst > ox0 ? dst : ox0, hi = dst + len < ox1 ? dst + len : ox1;
+        Op o; o.src = kind == 0 ? nlits - (hi - lo) : (uint32_t)src; o.dk = (uint16_t)(dst | (kind << 14)); o.len = (uint16_t)len;
+        ops[nops++] = o;
+        return true;
+    }
+};
+// heavy path: literals straight into the block buffer, copies (up to ox1) into a chunk of HOPS ops
+struct BlockSink {
+    uint8_t* buf; Op* ops; uint32_t nops, ox1;
+    __device__ bool more() const { return nops + 1 < (uint32_t)HOPS; }
+    __device__ bool lit(uint32_t o, uint8_t b) { buf[o] = b; return true; }
+    __device__ bool op(uint32_t kind, uint64_t src, uint32_t dst, uint32_t len) {
+        if (kind == 0 || dst >= ox1) return true;
+        Op o; o.src = (uint32_t)src; o.dk = (uint16_t)(dst | (kind << 14)); o.len = (uint16_t)len;
+        ops[nops++] = o;
+        return true;
+    }
+};
+
+// ---------------------------------------------------------------- 16-byte register transforms
+__device__ __forceinline__ uint32_t comp4(uint32_t w) {        // ACGTacgt complemented, case kept (pv_v1.h:74-75)
+    const uint32_t l = w | 0x20202020u;
+    const uint32_t at = __vcmpeq4(l, 0x61616161u) | __vcmpeq4(l, 0x74747474u);
+    const uint32_t cg = __vcmpeq4(l, 0x63636363u) | __vcmpeq4(l, 0x67676767u);
+    return w ^ (at & 0x15151515u) ^ (cg & 0x04040404u);
+}
+__device__ __forceinline__ uint32_t tok4(uint32_t w) {         // A/a 0, C/c 1, G/g 2, T/t 3, else 4 (pv_v1.h:76)
+    const uint32_t l = w | 0x20202020u;
+    const uint32_t ma = __vcmpeq4(l, 0x61616161u), mc = __vcmpeq4(l, 0x63636363u), mg = __vcmpeq4(l, 0x67676767u),
+                   mt = __vcmpeq4(l, 0x74747474u);
+    return (~(ma | mc | mg | mt) & 0x04040404u) | (mc & 0x01010101u) | (mg & 0x02020202u) | (mt & 0x03030303u);
+}
+__device__ __forceinline__ void rev16(uint32_t v[4]) {
+    const uint32_t a = __byte_perm(v[3], 0, 0x0123), b = __byte_perm(v[2], 0, 0x0123), c = __byte_perm(v[1], 0, 0x0123),
+                   d = __byte_perm(v[0], 0, 0x0123);
+    v[0] = a; v[1] = b; v[2] = c; v[3] = d;
+}
+__device__ __forceinline__ uint32_t bytes_mask(int k0, int k1, int i) {   // bytes of word i inside [k0, k1)
+    int lo = k0 - 4 * i, hi = k1 - 4 * i;
+    lo = lo < 0 ? 0 : lo > 4 ? 4 : lo;
+    hi = hi < 0 ? 0 : hi > 4 ? 4 : hi;
+    if (lo >= hi) return 0;
+    const uint32_t m = (hi - lo) == 4 ? 0xFFFFFFFFu : ((1u << (8 * (hi - lo))) - 1);
+    return m << (8 * lo);
+}
+__device__ __forceinline__ void merge16(uint32_t r[4], const uint32_t v[4], int k0, int k1) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) { const uint32_t m = bytes_mask(k0, k1, i); r[i] = (r[i] & ~m) | (v[i] & m); }
+}
+// 16 bytes from any address (16-byte aligned loads on both sides, funnel-shifted)
+__device__ __forceinline__ void ldg16u(const uint8_t* p, uint32_t v[4]) {
+    const uintptr_t a = (uintptr_t)p;
+    const uint4* q = (const uint4*)(a & ~(uintptr_t)15);
+    const uint32_t sh = (uint32_t)(a & 15);
+    const uint4 lo = __ldg(q);
+    if (sh == 0) { v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w; return; }
+    const uint4 hi = __ldg(q + 1);
+    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    const uint32_t j = sh >> 2, b = (sh & 3) * 8;
+    uint32_t x[5];
+#pragma unroll
+    for (int i = 0; i < 5; i++) x[i] = j == 0 ? w[i] : j == 1 ? w[i + 1] : j == 2 ? w[i + 2] : w[(i + 3) & 7];
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] = __funnelshift_r(x[i], x[i + 1], b);
+}
+
+// ---------------------------------------------------------------- gathers: raw block bytes [blo, blo + 16)
+struct OpsGather {
+    const Item* it; const uint8_t* ref;
+    __device__ void operator()(int64_t blo, uint32_t r[4]) const {
+        r[0] = r[1] = r[2] = r[3] = 0;
+        const int64_t klo = blo > (int64_t)it->ox0 ? blo : (int64_t)it->ox0;
+        const int64_t khi = blo + 16 < (int64_t)it->ox1 ? blo + 16 : (int64_t)it->ox1;
+        if (klo >= khi) return;
+        int lo = 0, hi = it->nops;                 // first op ending after klo
+        while (lo < hi) {
+            const int m = (lo + hi) >> 1;
+            if ((int64_t)op_dst(it->ops[m]) + it->ops[m].len <= klo) lo = m + 1; else hi = m;
+        }
+        for (int k = lo; k < it->nops; k++) {
+            const Op o = it->ops[k];
+            const int64_t dst = op_dst(o), len = o.len;
+            if (dst >= khi) break;
+            const int64_t a = dst > klo ? dst : klo, e = dst + len < khi ? dst + len : khi;
+            if (a >= e) continue;
+            const uint32_t kind = op_kind(o);
+            uint32_t v[4];
+            if (kind == 1) {
+                ldg16u(ref + (int64_t)o.src + (blo - dst), v);
+            } else if (kind == 3) {
+                ldg16u(ref + ((int64_t)o.src + len - 1 - (blo - dst) - 15), v);
+                rev16(v);
+#pragma unroll
+                for (int i = 0; i < 4; i++) v[i] = comp4(v[i]);
+            } else {
+                const int64_t first = dst > (int64_t)it->ox0 ? dst : (int64_t)it->ox0;
+                v[0] = v[1] = v[2] = v[3] = 0;
+                for (int64_t q = a; q < e; q++) {
+                    const uint32_t byte = it->lits[o.src + (uint32_t)(q - first)];
+                    const int kb = (int)(q - blo);
+                    v[kb >> 2] |= byte << (8 * (kb & 3));
+                }
+            }
+            merge16(r, v, (int)(a - blo), (int)(e - blo));
+        }
+    }
+};
+struct BufGather {
+    const Item* it; const uint8_t* buf;
+    __device__ void operator()(int64_t blo, uint32_t r[4]) const {
+        r[0] = r[1] = r[2] = r[3] = 0;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            const int64_t q = blo + k;
+            if (q >= (int64_t)it->ox0 && q < (int64_t)it->ox1) r[k >> 2] |= (uint32_t)buf[q] << (8 * (k & 3));
+        }
+    }
+};
+
+// lower-case mask of window positions [wp, wp + 16) (bit k = position wp + k)
+__device__ __forceinline__ uint32_t case_mask(const Item* it, const uint64_t* __restrict__ low, int64_t wp) {
+    uint32_t m = 0;
+    if (it->run_cnt <= (uint32_t)RUN_CAP) {
+        for (uint32_t r = 0; r < it->run_cnt; r++) {
+            const int64_t lo = it->runs[2 * r] > wp ? it->runs[2 * r] : wp;
+            const int64_t hi = it->runs[2 * r + 1] < wp + 16 ? it->runs[2 * r + 1] : wp + 16;
+            if (lo < hi) m |= ((1u << (hi - lo)) - 1) << (lo - wp);
+        }
+        return m;
+    }
+    const int64_t x = (int64_t)it->s + wp;              // stream position of bit 0
+    uint32_t lo = 0, hi = it->run_cnt;
+    while (lo < hi) { const uint32_t mid = (lo + hi) >> 1; if ((int64_t)__ldg(low + 2 * (it->run_first + mid) + 1) <= x) lo = mid + 1; else hi = mid; }
+    for (uint32_t r = lo; r < it->run_cnt; r++) {
+        const int64_t rs = (int64_t)__ldg(low + 2 * (it->run_first + r)), re = (int64_t)__ldg(low + 2 * (it->run_first + r) + 1);
+        if (rs >= x + 16) break;
+        const int64_t a = rs > x ? rs : x, e = re < x + 16 ? re : x + 16;
+        if (a < e) m |= ((1u << (e - a)) - 1) << (a - x);
+    }
+    return m;
+}
+
+// one item's output range in 16-byte chunks of the output row; lanes `lane` of `nl` share the chunks
+template <class Gather>
+__device__ void emit(const Params& P, const Item* it, const Gather& g, int lane, int nl) {
+    const uint64_t W = P.W;
+    const int rcw = P.rc ? (P.rc[it->w] != 0) : 0;
+    uint8_t* row = P.out + (uint64_t)it->w * W;
+    const int64_t wx0 = (int64_t)(it->bst + it->ox0 - it->s), wx1 = (int64_t)(it->bst + it->ox1 - it->s);
+    const int64_t o_lo = rcw ? (int64_t)W - wx1 : wx0, o_hi = rcw ? (int64_t)W - wx0 : wx1;
+    const uintptr_t A = (uintptr_t)(row + o_lo), B = (uintptr_t)(row + o_hi);
+    const bool cased = P.apply_case && !P.tokens && it->run_cnt;
+    for (uintptr_t ca = (A & ~(uintptr_t)15) + 16 * (uintptr_t)lane; ca < B; ca += 16 * (uintptr_t)nl) {
+        const int64_t opos = (int64_t)(ca - (uintptr_t)row);
+        const int64_t wpf = rcw ? (int64_t)W - 16 - opos : opos;      // window position of the first forward byte
+        uint32_t v[4];
+        g(wpf + (int64_t)it->s - (int64_t)it->bst, v);
+        if (cased) {
+            const uint32_t m = case_mask(it, P.C.low, wpf);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t m4 = (m >> (4 * i)) & 15u;
+                const uint32_t bm = (m4 & 1u) * 0xFFu | (m4 & 2u) * 0x7F80u | (m4 & 4u) * 0x3FC000u | (m4 & 8u) * 0x1FE00000u;
+                v[i] |= bm & 0x20202020u;
+            }
+        }
+        if (rcw) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) v[i] = comp4(v[i]);
+            rev16(v);
+        }
+        if (P.tokens) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) v[i] = tok4(v[i]);
+        }
+        if (ca >= A && ca + 16 <= B) {
+            *(uint4*)ca = make_uint4(v[0], v[1], v[2], v[3]);
+        } else {
+            for (int k = 0; k < 16; k++) {
+                const uintptr_t q = ca + (uintptr_t)k;
+                if (q >= A && q < B) *(uint8_t*)q = (uint8_t)(v[k >> 2] >> (8 * (k & 3)));
+            }
+        }
+    }
+}
+
+// phase 1 of one item: locate, decode keeping the window's ops, find its lower-case runs
+__device__ void decode_item(const Params& P, uint64_t item, Item* it) {
+    it->state = ST_IDLE;
+    if (item >= P.total) return;
+    const uint64_t w = item / P.bpw, j = item % P.bpw;
+    const int64_t a = P.wasm[w], s = P.wstart[w];
+    const pv_dev_cohort& C = P.C;
+    if (a < 0 || a >= C.nasm) { if (j == 0) atomicOr(P.status, PV_STATUS_WINDOW); return; }
+    const pv_asm_rec& R = C.asms[a];
+    if (s < 0 || (uint64_t)s + P.W > R.nbases) { if (j == 0) atomicOr(P.status, PV_STATUS_WINDOW); return; }
+    const uint64_t Q = C.Q, b0 = (uint64_t)s / Q, b1 = ((uint64_t)s + P.W - 1) / Q, b = b0 + j;
+    if (b > b1) return;
+    const uint64_t bst = b * Q, blen = R.nbases - bst < Q ? R.nbases - bst : Q;
+    const uint64_t x0 = (uint64_t)s > bst ? (uint64_t)s : bst, x1 = (uint64_t)s + P.W < bst + blen ? (uint64_t)s + P.W : bst + blen;
+    it->w = (int64_t)w; it->s = (uint64_t)s; it->bst = bst; it->gblk = R.blk_base + b; it->a = (int32_t)a;
+    it->ox0 = (uint32_t)(x0 - bst); it->ox1 = (uint32_t)(x1 - bst); it->blen = (uint32_t)blen;
+    it->run_first = 0; it->run_cnt = 0;
+    if (P.apply_case && !P.tokens && R.low_cnt) {                      // runs overlapping [x0, x1)
+        const uint64_t* low = C.low + 2 * R.low_base;
+        uint64_t lo = 0, hi = R.low_cnt;
+        while (lo < hi) { const uint64_t m = (lo + hi) >> 1; if (__ldg(low + 2 * m + 1) <= x0) lo = m + 1; else hi = m; }
+        uint64_t e = lo;
+        while (e < R.low_cnt && __ldg(low + 2 * e) < x1) e++;
+        it->run_first = (uint32_t)(R.low_base + lo); it->run_cnt = (uint32_t)(e - lo);
+        if (e - lo <= (uint64_t)RUN_CAP)
+            for (uint64_t r = lo; r < e; r++) {
+                const uint64_t rs = __ldg(low + 2 * r), re = __ldg(low + 2 * r + 1);
+                it->runs[2 * (r - lo)] = (int32_t)((rs > x0 ? rs : x0) - (uint64_t)s);
+                it->runs[2 * (r - lo) + 1] = (int32_t)((re < x1 ? re : x1) - (uint64_t)s);
+            }
+    }
+    const uint64_t loc = C.blocks[2 * it->gblk];
+    const int64_t st = (int64_t)C.blocks[2 * it->gblk + 1];
+    const uint32_t plen = loc_len(loc);
+    if (plen == (uint32_t)PV_BLEN_BAD) { it->state = ST_ERR; atomicOr(P.status, PV_STATUS_DECODE); return; }
+    if (P.force_block) { it->state = ST_HEAVY; return; }
+    Dec d;
+    dec_init(d, C.payload + loc_off(loc), plen, st);
+    WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
+    const int r = decode_events(d, C.tabs + (uint64_t)a * PV_TAB_BYTES, C.ref, C.ref_n, (uint32_t)blen, sk);
+    it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
+    if (r == DEC_DONE) it->state = ST_OK;
+    else if (r == DEC_ABORT) it->state = ST_HEAVY;
+    else { it->state = ST_ERR; atomicOr(P.status, PV_STATUS_DECODE); }
+}
+
+// the CTA decodes a heavy item into its shared block buffer, ops in order, then emits it
+__device__ void heavy_item(const Params& P, const Item* it, uint8_t* buf, Op* hops) {
+    __shared__ int h_res, h_nops;
+    __shared__ Dec h_dec;
+    const pv_dev_cohort& C = P.C;
+    const uint8_t* T = C.tabs + (uint64_t)it->a * PV_TAB_BYTES;
+    if (threadIdx.x == 0) {
+        const uint64_t loc = C.blocks[2 * it->gblk];
+        dec_init(h_dec, C.payload + loc_off(loc), loc_len(loc), (int64_t)C.blocks[2 * it->gblk + 1]);
+    }
+    for (;;) {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            Dec d = h_dec;
+            BlockSink sk{buf, hops, 0, it->ox1};
+            h_res = decode_events(d, T, C.ref, C.ref_n, it->blen, sk);
+            h_nops = (int)sk.nops;
+            h_dec = d;
+        }
+        __syncthreads();
+        const int nops = h_nops;
+        for (int k = 0; k < nops; k++) {
+            const Op o = hops[k];
+            const uint32_t dst = op_dst(o), len = o.len, kind = op_kind(o);
+            if (kind == 1) {
+                for (uint32_t i = threadIdx.x; i < len; i += CTA) buf[dst + i] = __ldg(C.ref + o.src + i);
+            } else if (kind == 3) {
+                for (uint32_t i = threadIdx.x; i < len; i += CTA) buf[dst + i] = comp_up(__ldg(C.ref + o.src + len - 1 - i));
+            } else {
+                const uint32_t dist = dst - o.src;
+                for (uint32_t c = 0; c < len;) {
+                    const uint32_t step = dist < len - c ? dist : len - c;
+                    for (uint32_t i = threadIdx.x; i < step; i += CTA) buf[dst + c + i] = buf[o.src + c + i];
+                    __syncthreads();
+                    c += step;
+                }
+            }
+            __syncthreads();
+        }
+        if (h_res != DEC_PAUSE) break;
+    }
+    if (h_res != DEC_DONE) {
+        if (threadIdx.x == 0) atomicOr(P.status, PV_STATUS_DECODE);
+        __syncthreads();
+        return;
+    }
+    emit(P, it, BufGather{it, buf}, threadIdx.x, CTA);
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(CTA) pv_windows_kernel(const Params P) {
+    extern __shared__ uint4 smem_raw[];
+    Item* items = (Item*)smem_raw;
+    uint8_t* buf = (uint8_t*)(items + P.ipc);
+    Op* hops = (Op*)(buf + P.C.Q);
+    const uint64_t item0 = (uint64_t)blockIdx.x * P.ipc;
+    for (uint32_t t = threadIdx.x; t < P.ipc; t += CTA) decode_item(P, item0 + t, &items[t]);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint32_t t = warp; t < P.ipc; t += CTA / 32)
+        if (items[t].state == ST_OK) emit(P, &items[t], OpsGather{&items[t], P.C.ref}, lane, 32);
+    for (uint32_t t = 0; t < P.ipc; t++)
+        if (items[t].state == ST_HEAVY) heavy_item(P, &items[t], buf, hops);
+}
+
+thread_local char g_cuda_err[256];
+
+}  // namespace
+
+extern "C" {
+
+const char* pv_kernels_last_error(void) { return g_cuda_err; }
+
+int pv_windows_launches(int64_t n, int64_t W) { return (n > 0 && W > 0) ? 1 : 0; }
+
+int pv_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,
+               int tokens, int apply_case, uint8_t* out, int32_t* status, void* stream) {
+    return pv_windows_ex(cohort, asm_index, start, n, W, rc, tokens, apply_case, 0u, out, status, stream);
+}
+
+int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,
+                  int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, void* stream) {
+    const uint32_t Q = cohort->Q;
+    if (!(Q == 1024 || Q == 2048 || Q == 4096 || Q == 16384)) { snprintf(g_cuda_err, sizeof g_cuda_err, "block size"); return PV_EARG; }
+    if (W < 0 || W >= (1ll << 31)) { snprintf(g_cuda_err, sizeof g_cuda_err, "W"); return PV_EARG; }
+    if (n < 0) { snprintf(g_cuda_err, sizeof g_cuda_err, "n"); return PV_EARG; }
+    if (n == 0 || W == 0) return PV_OK;
+    Params P;
+    P.C = *cohort; P.wasm = asm_index; P.wstart = start; P.rc = rc; P.out = out; P.status = status;
+    P.n = (uint64_t)n; P.W = (uint64_t)W; P.bpw = ((uint64_t)W + Q - 1) / Q + 1;
+    if ((uint64_t)n > (1ull << 62) / P.bpw) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
+    P.total = P.n * P.bpw;
+    P.tokens = tokens; P.apply_case = apply_case; P.force_block = (flags & PV_WIN_BLOCK_PATH) ? 1 : 0;
+    uint32_t ipc = 8;
+    while (ipc < 128 && P.total / ipc > 2 * 148) ipc *= 2;
+    P.ipc = ipc;
+    const uint64_t grid = (P.total + ipc - 1) / ipc;
+    if (grid >= (1ull << 31)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
+    const size_t smem = (size_t)ipc * sizeof(Item) + Q + HOPS * sizeof(Op);
+    static size_t smem_set[64] = {0};                    // the attribute is per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || smem > smem_set[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(pv_windows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
+        if (dev >= 0 && dev < 64) smem_set[dev] = smem;
+    }
+    pv_windows_kernel<<<(unsigned)grid, CTA, smem, (cudaStream_t)stream>>>(P);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
+    return PV_OK;
+}
+
+}  // extern "C"
