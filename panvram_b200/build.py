@@ -16,6 +16,7 @@ CSRC = os.path.join(PKG, "csrc")
 INC = os.path.join(ROOT, "include")
 BUILD = os.path.join(ROOT, "_build", "panvram_b200")
 LIB = os.path.join(PKG, "libpanvram_b200.so")
+SYNTH_LIB = os.path.join(PKG, "synth", "libpvsynth.so")
 CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 LIBDIR = "/usr/lib/x86_64-linux-gnu"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -55,6 +56,11 @@ def build(force=False, verbose=False, ptxas_info=False):
             log += _run(cmd, verbose)
     if force or _stale(LIB, objs):
         _run(["g++", "-shared", "-o", LIB, *objs, "-L" + os.path.join(CUDA, "lib64"), "-lcudart_static", "-ldl", "-lrt", "-lpthread",
+              os.path.join(LIBDIR, "libzstd.so.1"), os.path.join(LIBDIR, "libxxhash.so.0"), os.path.join(LIBDIR, "libcrypto.so.3")], verbose)
+    # the cohort synthesizer (test and benchmark data; not linked into the decode library)
+    src = os.path.join(PKG, "synth", "pv_synth.cpp")
+    if force or _stale(SYNTH_LIB, [src] + HEADERS):
+        _run(["g++", "-O3", "-std=c++17", "-fPIC", "-shared", "-Wall", "-I" + INC, "-I" + CSRC, src, "-o", SYNTH_LIB, "-lpthread",
               os.path.join(LIBDIR, "libzstd.so.1"), os.path.join(LIBDIR, "libxxhash.so.0"), os.path.join(LIBDIR, "libcrypto.so.3")], verbose)
     return LIB, log
 

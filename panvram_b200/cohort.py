@@ -50,6 +50,8 @@ class Cohort:
                                   low=d["low"].data_ptr(), nasm=core.n, Q=core.Q, pad=0)
         self._valid = {}
         self._info = [core.info(i) for i in range(core.n)]
+        # a list to collect (start, end) CUDA events around each window-kernel launch (measurement); None = off
+        self.kernel_events = None
 
     @classmethod
     def open(cls, path, device="cuda", dataset="q4k", reference=None, threads=0, assemblies=None,
@@ -150,7 +152,16 @@ class Cohort:
             rc = None
             if reverse_complement is not None:
                 rc = torch.as_tensor(reverse_complement).to(dev, torch.uint8).contiguous()
-            return _C.windows_cuda(self._devc, asm, start, W, rc, tokens, apply_case, out=out, status=status, flags=flags)
+            if self.kernel_events is None:
+                return _C.windows_cuda(self._devc, asm, start, W, rc, tokens, apply_case, out=out, status=status, flags=flags)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            out = torch.empty((asm.numel(), int(W)), dtype=torch.uint8, device=dev) if out is None else out
+            status = torch.zeros(1, dtype=torch.int32, device=dev) if status is None else status
+            a.record()
+            r = _C.windows_cuda(self._devc, asm, start, W, rc, tokens, apply_case, out=out, status=status, flags=flags)
+            b.record()
+            self.kernel_events.append((a, b))
+            return r
 
     def windows(self, asm, start, W, reverse_complement=None, tokens=False, check=True):
         """Bases [start, start + W) of assembly asm[i] (start = offset in the assembly's base stream: contigs
