@@ -24,7 +24,7 @@ extern "C" {
 #define PV_STATUS_WINDOW 8    /* a window lies outside its assembly (or names no assembly) */
 
 #define PV_NCTX 61                 /* refrel3 model contexts (refrel3.h:24) */
-#define PV_TAB_BYTES 11264         /* per-assembly device decode table (see panvram_b200/csrc/pv_layout.h) */
+#define PV_TAB_MAX_BYTES 8208      /* largest per-assembly device decode table (layout: panvram_b200/csrc/pv_layout.h) */
 
 /* Per assembly, device record (64 bytes). */
 typedef struct pv_asm_rec {
@@ -33,7 +33,9 @@ typedef struct pv_asm_rec {
     uint64_t nb;          /* blocks = ceil(nbases / Q) */
     uint64_t low_base;    /* its first lower-case run in pv_dev_cohort.low */
     uint64_t low_cnt;     /* its lower-case run count */
-    uint64_t pad[3];
+    uint64_t tab_off;     /* its decode table: byte offset in pv_dev_cohort.tabs (16-byte aligned) */
+    uint64_t tab_bytes;   /* and size (a multiple of 16) */
+    uint64_t pad;
 } pv_asm_rec;
 
 /* The pooled cohort as the window kernel reads it (device addresses). Built on the host by pv_core_pools() and
@@ -45,12 +47,18 @@ typedef struct pv_dev_cohort {
     const uint8_t* payload;      /* pooled rANS streams; 64 zero bytes readable after the end */
     const uint64_t* blocks;      /* 2 words per block: payload offset | payload length << 40, start state c << 1 | dir */
     const pv_asm_rec* asms;      /* [nasm] */
-    const uint8_t* tabs;         /* [nasm][PV_TAB_BYTES] decode tables */
+    const uint8_t* tabs;         /* pooled decode tables (pv_asm_rec.tab_off / tab_bytes) */
+    uint64_t tab_max;            /* the largest table's bytes */
     const uint64_t* low;         /* pooled lower-case runs, [start, end) pairs, sorted per assembly */
+    const uint8_t* cache;        /* decoded blocks (Q bytes each, upper case), 64 readable bytes on each side, or NULL */
     int64_t nasm;
     uint32_t Q;                  /* block size of the cohort: 1024, 2048, 4096 or 16384 */
     uint32_t pad;
 } pv_dev_cohort;
+
+/* Block table word 0 of a block served from pv_dev_cohort.cache: cache slot | PV_BLOCK_CACHED << 40 (the payload
+ * length field 0xFFFFFE never occurs for a block stream; 0xFFFFFF marks a stream too long to be valid). */
+#define PV_BLOCK_CACHED 0xFFFFFEull
 
 /* The host-side pooled arrays (pv_core_pools); byte sizes give the device allocation for each. The device `ref`
  * pointer is (device copy of ref_padded) + 64. */
@@ -59,7 +67,7 @@ typedef struct pv_host_pools {
     const uint8_t* payload; uint64_t payload_bytes;
     const uint64_t* blocks; uint64_t blocks_bytes;
     const pv_asm_rec* asms; uint64_t asms_bytes;
-    const uint8_t* tabs; uint64_t tabs_bytes;
+    const uint8_t* tabs; uint64_t tabs_bytes; uint64_t tab_max;
     const uint64_t* low; uint64_t low_bytes;
     const int64_t* ctg_asm; const int64_t* ctg_local; const int64_t* ctg_boff; const int64_t* ctg_len; uint64_t ncontigs;
 } pv_host_pools;
@@ -114,17 +122,23 @@ int pv_sha256_file_bases(const char* path, char hex[65]);
 /* out[i, 0:W] = bases [start[i], start[i] + W) of assembly asm[i], lower-case runs applied (apply_case, skipped when
  * tokens), reverse-complemented where rc[i] != 0 (rc may be NULL), then mapped to tokens A/a 0 C/c 1 G/g 2 T/t 3
  * else 4 when tokens. asm, start: int64 [n] device; out: uint8 [n * W] device; status: int32 device word that the
- * call ORs PV_STATUS_* bits into (the caller zeroes it). Launches on `stream` (a cudaStream_t), asynchronous.
- * Same argument checks as pv_cuda.cu:119-128: W in [0, 2^31), n >= 0. */
+ * call ORs PV_STATUS_* bits into (the caller zeroes it); work: device scratch of at least pv_windows_work_bytes()
+ * bytes (the general path's block buffers). Launches on `stream` (a cudaStream_t), asynchronous. Same argument checks
+ * as pv_cuda.cu:119-128: W in [0, 2^31), n >= 0. */
 int pv_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
-               const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* stream);
+               const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* work, size_t work_bytes,
+               void* stream);
+/* device scratch one pv_windows / pv_windows_ex call with these sizes needs (0 for an empty call) */
+size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W);
 
-/* pv_windows with flags. PV_WIN_BLOCK_PATH routes every block through the general path (the whole block
- * materialised in shared memory, ops executed in order) instead of only the blocks that need it; the output is the
- * same, it is for testing that path on every input. */
+/* pv_windows with flags and an optional per-window status. PV_WIN_BLOCK_PATH routes every block through the general
+ * path (the whole block materialised in shared memory, ops executed in order) instead of only the blocks that need
+ * it; the output is the same, it is for testing that path on every input. wstatus (NULL or uint8 [n], zeroed by the
+ * caller) receives the PV_STATUS_* bits of each window; the cohort's block cache is filled this way at open. */
 #define PV_WIN_BLOCK_PATH 1u
 int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
-                  const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, void* stream);
+                  const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, uint8_t* wstatus,
+                  void* work, size_t work_bytes, void* stream);
 
 /* number of kernel launches one pv_windows call with these sizes makes (0 for an empty call) */
 int pv_windows_launches(int64_t n, int64_t W);

@@ -17,7 +17,7 @@ if not os.path.exists(LIB_PATH):
 _lib = ctypes.CDLL(LIB_PATH)
 
 PV_OK, PV_EFORMAT, PV_EARG, PV_ECUDA, PV_EIO = 0, 1, 2, 3, 4
-PV_TAB_BYTES = 11264
+PV_TAB_MAX_BYTES = 8208
 with_cuda = True
 
 
@@ -27,12 +27,13 @@ class FormatError(ValueError):
 
 class AsmRec(ctypes.Structure):
     _fields_ = [("nbases", ctypes.c_uint64), ("blk_base", ctypes.c_uint64), ("nb", ctypes.c_uint64), ("low_base", ctypes.c_uint64),
-                ("low_cnt", ctypes.c_uint64), ("pad", ctypes.c_uint64 * 3)]
+                ("low_cnt", ctypes.c_uint64), ("tab_off", ctypes.c_uint64), ("tab_bytes", ctypes.c_uint64), ("pad", ctypes.c_uint64)]
 
 
 class DevCohort(ctypes.Structure):
     _fields_ = [("ref", ctypes.c_void_p), ("ref_n", ctypes.c_uint64), ("payload", ctypes.c_void_p), ("blocks", ctypes.c_void_p),
-                ("asms", ctypes.c_void_p), ("tabs", ctypes.c_void_p), ("low", ctypes.c_void_p), ("nasm", ctypes.c_int64),
+                ("asms", ctypes.c_void_p), ("tabs", ctypes.c_void_p), ("tab_max", ctypes.c_uint64), ("low", ctypes.c_void_p),
+                ("cache", ctypes.c_void_p), ("nasm", ctypes.c_int64),
                 ("Q", ctypes.c_uint32), ("pad", ctypes.c_uint32)]
 
 
@@ -40,7 +41,8 @@ class HostPools(ctypes.Structure):
     _fields_ = [(k, t) for k, t in (
         ("ref_padded", ctypes.c_void_p), ("ref_padded_bytes", ctypes.c_uint64), ("payload", ctypes.c_void_p), ("payload_bytes", ctypes.c_uint64),
         ("blocks", ctypes.c_void_p), ("blocks_bytes", ctypes.c_uint64), ("asms", ctypes.c_void_p), ("asms_bytes", ctypes.c_uint64),
-        ("tabs", ctypes.c_void_p), ("tabs_bytes", ctypes.c_uint64), ("low", ctypes.c_void_p), ("low_bytes", ctypes.c_uint64),
+        ("tabs", ctypes.c_void_p), ("tabs_bytes", ctypes.c_uint64), ("tab_max", ctypes.c_uint64), ("low", ctypes.c_void_p),
+        ("low_bytes", ctypes.c_uint64),
         ("ctg_asm", ctypes.c_void_p), ("ctg_local", ctypes.c_void_p), ("ctg_boff", ctypes.c_void_p), ("ctg_len", ctypes.c_void_p),
         ("ncontigs", ctypes.c_uint64))]
 
@@ -70,8 +72,9 @@ for _name, _res, _args in (
         ("pv_core_check_block_hashes", _I32, [_P, _I64, _P, _U64, ctypes.POINTER(_I64)]),
         ("pv_core_apply_case", _I32, [_P, _I64, _P, _U64]),
         ("pv_sha256_file_bases", _I32, [ctypes.c_char_p, ctypes.c_char_p]),
-        ("pv_windows", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _P, _P, _P]),
-        ("pv_windows_ex", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _U32, _P, _P, _P]),
+        ("pv_windows", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _P, _P, _P, _SZ, _P]),
+        ("pv_windows_ex", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _U32, _P, _P, _P, _P, _SZ, _P]),
+        ("pv_windows_work_bytes", _SZ, [ctypes.POINTER(DevCohort), _I64, _I64]),
         ("pv_windows_launches", _I32, [_I64, _I64])):
     _f = getattr(_lib, _name)
     _f.restype, _f.argtypes = _res, _args
@@ -135,7 +138,7 @@ class Core:
             "payload": _host_array(p.payload, p.payload_bytes, np.uint8),
             "blocks": _host_array(p.blocks, p.blocks_bytes, np.uint64),
             "asms": _host_array(p.asms, p.asms_bytes, np.uint8),
-            "tabs": _host_array(p.tabs, p.tabs_bytes, np.uint8),
+            "tabs": _host_array(p.tabs, p.tabs_bytes, np.uint8), "tab_max": int(p.tab_max),
             "low": _host_array(p.low, p.low_bytes, np.uint64),
             "ctg_asm": _host_array(p.ctg_asm, n * 8, np.int64), "ctg_local": _host_array(p.ctg_local, n * 8, np.int64),
             "ctg_boff": _host_array(p.ctg_boff, n * 8, np.int64), "ctg_len": _host_array(p.ctg_len, n * 8, np.int64),
@@ -213,12 +216,29 @@ def sha256_file_bases(path):
 
 
 PV_WIN_BLOCK_PATH = 1
+PV_BLOCK_CACHED = 0xFFFFFE
 
 
-def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, out=None, status=None, flags=0):
+_work = {}
+
+
+def work_buffer(dev, device, n, W):
+    """The device scratch a window call needs (grown and kept per device; calls on one device share it in stream
+    order, as torch's own caching allocator would)."""
+    need = int(_lib.pv_windows_work_bytes(ctypes.byref(dev), int(n), int(W)))
+    key = (device.type, device.index)
+    buf = _work.get(key)
+    if need and (buf is None or buf.numel() < need):
+        buf = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=device)
+        _work[key] = buf
+    return buf, need
+
+
+def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, out=None, status=None, flags=0, wstatus=None):
     """out uint8 [n, W], status int32 [1] on the cohort's device: the one-kernel window decode (pv_windows_ex).
     dev: the DevCohort of device pointers; wasm / wstart: int64 device tensors [n]; rc: None or a [n] bool/uint8 device
-    tensor. Asynchronous on torch's current stream of that device."""
+    tensor; wstatus: None or a zeroed uint8 device tensor of at least n bytes rounded up to 4 (per-window status).
+    Asynchronous on torch's current stream of that device."""
     n, W = int(wasm.numel()), int(W)
     if wstart.numel() != n:
         raise RuntimeError("assembly and start counts differ")
@@ -235,8 +255,12 @@ def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, o
             raise RuntimeError("reverse_complement mask size")
         rp = rc.data_ptr()
     stream = torch.cuda.current_stream(device).cuda_stream
+    if wstatus is not None and wstatus.numel() < (n + 3) // 4 * 4:
+        raise RuntimeError("wstatus: n bytes rounded up to a multiple of 4")
+    work, need = work_buffer(dev, device, n, W)
     code = _lib.pv_windows_ex(ctypes.byref(dev), wasm.data_ptr(), wstart.data_ptr(), n, W, rp, int(bool(tokens)), int(bool(apply_case)),
-                              int(flags), out.data_ptr(), status.data_ptr(), stream)
+                              int(flags), out.data_ptr(), status.data_ptr(), wstatus.data_ptr() if wstatus is not None else None,
+                              work.data_ptr() if work is not None else None, need, stream)
     if code:
         msg = (_lib.pv_kernels_last_error() or b"").decode()
         raise RuntimeError(f"panvram_b200 window launch: {msg}")

@@ -12,6 +12,7 @@ import glob
 import os
 import re
 
+import numpy as np
 import torch
 
 from . import _C
@@ -31,7 +32,7 @@ class Cohort:
     space or tab, or its index in the assembly; an assembly is its name (archive file name without .<dataset>.rr3) or
     its index."""
 
-    def __init__(self, core, names, device):
+    def __init__(self, core, names, device, block_cache=True):
         self._core, self.names, self.device = core, list(names), torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("panvram_b200 decodes on the GPU only: open the cohort with device='cuda' or 'cuda:N'")
@@ -42,25 +43,77 @@ class Cohort:
         self._ctg_names = [{c[0]: k for k, c in enumerate(core.contigs(i))} for i in range(core.n)]
         pools = core.pools()
         with torch.cuda.device(self.device):
-            self._dev = {k: torch.from_numpy(v).to(self.device) for k, v in pools.items() if not k.startswith("ctg_")}
+            self._dev = {k: torch.from_numpy(v).to(self.device) for k, v in pools.items() if not k.startswith("ctg_") and k != "tab_max"}
             self._ctg = {k: torch.from_numpy(pools[k]).to(self.device) for k in ("ctg_asm", "ctg_local", "ctg_boff", "ctg_len")}
         d = self._dev
         self._devc = _C.DevCohort(ref=d["ref_padded"].data_ptr() + 64, ref_n=core.ref_bases, payload=d["payload"].data_ptr(),
                                   blocks=d["blocks"].data_ptr(), asms=d["asms"].data_ptr(), tabs=d["tabs"].data_ptr(),
-                                  low=d["low"].data_ptr(), nasm=core.n, Q=core.Q, pad=0)
+                                  tab_max=pools["tab_max"], low=d["low"].data_ptr(), cache=None, nasm=core.n, Q=core.Q, pad=0)
         self._valid = {}
         self._info = [core.info(i) for i in range(core.n)]
         # a list to collect (start, end) CUDA events around each window-kernel launch (measurement); None = off
         self.kernel_events = None
+        self._cache, self.cached_blocks = None, 0
+        if block_cache:
+            self._build_block_cache(pools)
+
+    CACHE_BYTES = 4 << 30
+
+    def _build_block_cache(self, pools):
+        """Decode once, into an HBM cache, the blocks whose rANS stream is at least Q/32 bytes - literal-heavy novel
+        sequence, whose serial decode is many times longer than a typical block's - and point their block-table entries
+        at the cache (PV_BLOCK_CACHED): windows then copy those bytes instead of decoding them. A block that fails to
+        decode stays uncached, so a window touching it still reports status 1. At most CACHE_BYTES (the longest
+        streams first)."""
+        Q = self._core.Q
+        loc = pools["blocks"][0::2]
+        plen = (loc >> np.uint64(40)).astype(np.int64)
+        cand = np.nonzero((plen >= max(64, Q // 32)) & (plen < _C.PV_BLOCK_CACHED))[0]
+        if len(cand) == 0:
+            return
+        if len(cand) * Q > self.CACHE_BYTES:
+            cand = np.sort(cand[np.argsort(-plen[cand], kind="stable")[: self.CACHE_BYTES // Q]])
+        asms = pools["asms"].view(np.uint64).reshape(-1, 8)
+        base, nbases = asms[:, 1].astype(np.int64), asms[:, 0].astype(np.int64)
+        a = np.searchsorted(base, cand, side="right") - 1
+        start = (cand - base[a]) * Q
+        W = np.minimum(Q, nbases[a] - start)
+        order = np.concatenate([np.nonzero(W == Q)[0], np.nonzero(W < Q)[0]])
+        cand, a, start, W = cand[order], a[order], start[order], W[order]
+        n, nfull = len(cand), int((W == Q).sum())
+        dev = self.device
+        with torch.cuda.device(dev):
+            cache = torch.empty(64 + n * Q + 64, dtype=torch.uint8, device=dev)
+            ws = torch.zeros((n + 3) // 4 * 4, dtype=torch.uint8, device=dev)
+            at = torch.from_numpy(a).to(dev)
+            st = torch.from_numpy(start).to(dev)
+            if nfull:
+                _C.windows_cuda(self._devc, at[:nfull], st[:nfull], Q, None, False, False, out=cache[64:64 + nfull * Q].view(nfull, Q),
+                                wstatus=ws)
+            for i in range(nfull, n):
+                w4 = torch.zeros(4, dtype=torch.uint8, device=dev)
+                _C.windows_cuda(self._devc, at[i:i + 1], st[i:i + 1], int(W[i]), None, False, False,
+                                out=cache[64 + i * Q:64 + i * Q + int(W[i])].view(1, -1), wstatus=w4)
+                ws[i:i + 1].copy_(w4[:1])
+            ok = (ws[:n] == 0).cpu().numpy()
+            slots = np.nonzero(ok)[0]
+            if len(slots):
+                blk = self._dev["blocks"].view(torch.int64)
+                vals = torch.from_numpy((slots.astype(np.uint64) | np.uint64(_C.PV_BLOCK_CACHED << 40)).view(np.int64)).to(dev)
+                blk[torch.from_numpy(2 * cand[slots]).to(dev)] = vals
+            torch.cuda.synchronize(dev)
+        self._cache, self.cached_blocks = cache, int(len(slots))
+        self._devc.cache = cache.data_ptr() + 64
 
     @classmethod
     def open(cls, path, device="cuda", dataset="q4k", reference=None, threads=0, assemblies=None,
-             packed_reference=False, compact_blocks=False):
+             packed_reference=False, compact_blocks=False, block_cache=True):
         """Open the cohort directory `path`: every `*.<dataset>.rr3` in it (sorted by name; `assemblies` = a list of
         names to take only those) and the reference they were encoded against - `reference` if given, else
         `path/reference.fa`, else the file named in the archives' header in `path`. Every archive is checked before
         any decode (header XXH3, reference SHA-256 and size, sections, tables). One block size per cohort.
-        device: "cuda" or "cuda:N"."""
+        device: "cuda" or "cuda:N". block_cache: decode the long (literal-heavy) blocks once at open and serve them
+        from HBM (same output; see _build_block_cache)."""
         if dataset is not None and not re.fullmatch(r"q\d+k", dataset):
             raise ValueError(f"dataset: {DATASETS} (or another q<N>k suffix), or None for every *.rr3")
         pat = f"*.{dataset}.rr3" if dataset else "*.rr3"
@@ -92,7 +145,7 @@ class Cohort:
         if device.index is None:
             device = torch.device("cuda", torch.cuda.current_device())
         core = _C.Core(os.fspath(reference), [os.fspath(f) for f in files], int(threads), bool(packed_reference), bool(compact_blocks))
-        return cls(core, names, device)
+        return cls(core, names, device, block_cache=block_cache)
 
     # ------------------------------------------------------------------ description
     def __len__(self):
@@ -116,10 +169,11 @@ class Cohort:
     def resident_bytes(self):
         """Bytes of the cohort on its device (reference included), by component. Keys follow the reference's where
         the component is the same (P payload, tab model tables, ref reference); blocks is the block table (the
-        reference's off + st), low the lower-case runs (low_s + low_l), asm the per-assembly records."""
+        reference's off + st), low the lower-case runs (low_s + low_l), asm the per-assembly records, cache the decoded
+        long blocks."""
         d = self._dev
         r = {"P": d["payload"].numel(), "blocks": d["blocks"].numel() * 8, "tab": d["tabs"].numel(), "low": d["low"].numel() * 8,
-             "ref": d["ref_padded"].numel(), "asm": d["asms"].numel()}
+             "ref": d["ref_padded"].numel(), "asm": d["asms"].numel(), "cache": self._cache.numel() if self._cache is not None else 0}
         r["total"] = sum(r.values())
         return r
 
@@ -175,13 +229,8 @@ class Cohort:
                 raise RuntimeError(STATUS_TEXT.format(s))
         return out
 
-    def sample(self, n, W, generator=None, reverse_complement=False, tokens=False, return_coords=False, check=True):
-        """n windows of W bases, uniform over every (assembly, contig, start) with start + W <= contig length (a
-        window never crosses contigs) -> uint8 [n, W] on the cohort's device. generator: a torch.Generator (its device
-        draws the numbers). reverse_complement: False, True, or p in (0, 1) - each window reverse-complemented with
-        probability p. return_coords: also an int64 [n, 4] tensor (assembly, contig index, start in the contig,
-        reverse-complemented 0/1)."""
-        n, W = int(n), int(W)
+    def _draw(self, n, W, generator, reverse_complement, tokens, return_coords):
+        """The sample() sequence without the host check: (windows, coords or None, status tensor)."""
         if W <= 0 or n < 0:
             raise ValueError("W must be positive, n non-negative")
         if W not in self._valid:
@@ -206,11 +255,33 @@ class Cohort:
             if not 0 < p <= 1:
                 raise ValueError("reverse_complement: False, True or a probability")
             rc = (torch.rand(n, generator=generator, device=gdev) < p).to(self.device)
-        x = self.windows(asm, start, W, rc, tokens, check)
+        x, status = self._launch(asm, start, W, rc, tokens, True)
         if not return_coords:
-            return x
+            return x, None, status
         strand = rc.to(torch.int64) if rc is not None else torch.zeros(n, dtype=torch.int64, device=self.device)
-        return x, torch.stack([asm, self._ctg["ctg_local"][k], pos, strand], 1)
+        return x, torch.stack([asm, self._ctg["ctg_local"][k], pos, strand], 1), status
+
+    def sample(self, n, W, generator=None, reverse_complement=False, tokens=False, return_coords=False, check=True):
+        """n windows of W bases, uniform over every (assembly, contig, start) with start + W <= contig length (a
+        window never crosses contigs) -> uint8 [n, W] on the cohort's device. generator: a torch.Generator (its device
+        draws the numbers). reverse_complement: False, True, or p in (0, 1) - each window reverse-complemented with
+        probability p. return_coords: also an int64 [n, 4] tensor (assembly, contig index, start in the contig,
+        reverse-complemented 0/1)."""
+        x, coords, status = self._draw(int(n), int(W), generator, reverse_complement, tokens, return_coords)
+        if check:
+            s = int(status.item())
+            if s:
+                raise RuntimeError(STATUS_TEXT.format(s))
+        return (x, coords) if return_coords else x
+
+    def sampler(self, n, W, generator, reverse_complement=False, tokens=False, return_coords=False):
+        """sample(n, W, generator, reverse_complement, tokens, return_coords) captured once as a CUDA graph: calling
+        the returned Sampler replays it - the generator's Philox draws, the coordinate arithmetic and the decode kernel
+        in one graph launch - and gives the windows (and coordinates) the same successive sample() calls would give.
+        The outputs are the graph's static tensors, overwritten by the next call on the stream: consume them in
+        stream order, or clone. Each call checks nothing on the host; Sampler.status() reads the OR of the status
+        words since the last read (one sync)."""
+        return Sampler(self, int(n), int(W), generator, reverse_complement, tokens, return_coords)
 
     def fetch(self, assembly, contig, start, length, reverse_complement=False, tokens=False):
         """Bases [start, start + length) of a contig (0-based) -> uint8 [length] on the cohort's device."""
@@ -270,3 +341,45 @@ class Cohort:
             if "%016x" % xxhash.xxh3_64_intdigest(fa) != self._info[a]["fasta_xxh3"]:
                 raise _C.FormatError(path + ": FASTA XXH3 differs from the header")
         return fa
+
+
+class Sampler:
+    """A captured sample() call (Cohort.sampler). The graph registers the generator's state, so replays advance the
+    same Philox stream successive eager sample() calls would."""
+
+    def __init__(self, cohort, n, W, generator, reverse_complement, tokens, return_coords):
+        if generator is None or generator.device.type != "cuda":
+            raise ValueError("sampler: a CUDA torch.Generator on the cohort's device")
+        self.cohort, self.n, self.W, self.return_coords = cohort, n, W, return_coords
+        dev = cohort.device
+        args = (n, W, generator, reverse_complement, tokens, return_coords)
+        with torch.cuda.device(dev):
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            state = generator.get_state()
+            with torch.cuda.stream(side):
+                cohort._draw(*args)                              # caches the per-W prefix sums, sizes the scratch
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+            generator.set_state(state)                           # the warm-up draws are not part of the stream
+            self.graph = torch.cuda.CUDAGraph()
+            self.graph.register_generator_state(generator)
+            self._acc = torch.zeros(1, dtype=torch.int32, device=dev)
+            events, cohort.kernel_events = cohort.kernel_events, None
+            try:
+                with torch.cuda.graph(self.graph):
+                    self.x, self.coords, status = cohort._draw(*args)
+                    torch.bitwise_or(self._acc, status, out=self._acc)
+            finally:
+                cohort.kernel_events = events
+
+    def __call__(self):
+        self.graph.replay()
+        return (self.x, self.coords) if self.return_coords else self.x
+
+    def status(self):
+        """OR of the decode status words of the calls since the last status() (1 corrupt block, 4 wait expired,
+        8 window outside an assembly); one device sync."""
+        s = int(self._acc.item())
+        self._acc.zero_()
+        return s

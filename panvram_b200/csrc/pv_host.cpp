@@ -114,7 +114,10 @@ struct Arc {
     std::vector<uint16_t> freq;            // [61][104]
     std::vector<uint32_t> off;             // [nb + 1] payload offsets within the archive's payload
     std::vector<int64_t> st;               // [nb] packed start states c << 1 | dir
+    std::vector<uint8_t> tab;              // device decode table (pv_layout.h)
 };
+
+std::vector<uint8_t> build_table(const uint16_t* freq);
 
 // pv_v1.h:99-146, every check in the reference's order and with its text; the payload itself is not read here
 void open_archive(const std::string& path, const uint8_t ref_sha[32], uint64_t ref_n, Arc& X) {
@@ -207,6 +210,7 @@ void open_archive(const std::string& path, const uint8_t ref_sha[32], uint64_t r
         if (sum && sum != pvb::MTOT) bad = true;
     }
     if (bad) refuse("model tables");
+    X.tab = build_table(X.freq.data());
     if (pl >= (1ull << 32)) refuse("payload over 4 GiB (pooled offsets are 32-bit)");
     X.off.assign(X.nb + 1, 0); X.st.assign(X.nb, 0);
     uint64_t prevc = 0; uint32_t prevd = 0, acc = 0;
@@ -227,12 +231,14 @@ void open_archive(const std::string& path, const uint8_t ref_sha[32], uint64_t r
     X.payload_bytes = pl; X.payload_at = pstart; X.file_bytes = n; X.path = path;
 }
 
-// the per-assembly decode table of pv_layout.h from the model frequencies
-void build_table(const uint16_t* freq, uint8_t* out) {
-    memset(out, 0, PV_TAB_BYTES);
-    uint16_t* cum8 = (uint16_t*)(out + pvb::TAB_CUM8);
-    uint8_t* bidx = out + pvb::TAB_BIDX;
-    uint32_t* dense = (uint32_t*)(out + pvb::TAB_DENSE);
+// the per-assembly decode table of pv_layout.h from the model frequencies (its size is a multiple of 16)
+std::vector<uint8_t> build_table(const uint16_t* freq) {
+    std::vector<uint8_t> out((size_t)pvb::TAB_MAX, 0);
+    uint16_t* cum8 = (uint16_t*)(out.data() + pvb::TAB_CUM8);
+    uint8_t* bidx = out.data() + pvb::TAB_BIDX;
+    uint16_t* doff = (uint16_t*)(out.data() + pvb::TAB_DOFF);
+    uint32_t* dense = (uint32_t*)(out.data() + pvb::TAB_DENSE);
+    uint32_t nd = 0;
     for (int c = 0; c < pvb::NCTX; c++) {
         const int A = pvb::alpha(c);
         const uint16_t* f = freq + (size_t)c * pvb::AB;
@@ -243,17 +249,23 @@ void build_table(const uint16_t* freq, uint8_t* out) {
             for (int k = 0; k < 8; k++) cum8[c * 8 + k] = (uint16_t)cum[std::min(k, A)];
             continue;
         }
-        uint32_t* d = dense + bi * pvb::AB;
+        doff[bi] = (uint16_t)nd;
+        uint32_t* d = dense + nd;
         int nu = 0;
         for (int s = 0; s < A; s++) if (f[s]) d[nu++] = pvb::dense_entry(cum[s], f[s], (uint32_t)s);
-        uint8_t* bx = bidx + bi * 256;
+        if (!nu) d[nu++] = 0;                                  // an unused context: one zero-frequency entry
+        uint8_t* bx = bidx + bi * (4096 / pvb::TAB_BUCKET);
         int u = 0;
-        for (int k = 0; k < 256 && nu; k++) {
-            const uint32_t slot = (uint32_t)k * 16;
+        for (int k = 0; k < 4096 / pvb::TAB_BUCKET; k++) {
+            const uint32_t slot = (uint32_t)k * pvb::TAB_BUCKET;
             while (u + 1 < nu && slot >= pvb::dense_cum(d[u]) + pvb::dense_freq(d[u])) u++;
             bx[k] = (uint8_t)u;
         }
+        nd += (uint32_t)nu;
     }
+    doff[pvb::NBIG] = (uint16_t)nd;
+    out.resize(((size_t)pvb::TAB_DENSE + 4 * nd + 15) & ~(size_t)15);
+    return out;
 }
 
 uint64_t fasta_size(const Arc& X) {
@@ -277,6 +289,7 @@ struct pv_core {
     std::vector<uint64_t> blocks, low;
     std::vector<pv_asm_rec> asms;
     std::vector<uint8_t> tabs;
+    uint64_t tab_max = 0;
     std::vector<int64_t> ctg_asm, ctg_local, ctg_boff, ctg_len;
 };
 
@@ -295,17 +308,18 @@ void load_reference(pv_core& C, const std::string& path) {
 
 void pool(pv_core& C, const std::vector<std::string>& paths) {
     const size_t n = C.A.size();
-    std::vector<uint64_t> pb(n), bb(n), lb(n), cb(n);
-    uint64_t sp = 0, sb = 0, sl = 0, sc = 0;
+    std::vector<uint64_t> pb(n), bb(n), lb(n), cb(n), tb(n);
+    uint64_t sp = 0, sb = 0, sl = 0, sc = 0, st = 0;
     for (size_t i = 0; i < n; i++) {
-        pb[i] = sp; bb[i] = sb; lb[i] = sl; cb[i] = sc;
-        sp += C.A[i].payload_bytes; sb += C.A[i].nb; sl += C.A[i].low_s.size(); sc += C.A[i].rec.size();
+        pb[i] = sp; bb[i] = sb; lb[i] = sl; cb[i] = sc; tb[i] = st;
+        sp += C.A[i].payload_bytes; sb += C.A[i].nb; sl += C.A[i].low_s.size(); sc += C.A[i].rec.size(); st += C.A[i].tab.size();
+        C.tab_max = std::max<uint64_t>(C.tab_max, C.A[i].tab.size());
     }
     C.payload.assign(sp + 64, 0);
     C.blocks.assign(2 * std::max<uint64_t>(1, sb), 0);
     C.low.assign(2 * std::max<uint64_t>(1, sl), 0);
     C.asms.assign(n, pv_asm_rec{});
-    C.tabs.assign(n * (size_t)PV_TAB_BYTES, 0);
+    C.tabs.assign(std::max<uint64_t>(16, st), 0);
     C.ctg_asm.assign(sc, 0); C.ctg_local.assign(sc, 0); C.ctg_boff.assign(sc, 0); C.ctg_len.assign(sc, 0);
     std::mutex mu; std::string first;
     parallel_for(n, C.threads, [&](uint64_t i) {
@@ -320,13 +334,14 @@ void pool(pv_core& C, const std::vector<std::string>& paths) {
             }
             pv_asm_rec& r = C.asms[i];
             r.nbases = X.nbases; r.blk_base = bb[i]; r.nb = X.nb; r.low_base = lb[i]; r.low_cnt = X.low_s.size();
+            r.tab_off = tb[i]; r.tab_bytes = X.tab.size();
             for (size_t k = 0; k < X.low_s.size(); k++) { C.low[2 * (lb[i] + k)] = X.low_s[k]; C.low[2 * (lb[i] + k) + 1] = X.low_s[k] + X.low_l[k]; }
-            build_table(X.freq.data(), C.tabs.data() + i * (size_t)PV_TAB_BYTES);
+            memcpy(C.tabs.data() + tb[i], X.tab.data(), X.tab.size());
             for (size_t k = 0; k < X.rec.size(); k++) {
                 C.ctg_asm[cb[i] + k] = (int64_t)i; C.ctg_local[cb[i] + k] = (int64_t)k;
                 C.ctg_boff[cb[i] + k] = (int64_t)X.rec[k].boff; C.ctg_len[cb[i] + k] = (int64_t)X.rec[k].len;
             }
-            std::vector<uint32_t>().swap(X.off); std::vector<int64_t>().swap(X.st);
+            std::vector<uint32_t>().swap(X.off); std::vector<int64_t>().swap(X.st); std::vector<uint8_t>().swap(X.tab);
         } catch (const std::exception& e) {
             std::lock_guard<std::mutex> g(mu);
             if (first.empty()) first = e.what();
@@ -395,7 +410,7 @@ int pv_core_pools(const pv_core* c, pv_host_pools* o) {
     o->payload = c->payload.data(); o->payload_bytes = c->payload.size();
     o->blocks = c->blocks.data(); o->blocks_bytes = c->blocks.size() * 8;
     o->asms = c->asms.data(); o->asms_bytes = c->asms.size() * sizeof(pv_asm_rec);
-    o->tabs = c->tabs.data(); o->tabs_bytes = c->tabs.size();
+    o->tabs = c->tabs.data(); o->tabs_bytes = c->tabs.size(); o->tab_max = c->tab_max;
     o->low = c->low.data(); o->low_bytes = c->low.size() * 8;
     o->ctg_asm = c->ctg_asm.data(); o->ctg_local = c->ctg_local.data(); o->ctg_boff = c->ctg_boff.data(); o->ctg_len = c->ctg_len.data();
     o->ncontigs = c->ctg_asm.size();

@@ -2,17 +2,18 @@
 //
 // Replaces the reference's three-kernel path (pv_queue_kernel -> pv_case_kernel -> pv_rc_tok_kernel,
 // pv_cuda.cu:38-147) with one kernel that writes every output byte once:
-//   * work item = (window, one block the window touches); a CTA takes `ipc` consecutive items.
-//   * phase 1, one thread per item: the block's rANS stream is decoded in full (every validity check of
-//     refrel3.h:114-160, so a corrupt block reports status 1 exactly as the reference does), keeping in shared memory
-//     only the ops and literal bytes that land inside the window.
-//   * phase 2, one warp per item: the item's output range is written in 16-byte vector stores; each lane gathers its
-//     16 bytes from the ops (reference copies realigned with funnel shifts, reverse-complement copies byte-reversed),
-//     then applies lower-case runs, reverse complement and the token map in registers.
-//   * heavy items (a self copy inside the window, or more ops / literals than a shared-memory slot holds) are
-//     decoded again by the whole CTA into a Q-byte shared block buffer, ops executed in order, then emitted the same
-//     way. Every access is bounds-checked by the decoder; the kernel has no spin waits.
-// Model tables are the compact per-assembly decode tables of pv_layout.h, read through the read-only path.
+//   * work item = (window, one block the window touches); one item per warp, WARPS warps per CTA.
+//   * lane 0 stages the assembly's compact decode table (pv_layout.h) and the block's rANS stream into the warp's
+//     shared slot with TMA bulk copies completing on an mbarrier (bounded wait: status 4), and prefetches into L2 the
+//     reference span the block's start diagonal covers; then it decodes the stream in full (every validity check of
+//     refrel3.h:114-160, so a corrupt block reports status 1 exactly as the reference does), keeping only the ops and
+//     literal bytes that land inside the window. Each block's serial rANS chain runs in its own warp, so the chains'
+//     memory latencies overlap across warps instead of serialising inside one.
+//   * the warp then writes the item's output range in 16-byte vector stores; each lane gathers its 16 bytes from the
+//     ops (reference copies realigned with funnel shifts, reverse-complement copies byte-reversed), then applies
+//     lower-case runs, reverse complement and the token map in registers.
+//   * heavy items (a self copy inside the window, or more ops / literals than a slot holds) are decoded again by the
+//     whole CTA into a Q-byte shared block buffer, ops executed in order, then emitted the same way.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -24,12 +25,12 @@ namespace {
 using namespace pvb;
 
 constexpr int CTA = 128;
-constexpr int OPS_CAP = 40;    // ops inside the window per item (common path)
-constexpr int LIT_CAP = 48;    // literal bytes inside the window per item
+constexpr int OPS_CAP = 64;    // ops inside the window per item (common path)
+constexpr int LIT_CAP = 128;   // literal bytes inside the window per item
 constexpr int RUN_CAP = 8;     // lower-case runs per item kept in shared memory
 constexpr int HOPS = 64;       // ops per chunk on the heavy path
 
-enum { ST_IDLE = 0, ST_OK = 1, ST_HEAVY = 2, ST_ERR = 3 };
+enum { ST_IDLE = 0, ST_OK = 1, ST_HEAVY = 2, ST_ERR = 3, ST_CACHED = 4 };
 enum { DEC_DONE = 1, DEC_PAUSE = 0, DEC_ERR = -1, DEC_ABORT = -2 };
 
 struct Op { uint32_t src; uint16_t dk; uint16_t len; };   // dk: block offset | kind << 14
@@ -41,12 +42,15 @@ struct __align__(16) Item {
     uint64_t s;             // window start in the assembly's stream
     uint64_t bst;           // block start in the stream
     uint64_t gblk;          // pooled block index
+    const uint8_t* cptr;    // the block's decoded bytes in the cohort's block cache (ST_CACHED)
+    uint64_t tab_off;       // the assembly's decode table in the pooled tables
     int32_t a;              // assembly
     uint32_t ox0, ox1, blen;
     int32_t state;
     uint16_t nops, nlits;
     uint32_t run_first, run_cnt;
-    uint32_t pad[3];
+    uint32_t tab_bytes, span_len;   // span_len: bytes of the reference staged in the slot (from position span_lo)
+    int64_t span_lo;
     Op ops[OPS_CAP];
     uint8_t lits[LIT_CAP];
     int32_t runs[2 * RUN_CAP];   // window-relative [start, end), clipped to the item's range
@@ -55,54 +59,77 @@ struct __align__(16) Item {
 struct Params {
     pv_dev_cohort C;
     const int64_t* wasm; const int64_t* wstart; const uint8_t* rc;
-    uint8_t* out; int32_t* status;
+    uint8_t* out; int32_t* status; uint8_t* wstatus;
+    uint8_t* work;                 // block-path buffers in global memory: Q bytes per CTA
     uint64_t n, W, bpw, total;
-    uint32_t ipc; int tokens, apply_case, force_block;
+    uint32_t slot_bytes, tab_area, pay_cap, span_cap;   // a warp's shared slot: Item | table | payload | reference span
+    int tokens, apply_case, force_block;
 };
 
+// status bits into the call's word and, when asked, into the window's byte (4-byte aligned, padded array)
+__device__ __forceinline__ void report(const Params& P, uint64_t w, int bits) {
+    atomicOr(P.status, bits);
+    if (P.wstatus) atomicOr((unsigned int*)(P.wstatus + (w & ~3ull)), (unsigned int)bits << (8 * (w & 3)));
+}
+
 // ---------------------------------------------------------------- rANS decoder (refrel3.h:69-109)
+// The decoder state is all scalar - the four-entry diagonal cache as named registers, indexed by selects - so that,
+// inlined, the block's serial rANS chain stays in registers and never round-trips through local memory.
 struct Dec {
     const uint8_t* p; const uint8_t* e;
     uint32_t x; int bad;
     uint32_t o, li; int prevk, nc;
-    uint64_t cc[4]; uint32_t cd[4];   // diagonal cache, most recent first
+    uint64_t c0, c1, c2, c3; uint32_t d0, d1, d2, d3;   // diagonal cache, most recent first
 };
+
+// shared-memory loads by 32-bit shared address (the decode tables are staged there by a TMA bulk copy)
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) { uint32_t v; asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a)); return v; }
+__device__ __forceinline__ uint32_t lds16(uint32_t a) { uint16_t v; asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a)); return v; }
+__device__ __forceinline__ uint32_t lds8(uint32_t a) { uint16_t v; asm volatile("ld.shared.u8 %0, [%1];" : "=h"(v) : "r"(a)); return v; }
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 __device__ __forceinline__ uint32_t cum_at(uint4 r, uint32_t k) {
     const uint32_t w = (k >> 1) == 0 ? r.x : (k >> 1) == 1 ? r.y : (k >> 1) == 2 ? r.z : r.w;
     return (k & 1) ? (w >> 16) : (w & 0xFFFFu);
 }
-// false when the stream ran out (the reference then sets bad and returns at once, refrel3.h:80,87)
+// byte renormalisation; false when the stream ran out (the reference then sets bad and returns at once,
+// refrel3.h:80,87). Stream bytes come from shared memory when the block's payload was staged, else global memory.
 __device__ __forceinline__ bool renorm(Dec& d) {
     while (d.x < RANS_L) {
         if (d.p >= d.e) { d.bad = 1; return false; }
-        d.x = (d.x << 8) | __ldg(d.p);
+        d.x = (d.x << 8) | *d.p;
         d.p++;
     }
     return true;
 }
-// one symbol of context c: the slot's symbol, state update, byte renormalisation (refrel3.h:76-82)
-__device__ __forceinline__ uint32_t dsym(Dec& d, const uint8_t* __restrict__ T, int c) {
-    const uint32_t slot = d.x & (MTOT - 1);
-    uint32_t s, f, cm;
-    const int bi = big_index(c);
-    if (bi < 0) {
-        const uint4 r = __ldg((const uint4*)(T + TAB_CUM8 + c * 16));
-        s = (uint32_t)((r.x >> 16) <= slot) + (uint32_t)((r.y & 0xFFFFu) <= slot) + (uint32_t)((r.y >> 16) <= slot) +
-            (uint32_t)((r.z & 0xFFFFu) <= slot) + (uint32_t)((r.z >> 16) <= slot);
-        cm = cum_at(r, s);
-        f = cum_at(r, s + 1) - cm;
-    } else {
-        const uint32_t* dn = (const uint32_t*)(T + TAB_DENSE) + bi * AB;
-        uint32_t u = __ldg(T + TAB_BIDX + bi * 256 + (slot >> 4));
-        uint32_t e = __ldg(dn + u);
-        while (dense_freq(e) && slot >= dense_cum(e) + dense_freq(e)) e = __ldg(dn + (++u));
-        s = dense_sym(e); f = dense_freq(e); cm = dense_cum(e);
-    }
-    if (!f) { d.bad = 1; return 0; }
+__device__ __forceinline__ uint32_t rans_step(Dec& d, uint32_t slot, uint32_t s, uint32_t f, uint32_t cm) {
+    if (!f) { d.bad = 1; return 0; }                        // a zero-frequency lookup (refrel3.h:78)
     d.x = f * (d.x >> PB) + slot - cm;
     renorm(d);
     return s;
+}
+// one symbol of a context with at most 6 symbols: the cum8 row of the staged table (T: its shared address)
+__device__ __forceinline__ uint32_t dsym_small(Dec& d, uint32_t T, int c) {
+    const uint32_t slot = d.x & (MTOT - 1);
+    const uint4 r = lds128(T + TAB_CUM8 + c * 16);
+    const uint32_t s = (uint32_t)((r.x >> 16) <= slot) + (uint32_t)((r.y & 0xFFFFu) <= slot) + (uint32_t)((r.y >> 16) <= slot) +
+                       (uint32_t)((r.z & 0xFFFFu) <= slot) + (uint32_t)((r.z >> 16) <= slot);
+    const uint32_t cm = cum_at(r, s);
+    return rans_step(d, slot, s, cum_at(r, s + 1) - cm, cm);
+}
+// one symbol of a 104-symbol context, bi its index among the 15 of them (pv_layout.h big_index)
+__device__ __forceinline__ uint32_t dsym_big(Dec& d, uint32_t T, int bi) {
+    const uint32_t slot = d.x & (MTOT - 1);
+    const uint32_t dn = T + TAB_DENSE;
+    uint32_t u = lds16(T + TAB_DOFF + 2 * bi) + lds8(T + TAB_BIDX + bi * (4096 / TAB_BUCKET) + slot / TAB_BUCKET);
+    uint32_t e = lds32(dn + 4 * u);
+    while (dense_freq(e) && slot >= dense_cum(e) + dense_freq(e)) e = lds32(dn + 4 * (++u));
+    return rans_step(d, slot, dense_sym(e), dense_freq(e), dense_cum(e));
 }
 // raw bits, at most 16 per step (refrel3.h:83-90)
 __device__ __forceinline__ uint64_t draw(Dec& d, uint32_t nb) {
@@ -121,55 +148,72 @@ __device__ __forceinline__ uint64_t unbucket(uint32_t s, uint64_t extra) {
     const uint32_t e = (s - 16) / 4 + 4, m = (s - 16) & 3;
     return (1ull << e) | ((uint64_t)m << (e - 2)) | extra;
 }
-__device__ __forceinline__ uint64_t dval(Dec& d, const uint8_t* T, int c) {
-    const uint32_t s = dsym(d, T, c);
+__device__ __forceinline__ uint64_t dval_big(Dec& d, uint32_t T, int bi) {   // bucketed value (refrel3.h:91)
+    const uint32_t s = dsym_big(d, T, bi);
     return unbucket(s, draw(d, s < 16 ? 0 : (s - 16) / 4 + 2));
 }
 __device__ __forceinline__ int kclass(int k) { return k < 0 ? 0 : k == K_CONT ? 1 : (k == K_DELTA || k == K_REP || k == K_FLIP) ? 2 : 3; }
 __device__ __forceinline__ int llc(uint64_t ll) { return ll == 0 ? 0 : ll == 1 ? 1 : ll <= 8 ? 2 : 3; }
 __device__ __forceinline__ int64_t unzz(uint64_t z) { return (int64_t)(z >> 1) ^ -(int64_t)(z & 1); }
 __device__ __forceinline__ uint8_t comp_up(uint8_t c) { return c == 'A' ? 'T' : c == 'C' ? 'G' : c == 'G' ? 'C' : c == 'T' ? 'A' : c; }
+// The reference as a block reads it: the span its start diagonal covers, staged in shared memory by the item's TMA
+// copy, and global memory (64 readable bytes on each side of the reference) for any position off that span.
+struct RefView {
+    const uint8_t* g; uint64_t n;           // global reference and its length
+    int64_t lo; uint32_t len; uint32_t sm;  // staged span: reference positions [lo, lo + len) at shared address sm
+    __device__ __forceinline__ uint32_t byte(int64_t q) const {
+        return (uint64_t)(q - lo) < (uint64_t)len ? lds8(sm + (uint32_t)(q - lo)) : (uint32_t)__ldg(g + q);
+    }
+};
 // the reference base the diagonal predicts at block offset o: 0..3, 4 = none (refrel3.h:104-109)
-__device__ __forceinline__ int refbase(const uint8_t* __restrict__ ref, uint64_t ref_n, uint64_t c, uint32_t dir, uint32_t o) {
+__device__ __forceinline__ int refbase(const RefView& R, uint64_t c, uint32_t dir, uint32_t o) {
     const int64_t q = dir ? (int64_t)c - (int64_t)o : (int64_t)c + (int64_t)o;
-    if (q < 0 || (uint64_t)q >= ref_n) return 4;
-    uint8_t b = __ldg(ref + q);
+    if (q < 0 || (uint64_t)q >= R.n) return 4;
+    uint8_t b = (uint8_t)R.byte(q);
     if (dir) b = comp_up(b);
     return b == 'A' ? 0 : b == 'C' ? 1 : b == 'G' ? 2 : b == 'T' ? 3 : 4;
 }
+__device__ __forceinline__ void dget(const Dec& d, int k, uint64_t& c, uint32_t& dir) {
+    c = k == 0 ? d.c0 : k == 1 ? d.c1 : k == 2 ? d.c2 : d.c3;
+    dir = k == 0 ? d.d0 : k == 1 ? d.d1 : k == 2 ? d.d2 : d.d3;
+}
+// move-to-front push of a diagonal (refrel3.h:98-102)
 __device__ __forceinline__ void dpush(Dec& d, uint64_t c, uint32_t dir) {
-    int j = 0;
-    while (j < d.nc && !(d.cc[j] == c && d.cd[j] == dir)) j++;
-    if (j == d.nc) { if (d.nc < 4) d.nc++; j = d.nc - 1; }
-    for (; j > 0; j--) { d.cc[j] = d.cc[j - 1]; d.cd[j] = d.cd[j - 1]; }
-    d.cc[0] = c; d.cd[0] = dir;
+    int j = (d.nc > 0 && d.c0 == c && d.d0 == dir) ? 0 : (d.nc > 1 && d.c1 == c && d.d1 == dir) ? 1
+          : (d.nc > 2 && d.c2 == c && d.d2 == dir) ? 2 : (d.nc > 3 && d.c3 == c && d.d3 == dir) ? 3 : -1;
+    if (j < 0) { if (d.nc < 4) d.nc++; j = d.nc - 1; }
+    if (j >= 3) { d.c3 = d.c2; d.d3 = d.d2; }
+    if (j >= 2) { d.c2 = d.c1; d.d2 = d.d1; }
+    if (j >= 1) { d.c1 = d.c0; d.d1 = d.d0; }
+    d.c0 = c; d.d0 = dir;
 }
 __device__ __forceinline__ void dec_init(Dec& d, const uint8_t* src, uint32_t n, int64_t st) {
     d.p = src; d.e = src + n; d.bad = 0; d.x = 0;
     d.o = 0; d.li = 0; d.prevk = -1; d.nc = 1;
-    d.cc[0] = (uint64_t)(st >> 1); d.cd[0] = (uint32_t)(st & 1);
+    d.c0 = (uint64_t)(st >> 1); d.d0 = (uint32_t)(st & 1);
+    d.c1 = d.c2 = d.c3 = 0; d.d1 = d.d2 = d.d3 = 0;
     if (n < 3) { d.bad = 1; return; }
-    d.x = (uint32_t)__ldg(src) | ((uint32_t)__ldg(src + 1) << 8) | ((uint32_t)__ldg(src + 2) << 16);
+    d.x = (uint32_t)src[0] | ((uint32_t)src[1] << 8) | ((uint32_t)src[2] << 16);
     d.p += 3;
 }
 
 // The event loop of refrel3.h:114-160. Sinks: more() is asked before each event (false pauses, resumable),
 // lit()/op() returning false abort the decode (the caller takes another path). Returns DEC_*.
 template <class Sink>
-__device__ int decode_events(Dec& d, const uint8_t* __restrict__ T, const uint8_t* __restrict__ ref, uint64_t ref_n, uint32_t blen,
-                             Sink& sk) {
+__device__ __forceinline__ int decode_events(Dec& d, uint32_t T, const RefView& R, uint32_t blen, Sink& sk) {
+    const uint64_t ref_n = R.n;
     if (d.bad) return DEC_ERR;
     while (d.o < blen) {
         if (!sk.more()) return DEC_PAUSE;
-        const uint64_t ll = dval(d, T, C_LL + kclass(d.prevk));
+        const uint64_t ll = dval_big(d, T, kclass(d.prevk));                 // LL x previous kind class
         if (d.bad || ll > blen - d.o) return DEC_ERR;
         if (ll) {
             uint32_t p1 = 16, p2 = 16;
             for (uint32_t j = 0; j < (uint32_t)ll; j++) {
                 int c;
-                if (ll <= 8) c = C_LITR + refbase(ref, ref_n, d.cc[0], d.cd[0], d.o + j) * 2 + (j == 0 ? 1 : 0);
+                if (ll <= 8) c = C_LITR + refbase(R, d.c0, d.d0, d.o + j) * 2 + (j == 0 ? 1 : 0);
                 else c = C_LIT2 + (p1 == 16 ? 16 : (int)((p2 == 16 ? p1 : p2 * 4 + p1) % 16));
-                const uint32_t s = dsym(d, T, c);
+                const uint32_t s = dsym_small(d, T, c);
                 const uint8_t byte = s == 0 ? 'A' : s == 1 ? 'C' : s == 2 ? 'G' : s == 3 ? 'T' : s == 4 ? 'N' : (uint8_t)draw(d, 8);
                 if (!sk.lit(d.o + j, byte)) return DEC_ABORT;
                 p2 = p1; p1 = s < 4 ? s : 0;
@@ -178,15 +222,15 @@ __device__ int decode_events(Dec& d, const uint8_t* __restrict__ T, const uint8_
             d.li += (uint32_t)ll; d.o += (uint32_t)ll;
         }
         if (d.o == blen) break;
-        const int kind = (int)dsym(d, T, C_KIND + llc(ll) * 4 + kclass(d.prevk));
+        const int kind = (int)dsym_small(d, T, C_KIND + llc(ll) * 4 + kclass(d.prevk));
         uint64_t p = 0; uint32_t dir = 0; int ki = 0; int64_t dd = 0; uint64_t dist = 0;
-        if (kind == K_CONT || kind == K_DELTA) { if (kind == K_DELTA) dd = unzz(dval(d, T, C_DELTA + (ll == 0 ? 0 : 1))); }
-        else if (kind == K_REP) { ki = 1 + (int)dsym(d, T, C_REPK); dd = unzz(dval(d, T, C_REPD)); if (ki >= d.nc) return DEC_ERR; }
-        else if (kind == K_ABS) { dir = dsym(d, T, C_DIR); p = draw(d, 32); }
-        else if (kind == K_SELF) dist = dval(d, T, C_SELF);
-        else if (kind == K_FLIP) { ki = (int)dsym(d, T, C_FLIPK); dd = unzz(dval(d, T, C_FLIPD)); if (ki >= d.nc) return DEC_ERR; }
+        if (kind == K_CONT || kind == K_DELTA) { if (kind == K_DELTA) dd = unzz(dval_big(d, T, 4 + (ll == 0 ? 0 : 1))); }
+        else if (kind == K_REP) { ki = 1 + (int)dsym_small(d, T, C_REPK); dd = unzz(dval_big(d, T, 6)); if (ki >= d.nc) return DEC_ERR; }
+        else if (kind == K_ABS) { dir = dsym_small(d, T, C_DIR); p = draw(d, 32); }
+        else if (kind == K_SELF) dist = dval_big(d, T, 7);
+        else if (kind == K_FLIP) { ki = (int)dsym_small(d, T, C_FLIPK); dd = unzz(dval_big(d, T, 14)); if (ki >= d.nc) return DEC_ERR; }
         else return DEC_ERR;
-        const uint64_t L = dval(d, T, C_LEN + kind) + MINL;
+        const uint64_t L = dval_big(d, T, 8 + kind) + MINL;                  // LEN x kind
         if (d.bad || L > blen - d.o) return DEC_ERR;
         uint32_t okind; uint64_t osrc;
         if (kind == K_SELF) {
@@ -194,14 +238,15 @@ __device__ int decode_events(Dec& d, const uint8_t* __restrict__ T, const uint8_
             okind = 2; osrc = d.o - dist;
         } else {
             if (kind == K_FLIP) {
-                const uint64_t gc = d.cc[ki]; const uint32_t gd = d.cd[ki];
+                uint64_t gc; uint32_t gd;
+                dget(d, ki, gc, gd);
                 dir = gd ^ 1;
                 const int64_t e = (gd ? (int64_t)gc - (int64_t)d.o : (int64_t)gc + (int64_t)d.o) + dd;
                 if (e < 0) return DEC_ERR;
                 p = (uint64_t)e;
             } else if (kind != K_ABS) {
-                const int k2 = kind == K_REP ? ki : 0;
-                const uint64_t gc = d.cc[k2]; const uint32_t gd = d.cd[k2];
+                uint64_t gc; uint32_t gd;
+                dget(d, kind == K_REP ? ki : 0, gc, gd);
                 dir = gd;
                 const int64_t e = (gd ? (int64_t)gc - (int64_t)d.o - (int64_t)L + 1 : (int64_t)gc + (int64_t)d.o) + dd;
                 if (e < 0) return DEC_ERR;
@@ -297,9 +342,24 @@ __device__ __forceinline__ void ldg16u(const uint8_t* p, uint32_t v[4]) {
     for (int i = 0; i < 4; i++) v[i] = __funnelshift_r(x[i], x[i + 1], b);
 }
 
+// 16 bytes at any shared address (4-byte aligned loads, funnel-shifted; 4 readable bytes past the end)
+__device__ __forceinline__ void lds16u(uint32_t a, uint32_t v[4]) {
+    const uint32_t b = a & ~3u, sh = (a & 3u) * 8;
+    uint32_t w[5];
+#pragma unroll
+    for (int i = 0; i < 5; i++) w[i] = lds32(b + 4 * i);
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] = __funnelshift_r(w[i], w[i + 1], sh);
+}
+// 16 reference bytes from position q: from the staged span when it holds all of them, else global memory
+__device__ __forceinline__ void ref16(const RefView& R, int64_t q, uint32_t v[4]) {
+    if (q >= R.lo && q - R.lo + 16 <= (int64_t)R.len) lds16u(R.sm + (uint32_t)(q - R.lo), v);
+    else ldg16u(R.g + q, v);
+}
+
 // ---------------------------------------------------------------- gathers: raw block bytes [blo, blo + 16)
 struct OpsGather {
-    const Item* it; const uint8_t* ref;
+    const Item* it; RefView R;
     __device__ void operator()(int64_t blo, uint32_t r[4]) const {
         r[0] = r[1] = r[2] = r[3] = 0;
         const int64_t klo = blo > (int64_t)it->ox0 ? blo : (int64_t)it->ox0;
@@ -319,9 +379,9 @@ struct OpsGather {
             const uint32_t kind = op_kind(o);
             uint32_t v[4];
             if (kind == 1) {
-                ldg16u(ref + (int64_t)o.src + (blo - dst), v);
+                ref16(R, (int64_t)o.src + (blo - dst), v);
             } else if (kind == 3) {
-                ldg16u(ref + ((int64_t)o.src + len - 1 - (blo - dst) - 15), v);
+                ref16(R, (int64_t)o.src + len - 1 - (blo - dst) - 15, v);
                 rev16(v);
 #pragma unroll
                 for (int i = 0; i < 4; i++) v[i] = comp4(v[i]);
@@ -348,6 +408,12 @@ struct BufGather {
             if (q >= (int64_t)it->ox0 && q < (int64_t)it->ox1) r[k >> 2] |= (uint32_t)buf[q] << (8 * (k & 3));
         }
     }
+};
+
+// a block served from the cohort's cache: its decoded bytes (the cache has 64 readable bytes around every row)
+struct CacheGather {
+    const uint8_t* blk;
+    __device__ void operator()(int64_t blo, uint32_t r[4]) const { ldg16u(blk + blo, r); }
 };
 
 // lower-case mask of window positions [wp, wp + 16) (bit k = position wp + k)
@@ -417,23 +483,63 @@ __device__ void emit(const Params& P, const Item* it, const Gather& g, int lane,
     }
 }
 
-// phase 1 of one item: locate, decode keeping the window's ops, find its lower-case runs
-__device__ void decode_item(const Params& P, uint64_t item, Item* it) {
+// ---------------------------------------------------------------- TMA bulk copies and the mbarrier they complete on
+__device__ __forceinline__ void mbar_init(uint32_t bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(bar) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(phase) : "memory");
+    return ok != 0;
+}
+// global -> shared, 16-byte aligned addresses and a multiple of 16 bytes, completing on `bar`
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
+}
+constexpr uint32_t WAIT_SPINS = 1u << 22;   // bounded wait on a bulk copy (milliseconds); then status 4
+
+// ---------------------------------------------------------------- items
+constexpr int WARPS = 4;                     // one item per warp
+// A warp's shared slot: its Item, then its assembly's decode table (tab_area bytes: the cohort's largest table), then
+// its block's stream (pay_cap bytes; a longer stream is read from global memory).
+__device__ __forceinline__ Item* slot_item(uint8_t* slot) { return (Item*)slot; }
+__device__ __forceinline__ uint8_t* slot_tab(const Params& P, uint8_t* slot) { (void)P; return slot + sizeof(Item); }
+__device__ __forceinline__ uint8_t* slot_pay(const Params& P, uint8_t* slot) { return slot + sizeof(Item) + P.tab_area; }
+__device__ __forceinline__ uint8_t* slot_span(const Params& P, uint8_t* slot) { return slot + sizeof(Item) + P.tab_area + P.pay_cap; }
+constexpr int SPAN_MARGIN = 64;              // reference bases staged on each side of the block's start diagonal
+__device__ __forceinline__ RefView slot_ref(const Params& P, uint8_t* slot) {
+    const Item* it = slot_item(slot);
+    return RefView{P.C.ref, P.C.ref_n, it->span_lo, it->span_len, smem_addr(slot_span(P, slot))};
+}
+
+// lane 0: the item's window and block; the ranges, its lower-case runs; false when there is nothing to decode
+__device__ bool item_locate(const Params& P, uint64_t item, Item* it) {
     it->state = ST_IDLE;
-    if (item >= P.total) return;
+    if (item >= P.total) return false;
     const uint64_t w = item / P.bpw, j = item % P.bpw;
     const int64_t a = P.wasm[w], s = P.wstart[w];
     const pv_dev_cohort& C = P.C;
-    if (a < 0 || a >= C.nasm) { if (j == 0) atomicOr(P.status, PV_STATUS_WINDOW); return; }
+    if (a < 0 || a >= C.nasm) { if (j == 0) report(P, w, PV_STATUS_WINDOW); return false; }
     const pv_asm_rec& R = C.asms[a];
-    if (s < 0 || (uint64_t)s + P.W > R.nbases) { if (j == 0) atomicOr(P.status, PV_STATUS_WINDOW); return; }
+    if (s < 0 || (uint64_t)s + P.W > R.nbases) { if (j == 0) report(P, w, PV_STATUS_WINDOW); return false; }
     const uint64_t Q = C.Q, b0 = (uint64_t)s / Q, b1 = ((uint64_t)s + P.W - 1) / Q, b = b0 + j;
-    if (b > b1) return;
+    if (b > b1) return false;
     const uint64_t bst = b * Q, blen = R.nbases - bst < Q ? R.nbases - bst : Q;
     const uint64_t x0 = (uint64_t)s > bst ? (uint64_t)s : bst, x1 = (uint64_t)s + P.W < bst + blen ? (uint64_t)s + P.W : bst + blen;
     it->w = (int64_t)w; it->s = (uint64_t)s; it->bst = bst; it->gblk = R.blk_base + b; it->a = (int32_t)a;
+    it->tab_off = R.tab_off; it->tab_bytes = (uint32_t)R.tab_bytes; it->span_lo = 0; it->span_len = 0;
     it->ox0 = (uint32_t)(x0 - bst); it->ox1 = (uint32_t)(x1 - bst); it->blen = (uint32_t)blen;
-    it->run_first = 0; it->run_cnt = 0;
+    it->run_first = 0; it->run_cnt = 0; it->nops = 0; it->nlits = 0;
     if (P.apply_case && !P.tokens && R.low_cnt) {                      // runs overlapping [x0, x1)
         const uint64_t* low = C.low + 2 * R.low_base;
         uint64_t lo = 0, hi = R.low_cnt;
@@ -448,27 +554,69 @@ __device__ void decode_item(const Params& P, uint64_t item, Item* it) {
                 it->runs[2 * (r - lo) + 1] = (int32_t)((re < x1 ? re : x1) - (uint64_t)s);
             }
     }
-    const uint64_t loc = C.blocks[2 * it->gblk];
-    const int64_t st = (int64_t)C.blocks[2 * it->gblk + 1];
+    return true;
+}
+
+// lane 0 of the item's warp: stage the assembly's decode table (and the block's stream when it fits) in the warp's
+// shared slot with TMA bulk copies, prefetch into L2 the reference span the block's diagonal covers up to the window's
+// end, then decode the block keeping the window's ops
+__device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
+    Item* it = slot_item(slot);
+    uint8_t* tab = slot_tab(P, slot);
+    uint8_t* pay = slot_pay(P, slot);
+    const pv_dev_cohort& C = P.C;
+    const uint64_t loc = __ldg(C.blocks + 2 * it->gblk);
+    const int64_t st = (int64_t)__ldg(C.blocks + 2 * it->gblk + 1);
     const uint32_t plen = loc_len(loc);
-    if (plen == (uint32_t)PV_BLEN_BAD) { it->state = ST_ERR; atomicOr(P.status, PV_STATUS_DECODE); return; }
+    if (plen == (uint32_t)PV_BLOCK_CACHED) { it->state = ST_CACHED; it->cptr = C.cache + loc_off(loc) * C.Q; return; }
+    if (plen == (uint32_t)PV_BLEN_BAD) { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); return; }
+    const uint8_t* src = C.payload + loc_off(loc);
+    const uintptr_t pa = (uintptr_t)src & ~(uintptr_t)15, pe = ((uintptr_t)src + plen + 15) & ~(uintptr_t)15;
+    const bool stage_pay = pe - pa <= (uintptr_t)P.pay_cap;
+    // the reference span the block's start diagonal covers over the whole block, with a margin: the literal contexts
+    // and (most) copy sources of the block read it from shared memory
+    uint64_t ra = 0, re = 0;
+    {
+        const int64_t c0 = st >> 1, bl = (int64_t)it->blen;
+        int64_t lo = (st & 1) ? c0 - bl + 1 - SPAN_MARGIN : c0 - SPAN_MARGIN, hi = (st & 1) ? c0 + 1 + SPAN_MARGIN : c0 + bl + SPAN_MARGIN;
+        lo = lo < 0 ? 0 : lo; hi = hi > (int64_t)C.ref_n ? (int64_t)C.ref_n : hi;
+        if (lo < hi) { ra = (uint64_t)lo & ~15ull; re = ((uint64_t)hi + 15) & ~15ull; }
+        if (re - ra + 16 > P.span_cap) re = ra;             // (cannot happen: span_cap holds Q + margins)
+    }
+    it->span_lo = (int64_t)ra; it->span_len = (uint32_t)(re - ra);
+    const uint32_t bytes = it->tab_bytes + (stage_pay ? (uint32_t)(pe - pa) : 0u) + it->span_len;
+    mbar_init(bar);
+    mbar_expect(bar, bytes);
+    bulk_g2s(smem_addr(tab), C.tabs + it->tab_off, it->tab_bytes, bar);
+    if (stage_pay) bulk_g2s(smem_addr(pay), (const void*)pa, (uint32_t)(pe - pa), bar);
+    if (it->span_len) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + ra, it->span_len, bar);
+    uint32_t spins = 0;
+    while (!mbar_try(bar, 0)) {
+        if (++spins == WAIT_SPINS) {                           // report, then wait (bounded) for the copies to land
+            report(P, it->w, PV_STATUS_WAIT);
+            it->state = ST_ERR;
+            for (uint32_t k = 0; k < WAIT_SPINS && !mbar_try(bar, 0); k++) {}
+            return;
+        }
+    }
     if (P.force_block) { it->state = ST_HEAVY; return; }
     Dec d;
-    dec_init(d, C.payload + loc_off(loc), plen, st);
+    dec_init(d, stage_pay ? pay + ((uintptr_t)src - pa) : src, plen, st);
     WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
-    const int r = decode_events(d, C.tabs + (uint64_t)a * PV_TAB_BYTES, C.ref, C.ref_n, (uint32_t)blen, sk);
+    const int r = decode_events(d, smem_addr(tab), slot_ref(P, slot), it->blen, sk);
     it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     if (r == DEC_DONE) it->state = ST_OK;
     else if (r == DEC_ABORT) it->state = ST_HEAVY;
-    else { it->state = ST_ERR; atomicOr(P.status, PV_STATUS_DECODE); }
+    else { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
 }
 
 // the CTA decodes a heavy item into its shared block buffer, ops in order, then emits it
-__device__ void heavy_item(const Params& P, const Item* it, uint8_t* buf, Op* hops) {
+__device__ void heavy_item(const Params& P, uint8_t* slot, uint8_t* buf, Op* hops) {
     __shared__ int h_res, h_nops;
     __shared__ Dec h_dec;
+    const Item* it = slot_item(slot);
     const pv_dev_cohort& C = P.C;
-    const uint8_t* T = C.tabs + (uint64_t)it->a * PV_TAB_BYTES;
+    const uint32_t T = smem_addr(slot_tab(P, slot));
     if (threadIdx.x == 0) {
         const uint64_t loc = C.blocks[2 * it->gblk];
         dec_init(h_dec, C.payload + loc_off(loc), loc_len(loc), (int64_t)C.blocks[2 * it->gblk + 1]);
@@ -478,7 +626,7 @@ __device__ void heavy_item(const Params& P, const Item* it, uint8_t* buf, Op* ho
         if (threadIdx.x == 0) {
             Dec d = h_dec;
             BlockSink sk{buf, hops, 0, it->ox1};
-            h_res = decode_events(d, T, C.ref, C.ref_n, it->blen, sk);
+            h_res = decode_events(d, T, slot_ref(P, slot), it->blen, sk);
             h_nops = (int)sk.nops;
             h_dec = d;
         }
@@ -505,7 +653,7 @@ __device__ void heavy_item(const Params& P, const Item* it, uint8_t* buf, Op* ho
         if (h_res != DEC_PAUSE) break;
     }
     if (h_res != DEC_DONE) {
-        if (threadIdx.x == 0) atomicOr(P.status, PV_STATUS_DECODE);
+        if (threadIdx.x == 0) report(P, it->w, PV_STATUS_DECODE);
         __syncthreads();
         return;
     }
@@ -515,17 +663,22 @@ __device__ void heavy_item(const Params& P, const Item* it, uint8_t* buf, Op* ho
 
 __global__ void __launch_bounds__(CTA) pv_windows_kernel(const Params P) {
     extern __shared__ uint4 smem_raw[];
-    Item* items = (Item*)smem_raw;
-    uint8_t* buf = (uint8_t*)(items + P.ipc);
-    Op* hops = (Op*)(buf + P.C.Q);
-    const uint64_t item0 = (uint64_t)blockIdx.x * P.ipc;
-    for (uint32_t t = threadIdx.x; t < P.ipc; t += CTA) decode_item(P, item0 + t, &items[t]);
-    __syncthreads();
+    __shared__ __align__(8) uint64_t bars[WARPS];
+    __shared__ Op hops[HOPS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (uint32_t t = warp; t < P.ipc; t += CTA / 32)
-        if (items[t].state == ST_OK) emit(P, &items[t], OpsGather{&items[t], P.C.ref}, lane, 32);
-    for (uint32_t t = 0; t < P.ipc; t++)
-        if (items[t].state == ST_HEAVY) heavy_item(P, &items[t], buf, hops);
+    uint8_t* slot = (uint8_t*)smem_raw + (size_t)warp * P.slot_bytes;
+    Item* it = slot_item(slot);
+    const uint64_t item = (uint64_t)blockIdx.x * WARPS + warp;
+    if (lane == 0 && item_locate(P, item, it)) item_decode(P, slot, smem_addr(&bars[warp]));
+    __syncwarp();
+    if (it->state == ST_OK) emit(P, it, OpsGather{it, slot_ref(P, slot)}, lane, 32);
+    else if (it->state == ST_CACHED) emit(P, it, CacheGather{it->cptr}, lane, 32);
+    __syncthreads();
+    uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
+    for (int t = 0; t < WARPS; t++) {
+        uint8_t* sl = (uint8_t*)smem_raw + (size_t)t * P.slot_bytes;
+        if (slot_item(sl)->state == ST_HEAVY) heavy_item(P, sl, buf, hops);
+    }
 }
 
 thread_local char g_cuda_err[256];
@@ -538,30 +691,46 @@ const char* pv_kernels_last_error(void) { return g_cuda_err; }
 
 int pv_windows_launches(int64_t n, int64_t W) { return (n > 0 && W > 0) ? 1 : 0; }
 
+static uint64_t grid_of(uint32_t Q, int64_t n, int64_t W, uint64_t* total, uint64_t* bpw) {
+    *bpw = ((uint64_t)W + Q - 1) / Q + 1;
+    *total = (uint64_t)n * *bpw;
+    return (*total + WARPS - 1) / WARPS;
+}
+
+size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W) {
+    if (n <= 0 || W <= 0) return 0;
+    uint64_t total, bpw;
+    return (size_t)grid_of(cohort->Q, n, W, &total, &bpw) * cohort->Q;
+}
+
 int pv_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,
-               int tokens, int apply_case, uint8_t* out, int32_t* status, void* stream) {
-    return pv_windows_ex(cohort, asm_index, start, n, W, rc, tokens, apply_case, 0u, out, status, stream);
+               int tokens, int apply_case, uint8_t* out, int32_t* status, void* work, size_t work_bytes, void* stream) {
+    return pv_windows_ex(cohort, asm_index, start, n, W, rc, tokens, apply_case, 0u, out, status, nullptr, work, work_bytes, stream);
 }
 
 int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,
-                  int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, void* stream) {
+                  int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, uint8_t* wstatus, void* work,
+                  size_t work_bytes, void* stream) {
     const uint32_t Q = cohort->Q;
     if (!(Q == 1024 || Q == 2048 || Q == 4096 || Q == 16384)) { snprintf(g_cuda_err, sizeof g_cuda_err, "block size"); return PV_EARG; }
     if (W < 0 || W >= (1ll << 31)) { snprintf(g_cuda_err, sizeof g_cuda_err, "W"); return PV_EARG; }
     if (n < 0) { snprintf(g_cuda_err, sizeof g_cuda_err, "n"); return PV_EARG; }
+    if (cohort->tab_max > PV_TAB_MAX_BYTES || cohort->tab_max % 16) { snprintf(g_cuda_err, sizeof g_cuda_err, "decode table size"); return PV_EARG; }
     if (n == 0 || W == 0) return PV_OK;
     Params P;
-    P.C = *cohort; P.wasm = asm_index; P.wstart = start; P.rc = rc; P.out = out; P.status = status;
-    P.n = (uint64_t)n; P.W = (uint64_t)W; P.bpw = ((uint64_t)W + Q - 1) / Q + 1;
-    if ((uint64_t)n > (1ull << 62) / P.bpw) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
-    P.total = P.n * P.bpw;
-    P.tokens = tokens; P.apply_case = apply_case; P.force_block = (flags & PV_WIN_BLOCK_PATH) ? 1 : 0;
-    uint32_t ipc = 8;
-    while (ipc < 128 && P.total / ipc > 2 * 148) ipc *= 2;
-    P.ipc = ipc;
-    const uint64_t grid = (P.total + ipc - 1) / ipc;
+    P.C = *cohort; P.wasm = asm_index; P.wstart = start; P.rc = rc; P.out = out; P.status = status; P.wstatus = wstatus;
+    P.n = (uint64_t)n; P.W = (uint64_t)W;
+    if ((uint64_t)n > (1ull << 62) / (((uint64_t)W + Q - 1) / Q + 1)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
+    const uint64_t grid = grid_of(Q, n, W, &P.total, &P.bpw);
     if (grid >= (1ull << 31)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
-    const size_t smem = (size_t)ipc * sizeof(Item) + Q + HOPS * sizeof(Op);
+    if (!work || work_bytes < grid * Q) { snprintf(g_cuda_err, sizeof g_cuda_err, "work buffer: %llu bytes needed", (unsigned long long)(grid * Q)); return PV_EARG; }
+    P.work = (uint8_t*)work;
+    P.tokens = tokens; P.apply_case = apply_case; P.force_block = (flags & PV_WIN_BLOCK_PATH) ? 1 : 0;
+    P.tab_area = (uint32_t)((cohort->tab_max + 15) & ~15ull);
+    P.pay_cap = ((Q / 32 + 32 < 160 ? 160 : Q / 32 + 32) + 15) & ~15u;
+    P.span_cap = (Q + 2 * SPAN_MARGIN + 64 + 15) & ~15u;
+    P.slot_bytes = (uint32_t)sizeof(Item) + P.tab_area + P.pay_cap + P.span_cap;
+    const size_t smem = (size_t)WARPS * P.slot_bytes;
     static size_t smem_set[64] = {0};                    // the attribute is per device
     int dev = 0;
     cudaGetDevice(&dev);

@@ -1,15 +1,18 @@
 // pv_layout.h - the refrel3 v1 model constants (refrel3.h:24-66) and this build's device layout of a cohort:
 // the per-assembly decode table that the window kernel reads, written on the host at open.
 //
-// Decode table (PV_TAB_BYTES per assembly). The reference keeps R3Tab {freq[61][104], cum[61][105], sym[61][4096]}
-// = 275,354 B per assembly (refrel3.h:66); this layout answers the same question - which symbol s, with which
-// frequency f and cumulative start, holds slot x & 4095 of context c - in 11,056 B, so that a cohort's tables stay
-// L2-resident and one assembly's table can be staged in shared memory:
+// Decode table (variable size per assembly, at most PV_TAB_MAX_BYTES). The reference keeps R3Tab {freq[61][104],
+// cum[61][105], sym[61][4096]} = 275,354 B per assembly (refrel3.h:66); this layout answers the same question - which
+// symbol s, with which frequency f and cumulative start, holds slot x & 4095 of context c - in typically 3-4 KB, so a
+// cohort's tables stay L2-resident and each decoding warp can stage its assembly's table in shared memory:
 //   cum8[61][8]     uint16  contexts with at most 6 symbols: cum[0..A], padded with cum[A]; the symbol is the number
 //                           of cum[1..5] at or below the slot (a zero-frequency symbol is skipped by construction)
-//   bidx[15][256]   uint8   contexts with 104 symbols: the dense index of the symbol holding slot 16 k
-//   dense[15][104]  uint32  those contexts' used symbols in order: cum | freq << 12 | sym << 25; a slot's symbol is
-//                           found from bidx[slot >> 4] by stepping while slot >= cum + freq (at most 15 steps)
+//   bidx[15][64]    uint8   contexts with 104 symbols: the index (in that context's dense list) of the symbol
+//                           holding slot 64 k
+//   doff[16]        uint16  the first dense entry of each 104-symbol context; doff[15] = entry count
+//   dense[...]      uint32  each 104-symbol context's used symbols in order: cum | freq << 12 | sym << 25 (an unused
+//                           context keeps one all-zero entry); a slot's symbol is found from bidx[slot >> 6] by
+//                           stepping while slot >= cum + freq (at most 63 steps, typically 0-2)
 // An all-zero context decodes as an error, as the reference's zero-frequency lookup does (refrel3.h:78).
 #pragma once
 #include <stdint.h>
@@ -31,11 +34,13 @@ constexpr int NBIG = 15;
 constexpr uint32_t PB = 12, MTOT = 1u << PB, RANS_L = 1u << 16, MINL = 12;
 
 constexpr int TAB_CUM8 = 0;                        // uint16 [61][8]
-constexpr int TAB_BIDX = TAB_CUM8 + NCTX * 16;     // uint8 [15][256]
-constexpr int TAB_DENSE = TAB_BIDX + NBIG * 256;   // uint32 [15][104]
-constexpr int TAB_END = TAB_DENSE + NBIG * AB * 4;
-static_assert(TAB_END <= PV_TAB_BYTES, "decode table layout");
-static_assert(TAB_DENSE % 16 == 0 && PV_TAB_BYTES % 16 == 0, "decode table alignment");
+constexpr int TAB_BUCKET = 64;                     // slots per bucket of the 104-symbol contexts' index
+constexpr int TAB_BIDX = TAB_CUM8 + NCTX * 16;     // uint8 [15][64]
+constexpr int TAB_DOFF = TAB_BIDX + NBIG * (4096 / TAB_BUCKET);   // uint16 [16]
+constexpr int TAB_DENSE = TAB_DOFF + 16 * 2;       // uint32 [entries]
+constexpr int TAB_MAX = TAB_DENSE + NBIG * AB * 4;
+static_assert(TAB_MAX <= PV_TAB_MAX_BYTES, "decode table layout");
+static_assert(TAB_DENSE % 4 == 0 && PV_TAB_MAX_BYTES % 16 == 0, "decode table alignment");
 
 // symbols per context (refrel3.h:29-41)
 PV_HD int alpha(int c) {

@@ -3,9 +3,11 @@ per-assembly device decode table. Used by tests to check the table the host buil
 NCTX, AB, NBIG = 61, 104, 15
 C_LL, C_LITR, C_LIT2, C_KIND, C_DELTA, C_REPK, C_REPD, C_DIR, C_SELF, C_LEN, C_FLIPK, C_FLIPD = 0, 4, 14, 31, 47, 49, 50, 51, 52, 53, 59, 60
 TAB_CUM8 = 0
+TAB_BUCKET = 64
 TAB_BIDX = TAB_CUM8 + NCTX * 16
-TAB_DENSE = TAB_BIDX + NBIG * 256
-TAB_BYTES = 11264
+TAB_DOFF = TAB_BIDX + NBIG * (4096 // TAB_BUCKET)
+TAB_DENSE = TAB_DOFF + 32
+TAB_MAX_BYTES = 8208
 
 
 def alpha(c):

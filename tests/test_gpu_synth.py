@@ -54,6 +54,39 @@ def test_cfg0_golden(cfg0):
             assert np.array_equal(got, gw["xxh3_" + tag]), (tag, flags)
 
 
+@pytest.mark.parametrize("Q", [1024, 16384])
+def test_block_cache_same_output(tmp_path_factory, oracle, cuda, Q):
+    """Blocks served from the open-time cache give the oracle's bytes, in every window that touches them."""
+    import panvram_b200 as P
+    d = str(tmp_path_factory.mktemp(f"cache{Q}"))
+    synth.make_cohort(d, "cfg1", Q=Q, nasm=3, scale=0.004)
+    ds = synth.dataset_of(Q)
+    c = P.Cohort.open(d, device=cuda, dataset=ds)
+    c0 = P.Cohort.open(d, device=cuda, dataset=ds, block_cache=False)
+    assert c.cached_blocks > 0 and c0.cached_blocks == 0 and c.resident_bytes()["cache"] > 0
+    ref = oracle.Reference(os.path.join(d, "reference.fa"))
+    arcs = [oracle.Archive(p, ref) for p in sorted(glob.glob(os.path.join(d, f"*.{ds}.rr3")))]
+    blocks = c._dev["blocks"].cpu().numpy().view(np.uint64)[0::2]
+    cached = np.nonzero((blocks >> np.uint64(40)) == np.uint64(0xFFFFFE))[0]
+    asms = c._core.pools()["asms"].view(np.uint64).reshape(-1, 8)
+    base = asms[:, 1].astype(np.int64)
+    rng = np.random.default_rng(Q)
+    for W in (1, 300, Q, 3 * Q + 5):
+        asm, start = [], []
+        for g in rng.choice(cached, min(200, len(cached))):
+            a = int(np.searchsorted(base, g, side="right") - 1)
+            s = int((g - base[a]) * Q) + int(rng.integers(-W + 1, Q))
+            s = max(0, min(s, arcs[a].nbases - W))
+            asm.append(a)
+            start.append(s)
+        rcm = rng.random(len(asm)) < 0.5
+        for tok in (False, True):
+            want = oracle.windows(arcs, ref, np.array(asm), np.array(start), W, rc=rcm, tokens=tok, threads=8)
+            for co in (c, c0):
+                x, st = co._launch(torch.tensor(asm), torch.tensor(start), W, torch.from_numpy(rcm), tok, True)
+                assert int(st.item()) == 0 and np.array_equal(x.cpu().numpy(), want), (Q, W, tok, co.cached_blocks)
+
+
 @pytest.mark.parametrize("Q", [1024, 2048, 4096, 16384])
 def test_synth_cohort_parity(tmp_path_factory, oracle, cuda, Q):
     import panvram_b200 as P
@@ -75,3 +108,21 @@ def test_synth_cohort_parity(tmp_path_factory, oracle, cuda, Q):
     for a in range(len(c)):
         ok, _ = c.check_full(a)
         assert ok
+
+
+def test_sampler_graph_equals_sample(cfg0, cuda):
+    """Cohort.sampler (sample() captured as one CUDA graph) gives, call after call, exactly what eager sample() gives
+    with an identically seeded generator - windows, coordinates and status."""
+    c, _, _ = cfg0
+    for rcp, tok, coords in ((False, False, False), (0.5, True, True), (True, False, True)):
+        g1 = torch.Generator(device=cuda).manual_seed(11)
+        g2 = torch.Generator(device=cuda).manual_seed(11)
+        s = c.sampler(256, 3000, g1, reverse_complement=rcp, tokens=tok, return_coords=coords)
+        for _ in range(4):
+            got = s()
+            want = c.sample(256, 3000, generator=g2, reverse_complement=rcp, tokens=tok, return_coords=coords)
+            if coords:
+                assert torch.equal(got[0], want[0]) and torch.equal(got[1], want[1])
+            else:
+                assert torch.equal(got, want)
+        assert s.status() == 0

@@ -13,7 +13,7 @@ from conftest import DATASETS, NAMES
 
 P = pytest.importorskip("panvram_b200")
 from panvram_b200 import _C  # noqa: E402
-from panvram_b200.layout import ALPHA, big_index, TAB_BIDX, TAB_CUM8, TAB_DENSE  # noqa: E402
+from panvram_b200.layout import ALPHA, big_index, TAB_BIDX, TAB_BUCKET, TAB_CUM8, TAB_DENSE, TAB_DOFF  # noqa: E402
 
 
 def paths(golden, ds):
@@ -99,10 +99,12 @@ def lookup_all_slots(tab, c):
         cm = cum8[s]
         f = cum8[s + 1] - cm
         return s, f, cm
-    bidx = tab[TAB_BIDX + 256 * bi: TAB_BIDX + 256 * bi + 256].astype(np.int64)
-    dense = np.frombuffer(tab[TAB_DENSE + 416 * bi: TAB_DENSE + 416 * bi + 416].tobytes(), dtype=np.uint32).astype(np.int64)
-    u = bidx[slot >> 4]
-    for _ in range(20):
+    nb = 4096 // TAB_BUCKET
+    bidx = tab[TAB_BIDX + nb * bi: TAB_BIDX + nb * bi + nb].astype(np.int64)
+    doff = np.frombuffer(tab[TAB_DOFF:TAB_DOFF + 32].tobytes(), dtype=np.uint16).astype(np.int64)
+    dense = np.frombuffer(tab[TAB_DENSE:].tobytes()[: 4 * int(doff[15])], dtype=np.uint32).astype(np.int64)
+    u = doff[bi] + bidx[slot // TAB_BUCKET]
+    for _ in range(TAB_BUCKET + 2):
         e = dense[u]
         fr, cu = (e >> 12) & 8191, e & 4095
         step = (fr > 0) & (slot >= cu + fr)
@@ -118,7 +120,9 @@ def test_decode_tables(golden, oracle_cohorts, ds):
     tabs = c.pools()["tabs"]
     _, arcs = oracle_cohorts[ds]
     for i, a in enumerate(arcs):
-        tab = tabs[i * _C.PV_TAB_BYTES:(i + 1) * _C.PV_TAB_BYTES]
+        rec = c.pools()["asms"].view(np.uint64).reshape(-1, 8)[i]
+        tab = tabs[int(rec[5]):int(rec[5]) + int(rec[6])]
+        assert int(rec[6]) % 16 == 0 and int(rec[5]) % 16 == 0 and int(rec[6]) <= c.pools()["tab_max"] <= _C.PV_TAB_MAX_BYTES
         freq = a.freq()
         for ctx in range(61):
             A = ALPHA[ctx]
@@ -177,7 +181,8 @@ def test_pools_padding(golden):
     assert len(p["ref_padded"]) == c.ref_bases + 128
     assert not p["ref_padded"][:64].any() and not p["ref_padded"][-64:].any()
     assert not p["payload"][-64:].any()
-    assert len(p["tabs"]) == 2 * _C.PV_TAB_BYTES
+    asms = p["asms"].view(np.uint64).reshape(-1, 8)
+    assert len(p["tabs"]) == int(asms[:, 6].sum()) and p["tab_max"] == int(asms[:, 6].max())
 
 
 def test_cohort_is_gpu_only(golden):
