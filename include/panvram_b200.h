@@ -140,6 +140,22 @@ int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const i
                   const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, uint8_t* wstatus,
                   void* work, size_t work_bytes, void* stream);
 
+/* pv_windows for callers that must not allocate device memory. This entry point has no counterpart in the reference.
+ * Some callers cannot call cudaMalloc or hand over a scratch buffer: a data-loading hook inside a training framework
+ * whose caching allocator already owns the device memory (a direct cudaMalloc there can fail or fragment its pool),
+ * or code that must not stall the device (cudaMalloc / cudaFree can synchronise it). This variant takes the same
+ * inputs and outputs as pv_windows but keeps its scratch (the general path's block buffers) in a fixed array of
+ * PV_NOALLOC_SCRATCH_BYTES that the library places in device memory; every GPU that loads the library holds that
+ * array until the process exits. A call that would need more scratch than that returns PV_EARG (message in
+ * pv_kernels_last_error()) without launching; split it into smaller calls. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress, with that device current), so make that first call before any CUDA
+ * stream capture. All calls share the one array: two calls that run on the GPU at the same time (different streams,
+ * or devices sharing nothing else) must not overlap, or they race on it. Nothing in it needs to start at zero: every
+ * byte of a block buffer is written before it is read. The call makes no cudaMalloc, cudaFree or other allocation. */
+#define PV_NOALLOC_SCRATCH_BYTES (16u << 20)
+int pv_windows_noalloc(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
+                       const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* stream);
+
 /* number of kernel launches one pv_windows call with these sizes makes (0 for an empty call) */
 int pv_windows_launches(int64_t n, int64_t W);
 /* message of the calling thread's last pv_windows / pv_windows_ex argument or launch failure */

@@ -75,6 +75,7 @@ for _name, _res, _args in (
         ("pv_windows", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _P, _P, _P, _SZ, _P]),
         ("pv_windows_ex", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _U32, _P, _P, _P, _P, _SZ, _P]),
         ("pv_windows_work_bytes", _SZ, [ctypes.POINTER(DevCohort), _I64, _I64]),
+        ("pv_windows_noalloc", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _P, _P, _P]),
         ("pv_windows_launches", _I32, [_I64, _I64])):
     _f = getattr(_lib, _name)
     _f.restype, _f.argtypes = _res, _args

@@ -746,3 +746,39 @@ int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const i
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- the no-allocation variant (pv_windows_noalloc)
+// Its scratch is this fixed array in device memory (PV_NOALLOC_SCRATCH_BYTES on every GPU that loads the library).
+// Host code only sees a stand-in symbol for it: the device address is looked up once per device with
+// cudaGetSymbolAddress and passed to the kernel like any other scratch pointer.
+namespace {
+static __device__ __align__(256) uint8_t g_noalloc_scratch[PV_NOALLOC_SCRATCH_BYTES];
+void* g_noalloc_addr[64] = {nullptr};
+}  // namespace
+
+extern "C" int pv_windows_noalloc(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
+                                  const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* stream) {
+    const size_t need = pv_windows_work_bytes(cohort, n, W);
+    if (need > (size_t)PV_NOALLOC_SCRATCH_BYTES) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_windows_noalloc: this call needs %zu bytes of scratch, more than the fixed %u; "
+                 "split it into smaller calls (or use pv_windows with a caller buffer)", need, (unsigned)PV_NOALLOC_SCRATCH_BYTES);
+        return PV_EARG;
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_windows_noalloc: current device: %s", e != cudaSuccess ? cudaGetErrorString(e) : "index >= 64");
+        return PV_ECUDA;
+    }
+    if (!g_noalloc_addr[dev]) {                              // set-up, once per device, with that device current
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            snprintf(g_cuda_err, sizeof g_cuda_err, "pv_windows_noalloc: scratch address: %s", cudaGetErrorString(e));
+            return PV_ECUDA;
+        }
+        g_noalloc_addr[dev] = p;
+    }
+    return pv_windows_ex(cohort, asm_index, start, n, W, rc, tokens, apply_case, 0u, out, status, nullptr, g_noalloc_addr[dev],
+                         (size_t)PV_NOALLOC_SCRATCH_BYTES, stream);
+}
