@@ -3,17 +3,19 @@
 // Replaces the reference's three-kernel path (pv_queue_kernel -> pv_case_kernel -> pv_rc_tok_kernel,
 // pv_cuda.cu:38-147) with one kernel that writes every output byte once:
 //   * work item = (window, one block the window touches); one item per warp, WARPS warps per CTA.
-//   * lane 0 stages the assembly's compact decode table (pv_layout.h) and the block's rANS stream into the warp's
-//     shared slot with TMA bulk copies completing on an mbarrier (bounded wait: status 4), and prefetches into L2 the
-//     reference span the block's start diagonal covers; then it decodes the stream in full (every validity check of
-//     refrel3.h:114-160, so a corrupt block reports status 1 exactly as the reference does), keeping only the ops and
-//     literal bytes that land inside the window. Each block's serial rANS chain runs in its own warp, so the chains'
-//     memory latencies overlap across warps instead of serialising inside one.
+//   * lane 0 stages into the warp's shared slot, with TMA bulk copies completing on one mbarrier (bounded wait:
+//     status 4), the assembly's compact decode table (pv_layout.h), the block's rANS stream and the reference span the
+//     block's start diagonal covers; then it decodes the stream in full (every validity check of refrel3.h:114-160, so
+//     a corrupt block reports status 1 exactly as the reference does) with the decoder state in registers, keeping
+//     only the ops and literal bytes that land inside the window. Each block's serial rANS chain runs in its own warp,
+//     so the chains' latencies overlap across warps.
 //   * the warp then writes the item's output range in 16-byte vector stores; each lane gathers its 16 bytes from the
-//     ops (reference copies realigned with funnel shifts, reverse-complement copies byte-reversed), then applies
-//     lower-case runs, reverse complement and the token map in registers.
-//   * heavy items (a self copy inside the window, or more ops / literals than a slot holds) are decoded again by the
-//     whole CTA into a Q-byte shared block buffer, ops executed in order, then emitted the same way.
+//     ops (reference copies realigned with funnel shifts, reverse-complement copies byte-reversed, from the staged span
+//     when it holds them), then applies lower-case runs, reverse complement and the token map in registers.
+//   * blocks in the cohort's block cache (decoded once at open) are copied from it like a reference span.
+//   * items needing the general path (a self copy inside the window, or more ops / literals than a slot holds) are
+//     decoded again by the whole CTA into a Q-byte block buffer in the caller's scratch, ops executed in order, then
+//     emitted the same way.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -502,9 +504,6 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t phase) {
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
-}
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
 }
 constexpr uint32_t WAIT_SPINS = 1u << 22;   // bounded wait on a bulk copy (milliseconds); then status 4
 
