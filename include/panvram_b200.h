@@ -140,6 +140,17 @@ int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const i
                   const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, uint8_t* wstatus,
                   void* work, size_t work_bytes, void* stream);
 
+/* The coordinate arithmetic of Cohort.sample between its draws and its pv_windows call (panvram/cohort.py:177-189 and 193-194,
+ * there six torch ops), as one launch. For window i: contig k = the first index with cum[k] > u[i] (searchsorted
+ * right; u[i] in [0, cum[nctg-1]), cum the inclusive prefix sum of valid[], valid[k] = max(0, contig length - W + 1)),
+ * pos = u[i] - (cum[k] - valid[k]); asm_index[i] = ctg_asm[k], start[i] = ctg_boff[k] + pos. rc_mode 0: no strand
+ * (rc untouched, may be NULL), 1: rc[i] = 1, 2: rc[i] = (r[i] < p) for the sample's rand() draw r. coords (NULL or int64
+ * [n, 4]): (assembly, ctg_local[k], pos, strand). status (NULL or an int32 device word) is set to 0 first, so the
+ * pv_windows call that follows on the stream can OR into it. All pointers device; asynchronous on `stream`. */
+int pv_sample_coords(const int64_t* cum, const int64_t* valid, const int64_t* ctg_asm, const int64_t* ctg_boff,
+                     const int64_t* ctg_local, int64_t nctg, const int64_t* u, const float* r, float p, int rc_mode, int64_t n,
+                     int64_t* asm_index, int64_t* start, uint8_t* rc, int64_t* coords, int32_t* status, void* stream);
+
 /* pv_windows for callers that must not allocate device memory. This entry point has no counterpart in the reference.
  * Some callers cannot call cudaMalloc or hand over a scratch buffer: a data-loading hook inside a training framework
  * whose caching allocator already owns the device memory (a direct cudaMalloc there can fail or fragment its pool),

@@ -76,6 +76,7 @@ for _name, _res, _args in (
         ("pv_windows_ex", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _U32, _P, _P, _P, _P, _SZ, _P]),
         ("pv_windows_work_bytes", _SZ, [ctypes.POINTER(DevCohort), _I64, _I64]),
         ("pv_windows_noalloc", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _P, _P, _P]),
+        ("pv_sample_coords", _I32, [_P, _P, _P, _P, _P, _I64, _P, _P, ctypes.c_float, _I32, _I64, _P, _P, _P, _P, _P, _P]),
         ("pv_windows_launches", _I32, [_I64, _I64])):
     _f = getattr(_lib, _name)
     _f.restype, _f.argtypes = _res, _args
@@ -266,6 +267,21 @@ def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, o
         msg = (_lib.pv_kernels_last_error() or b"").decode()
         raise RuntimeError(f"panvram_b200 window launch: {msg}")
     return out, status
+
+
+def sample_coords(cum, valid, ctg, u, r, p, rc_mode, asm, start, rc=None, coords=None, status=None):
+    """sample()'s coordinate arithmetic in one launch (pv_sample_coords): writes asm / start (int64 [n]), rc (uint8
+    [n], rc_mode 1 or 2), coords (int64 [n, 4]) when given, and zeroes status when given. cum / valid: the per-W
+    prefix sums and valid-start counts of the contigs; ctg: the cohort's contig arrays; u: int64 draws; r: the float
+    draws (rc_mode 2, strand = r < p). Asynchronous on torch's current stream of u's device."""
+    n = int(u.numel())
+    ptr = lambda t: t.data_ptr() if t is not None else None
+    code = _lib.pv_sample_coords(cum.data_ptr(), valid.data_ptr(), ctg["ctg_asm"].data_ptr(), ctg["ctg_boff"].data_ptr(),
+                                 ctg["ctg_local"].data_ptr(), int(cum.numel()), u.data_ptr(), ptr(r), float(p), int(rc_mode), n,
+                                 asm.data_ptr(), start.data_ptr(), ptr(rc), ptr(coords), ptr(status),
+                                 torch.cuda.current_stream(u.device).cuda_stream)
+    if code:
+        raise RuntimeError("panvram_b200 sample coordinates: " + (_lib.pv_kernels_last_error() or b"").decode())
 
 
 def launches_per_call(n, W):

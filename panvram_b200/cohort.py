@@ -5,8 +5,9 @@ decoded on the card by the one-kernel window decode (include/panvram_b200.h pv_w
 coordinates, errors and status text as the reference. Differences, by design:
   * GPU only: device="cpu" is refused (the reference's CPU decoder is this repository's test oracle, not a product
     path); fasta() decodes on the GPU and rebuilds / verifies the FASTA on the host.
-  * sample() keeps the reference's torch call sequence (same generator, same coordinates) but caches the per-W
-    valid-start total, so a call makes no host sync unless check=True.
+  * sample() keeps the reference's draws (the same torch.randint / torch.rand calls on the same generator, so the
+    same coordinates) but does the arithmetic from draws to coordinates in one kernel (pv_sample_coords) and caches
+    the per-W valid-start total, so a call makes no host sync unless check=True.
 """
 import glob
 import os
@@ -198,14 +199,19 @@ class Cohort:
             raise IndexError(f"contig index {c}")
         return c
 
-    def _launch(self, asm, start, W, reverse_complement, tokens, apply_case, out=None, status=None, flags=0):
+    def _launch(self, asm, start, W, reverse_complement, tokens, apply_case, out=None, status=None, flags=0, synced=False):
+        """synced: the caller waits for the stream before it returns (windows with check), so host inputs may be
+        copied without a wait of their own."""
         dev = self.device
         with torch.cuda.device(dev):
-            asm = torch.as_tensor(asm).to(dev, torch.int64).contiguous()
-            start = torch.as_tensor(start).to(dev, torch.int64).contiguous()
+            asm = torch.as_tensor(asm).to(dev, torch.int64, non_blocking=synced).contiguous()
+            start = torch.as_tensor(start).to(dev, torch.int64, non_blocking=synced).contiguous()
             rc = None
             if reverse_complement is not None:
-                rc = torch.as_tensor(reverse_complement).to(dev, torch.uint8).contiguous()
+                rc = torch.as_tensor(reverse_complement)
+                if rc.dtype == torch.bool:
+                    rc = rc.view(torch.uint8)                 # same bytes (0 / 1), no conversion kernel
+                rc = rc.to(dev, torch.uint8, non_blocking=synced).contiguous()
             if self.kernel_events is None:
                 return _C.windows_cuda(self._devc, asm, start, W, rc, tokens, apply_case, out=out, status=status, flags=flags)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -222,15 +228,18 @@ class Cohort:
         concatenated in file order) for every i -> uint8 [n, W] on the cohort's device. reverse_complement: None or a
         bool tensor [n]. tokens: A/a 0, C/c 1, G/g 2, T/t 3, anything else 4; else the FASTA's bytes, case kept.
         check: wait for the kernel and raise if any block failed to decode (one device sync)."""
-        out, status = self._launch(asm, start, int(W), reverse_complement, tokens, True)
+        out, status = self._launch(asm, start, int(W), reverse_complement, tokens, True, synced=bool(check))
         if check:
             s = int(status.item())
             if s:
                 raise RuntimeError(STATUS_TEXT.format(s))
         return out
 
-    def _draw(self, n, W, generator, reverse_complement, tokens, return_coords):
-        """The sample() sequence without the host check: (windows, coords or None, status tensor)."""
+    def _draw(self, n, W, generator, reverse_complement, tokens, return_coords, status=None):
+        """The sample() sequence without the host check: (windows, coords or None, status tensor). The draws are the
+        reference's (torch.randint over all valid starts, then torch.rand for the strand, on the generator's device);
+        the arithmetic from the draws to the decode's coordinates is one kernel (pv_sample_coords). status: None (a
+        fresh word, zeroed by that kernel) or an int32 device word the decode ORs into."""
         if W <= 0 or n < 0:
             raise ValueError("W must be positive, n non-negative")
         if W not in self._valid:
@@ -241,25 +250,29 @@ class Cohort:
         if total == 0:
             raise ValueError(f"no contig of {W} bases or more")
         gdev = generator.device if generator is not None else self.device
-        u = torch.randint(0, total, (n,), generator=generator, device=gdev, dtype=torch.int64).to(self.device)
-        k = torch.searchsorted(cum, u, right=True)
-        pos = u - (cum[k] - v[k])
-        asm = self._ctg["ctg_asm"][k]
-        start = self._ctg["ctg_boff"][k] + pos
+        dev = self.device
+        u = torch.randint(0, total, (n,), generator=generator, device=gdev, dtype=torch.int64).to(dev)
+        r, p, mode = None, 0.0, 0
         if reverse_complement is True:
-            rc = torch.ones(n, dtype=torch.bool, device=self.device)
+            mode = 1
         elif reverse_complement is False or reverse_complement is None or reverse_complement == 0:
-            rc = None
+            mode = 0
         else:
             p = float(reverse_complement)
             if not 0 < p <= 1:
                 raise ValueError("reverse_complement: False, True or a probability")
-            rc = (torch.rand(n, generator=generator, device=gdev) < p).to(self.device)
-        x, status = self._launch(asm, start, W, rc, tokens, True)
-        if not return_coords:
-            return x, None, status
-        strand = rc.to(torch.int64) if rc is not None else torch.zeros(n, dtype=torch.int64, device=self.device)
-        return x, torch.stack([asm, self._ctg["ctg_local"][k], pos, strand], 1), status
+            r, mode = torch.rand(n, generator=generator, device=gdev).to(dev), 2
+        with torch.cuda.device(dev):
+            asm = torch.empty(n, dtype=torch.int64, device=dev)
+            start = torch.empty(n, dtype=torch.int64, device=dev)
+            rc = torch.empty(n, dtype=torch.uint8, device=dev) if mode else None
+            coords = torch.empty((n, 4), dtype=torch.int64, device=dev) if return_coords else None
+            fresh = status is None
+            if fresh:
+                status = torch.empty(1, dtype=torch.int32, device=dev)
+            _C.sample_coords(cum, v, self._ctg, u, r, p, mode, asm, start, rc, coords, status if fresh else None)
+            x, status = self._launch(asm, start, W, rc, tokens, True, status=status)
+        return x, coords, status
 
     def sample(self, n, W, generator=None, reverse_complement=False, tokens=False, return_coords=False, check=True):
         """n windows of W bases, uniform over every (assembly, contig, start) with start + W <= contig length (a
@@ -368,8 +381,7 @@ class Sampler:
             events, cohort.kernel_events = cohort.kernel_events, None
             try:
                 with torch.cuda.graph(self.graph):
-                    self.x, self.coords, status = cohort._draw(*args)
-                    torch.bitwise_or(self._acc, status, out=self._acc)
+                    self.x, self.coords, _ = cohort._draw(*args, status=self._acc)
             finally:
                 cohort.kernel_events = events
 

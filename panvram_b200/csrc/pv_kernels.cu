@@ -680,6 +680,50 @@ __global__ void __launch_bounds__(CTA) pv_windows_kernel(const Params P) {
     }
 }
 
+// ---------------------------------------------------------------- sample() coordinates
+// The arithmetic between sample()'s draws and its window decode (panvram/cohort.py:177-189, 193-194): u uniform over all valid
+// starts -> contig k = searchsorted(cum, u, right=True), pos = u - (cum[k] - v[k]), assembly and base-stream start,
+// strand from the rand() draw. One warp per window: a 32-way search (each level one load per lane and a ballot), so
+// 3 dependent loads cover 32,768 contigs.
+struct CoordParams {
+    const int64_t *cum, *v, *casm, *cboff, *clocal, *u;
+    const float* r;
+    int64_t nctg, n;
+    float p;
+    int rc_mode;
+    int64_t *asm_out, *start_out, *coords;
+    uint8_t* rc_out;
+    int32_t* status;
+};
+constexpr int COORD_WARPS = 8;
+
+__global__ void __launch_bounds__(COORD_WARPS * 32) pv_sample_coords_kernel(const CoordParams P) {
+    const int lane = threadIdx.x & 31;
+    const int64_t w = (int64_t)blockIdx.x * COORD_WARPS + (threadIdx.x >> 5);
+    if (w == 0 && lane == 0 && P.status) *P.status = 0;
+    if (w >= P.n) return;
+    const int64_t u = P.u[w];
+    int64_t lo = 0, hi = P.nctg;                        // the answer (first k with cum[k] > u) lies in [lo, hi)
+    while (hi - lo > 1) {
+        const int64_t step = (hi - lo + 31) / 32;
+        const int64_t idx = lo + (int64_t)(lane + 1) * step - 1;   // lane 31's probe is at or past hi - 1
+        const bool above = idx >= hi - 1 || __ldg(P.cum + idx) > u;
+        const int f = __ffs(__ballot_sync(0xffffffffu, above)) - 1;
+        lo += (int64_t)f * step;
+        hi = min(hi, lo + step);
+    }
+    if (lane != 0) return;
+    const int64_t k = lo, pos = u - (__ldg(P.cum + k) - __ldg(P.v + k)), a = __ldg(P.casm + k);
+    const uint8_t s = P.rc_mode == 1 ? 1 : P.rc_mode == 2 ? (uint8_t)(P.r[w] < P.p) : 0;
+    P.asm_out[w] = a;
+    P.start_out[w] = __ldg(P.cboff + k) + pos;
+    if (P.rc_out) P.rc_out[w] = s;
+    if (P.coords) {
+        int64_t* c = P.coords + 4 * w;
+        c[0] = a; c[1] = __ldg(P.clocal + k); c[2] = pos; c[3] = s;
+    }
+}
+
 thread_local char g_cuda_err[256];
 
 }  // namespace
@@ -739,6 +783,27 @@ int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const i
         if (dev >= 0 && dev < 64) smem_set[dev] = smem;
     }
     pv_windows_kernel<<<(unsigned)grid, CTA, smem, (cudaStream_t)stream>>>(P);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
+    return PV_OK;
+}
+
+int pv_sample_coords(const int64_t* cum, const int64_t* valid, const int64_t* ctg_asm, const int64_t* ctg_boff,
+                     const int64_t* ctg_local, int64_t nctg, const int64_t* u, const float* r, float p, int rc_mode, int64_t n,
+                     int64_t* asm_index, int64_t* start, uint8_t* rc, int64_t* coords, int32_t* status, void* stream) {
+    if (n < 0 || n >= (1ll << 40) || nctg <= 0 || rc_mode < 0 || rc_mode > 2) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_sample_coords: n, contig count or rc_mode");
+        return PV_EARG;
+    }
+    if (n == 0 && !status) return PV_OK;
+    if (n > 0 && (!cum || !valid || !ctg_asm || !ctg_boff || !u || !asm_index || !start || (rc_mode == 2 && !r) || (rc_mode != 0 && !rc) ||
+                  (coords && !ctg_local))) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_sample_coords: a required pointer is NULL");
+        return PV_EARG;
+    }
+    CoordParams P{cum, valid, ctg_asm, ctg_boff, ctg_local, u, r, nctg, n, p, rc_mode, asm_index, start, coords, rc, status};
+    const int64_t grid = n > 0 ? (n + COORD_WARPS - 1) / COORD_WARPS : 1;
+    pv_sample_coords_kernel<<<(unsigned)grid, COORD_WARPS * 32, 0, (cudaStream_t)stream>>>(P);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
     return PV_OK;

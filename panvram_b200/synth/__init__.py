@@ -10,6 +10,7 @@ import ctypes
 import hashlib
 import json
 import os
+import sys
 import time
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -135,5 +136,6 @@ def make_cohort(out_dir, config="cfg0", Q=None, nasm=None, scale=1.0, threads=0,
         json.dump({"plan": P, "reference_sha256": sha.raw.hex(), "fasta": bool(write_fasta), "seconds_reference": round(t1 - t0, 2),
                    "seconds_archives": round(t2 - t1, 2), "threads": threads}, f)
     if verbose:
-        print(f"cohort {out_dir}: reference {t1 - t0:.1f} s, {len(paths)} archives {t2 - t1:.1f} s on {threads} threads")
+        print(f"cohort {out_dir}: reference {t1 - t0:.1f} s, {len(paths)} archives {t2 - t1:.1f} s on {threads} threads",
+              file=sys.stderr, flush=True)
     return out_dir

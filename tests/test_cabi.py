@@ -41,3 +41,22 @@ def test_last_error_without_gpu():
     lib.pv_windows_launches.argtypes = [ctypes.c_int64, ctypes.c_int64]
     assert lib.pv_last_error() is not None
     assert lib.pv_windows_launches(0, 10) == 0 and lib.pv_windows_launches(5, 0) == 0 and lib.pv_windows_launches(5, 10) == 1
+
+
+def test_sample_coords_refuses_bad_arguments_without_launching():
+    """pv_sample_coords checks its arguments before any CUDA call: a negative count, an empty contig table, an unknown
+    strand mode and missing pointers are refused (PV_EARG) with a message; an empty call with no status word is a no-op."""
+    from panvram_b200 import _C
+    lib = _C._lib
+    P = ctypes.c_void_p(16)
+    def call(n, nctg=3, mode=0, ptrs=True, r=None, rc=None):
+        p = P if ptrs else None
+        return lib.pv_sample_coords(p, p, p, p, p, nctg, p, r, 0.5, mode, n, p, p, rc, None, None, None)
+    assert call(-1) == _C.PV_EARG
+    assert call(4, nctg=0) == _C.PV_EARG
+    assert call(4, mode=3) == _C.PV_EARG
+    assert call(4, ptrs=False) == _C.PV_EARG
+    assert call(4, mode=2, rc=P) == _C.PV_EARG                  # strand from draws without the draws
+    assert call(4, mode=1) == _C.PV_EARG                        # strand output missing
+    assert b"NULL" in lib.pv_kernels_last_error()
+    assert call(0, ptrs=False) == _C.PV_OK

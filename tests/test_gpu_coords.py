@@ -1,0 +1,84 @@
+"""sample()'s coordinate step (pv_sample_coords) against the reference's own arithmetic, restated here with the torch
+ops of panvram/cohort.py:168-194 on the same draws. Integer work: compared exactly."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import DATASETS
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def cohorts(golden, cuda):
+    import panvram_b200 as P
+    return {ds: P.Cohort.open(golden["dirs"][ds], device=cuda, dataset=ds, reference=golden["ref"]) for ds in DATASETS}
+
+
+def _reference_coords(ctg, W, n, g, rcarg, device):
+    """panvram/cohort.py:168-194, the coordinate half of sample(), as the reference writes it."""
+    v = (ctg["ctg_len"] - W + 1).clamp_min(0)
+    cum = torch.cumsum(v, 0)
+    total = int(cum[-1].item())
+    u = torch.randint(0, total, (n,), generator=g, device=device, dtype=torch.int64)
+    k = torch.searchsorted(cum, u, right=True)
+    pos = u - (cum[k] - v[k])
+    if rcarg is True:
+        rc = torch.ones(n, dtype=torch.bool, device=device)
+    elif rcarg is False:
+        rc = None
+    else:
+        rc = torch.rand(n, generator=g, device=device) < float(rcarg)
+    strand = rc.to(torch.int64) if rc is not None else torch.zeros(n, dtype=torch.int64, device=device)
+    return torch.stack([ctg["ctg_asm"][k], ctg["ctg_local"][k], pos, strand], 1)
+
+
+@pytest.mark.parametrize("ds", DATASETS)
+def test_sample_coords_equal_reference_arithmetic(cohorts, ds, cuda):
+    """Same seed -> the same (assembly, contig, start, strand) as the reference's sample(), for every strand mode and
+    for window lengths that leave some contigs without a valid start; the generators end in the same state."""
+    c = cohorts[ds]
+    for W, rcarg, n in ((1, False, 50), (1000, True, 300), (5000, 0.5, 1000), (16385, 0.3, 257), (8192, 1.0, 4), (64, 0.5, 0)):
+        g1 = torch.Generator(device=cuda).manual_seed(W + n)
+        g2 = torch.Generator(device=cuda).manual_seed(W + n)
+        x, co = c.sample(n, W, generator=g1, reverse_complement=rcarg, return_coords=True)
+        want = _reference_coords(c._ctg, W, n, g2, rcarg, cuda)
+        assert co.dtype == torch.int64 and co.shape == (n, 4)
+        assert torch.equal(co, want), (W, rcarg)
+        assert torch.equal(g1.get_state(), g2.get_state())
+        assert x.shape == (n, W)
+
+
+def test_coords_kernel_many_contigs(cuda):
+    """The 32-way search at several levels: 40,000 contigs (about a fifth shorter than W, so runs of equal prefix
+    sums), draws including both ends of the range, against torch.searchsorted(right=True)."""
+    from panvram_b200 import _C
+    rng = np.random.default_rng(5)
+    for nctg, W in ((1, 100), (31, 100), (33, 100), (1025, 1000), (40000, 5000)):
+        lens = rng.integers(1, 3 * W, nctg)
+        lens[rng.random(nctg) < 0.2] = W - 1
+        lens[0] = max(lens[0], W)
+        ctg = {"ctg_len": torch.from_numpy(lens.astype(np.int64)).to(cuda),
+               "ctg_asm": torch.from_numpy(rng.integers(0, 100, nctg).astype(np.int64)).to(cuda),
+               "ctg_boff": torch.from_numpy(rng.integers(0, 1 << 40, nctg).astype(np.int64)).to(cuda),
+               "ctg_local": torch.arange(nctg, dtype=torch.int64, device=cuda) * 7}
+        v = (ctg["ctg_len"] - W + 1).clamp_min(0)
+        cum = torch.cumsum(v, 0)
+        total = int(cum[-1].item())
+        n = 5000
+        u = torch.from_numpy(np.concatenate([[0, total - 1], rng.integers(0, total, n - 2)]).astype(np.int64)).to(cuda)
+        r = torch.rand(n, device=cuda)
+        asm = torch.empty(n, dtype=torch.int64, device=cuda)
+        start = torch.empty(n, dtype=torch.int64, device=cuda)
+        rc = torch.empty(n, dtype=torch.uint8, device=cuda)
+        coords = torch.empty((n, 4), dtype=torch.int64, device=cuda)
+        status = torch.full((1,), 77, dtype=torch.int32, device=cuda)
+        _C.sample_coords(cum, v, ctg, u, r, 0.25, 2, asm, start, rc, coords, status)
+        k = torch.searchsorted(cum, u, right=True)
+        pos = u - (cum[k] - v[k])
+        strand = (r < 0.25).to(torch.int64)
+        assert int(status.item()) == 0
+        assert torch.equal(asm, ctg["ctg_asm"][k]) and torch.equal(start, ctg["ctg_boff"][k] + pos), nctg
+        assert torch.equal(rc.to(torch.int64), strand)
+        assert torch.equal(coords, torch.stack([ctg["ctg_asm"][k], ctg["ctg_local"][k], pos, strand], 1)), nctg
+        assert bool((v[k] > 0).all()) and bool((pos >= 0).all()) and bool((pos < v[k]).all())
