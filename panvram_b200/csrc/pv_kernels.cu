@@ -66,6 +66,7 @@ struct Params {
     uint64_t n, W, bpw, total;
     uint32_t slot_bytes, tab_area, pay_cap, span_cap;   // a warp's shared slot: Item | table | payload | reference span
     int tokens, apply_case, force_block;
+    uint32_t qshift;               // log2 of the block size
 };
 
 // status bits into the call's word and, when asked, into the window's byte (4-byte aligned, padded array)
@@ -73,16 +74,6 @@ __device__ __forceinline__ void report(const Params& P, uint64_t w, int bits) {
     atomicOr(P.status, bits);
     if (P.wstatus) atomicOr((unsigned int*)(P.wstatus + (w & ~3ull)), (unsigned int)bits << (8 * (w & 3)));
 }
-
-// ---------------------------------------------------------------- rANS decoder (refrel3.h:69-109)
-// The decoder state is all scalar - the four-entry diagonal cache as named registers, indexed by selects - so that,
-// inlined, the block's serial rANS chain stays in registers and never round-trips through local memory.
-struct Dec {
-    const uint8_t* p; const uint8_t* e;
-    uint32_t x; int bad;
-    uint32_t o, li; int prevk, nc;
-    uint64_t c0, c1, c2, c3; uint32_t d0, d1, d2, d3;   // diagonal cache, most recent first
-};
 
 // shared-memory loads by 32-bit shared address (the decode tables are staged there by a TMA bulk copy)
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
@@ -99,48 +90,94 @@ __device__ __forceinline__ uint32_t cum_at(uint4 r, uint32_t k) {
     const uint32_t w = (k >> 1) == 0 ? r.x : (k >> 1) == 1 ? r.y : (k >> 1) == 2 ? r.z : r.w;
     return (k & 1) ? (w >> 16) : (w & 0xFFFFu);
 }
-// byte renormalisation; false when the stream ran out (the reference then sets bad and returns at once,
-// refrel3.h:80,87). Stream bytes come from shared memory when the block's payload was staged, else global memory.
-__device__ __forceinline__ bool renorm(Dec& d) {
-    while (d.x < RANS_L) {
-        if (d.p >= d.e) { d.bad = 1; return false; }
-        d.x = (d.x << 8) | *d.p;
-        d.p++;
+// ---------------------------------------------------------------- rANS decoder (refrel3.h:69-109)
+// The block's rANS stream: staged in shared memory (32-bit shared addresses) or read from global memory. peek(k) is
+// the byte k ahead, or anything when that is past the end (the caller checks left() before using it): the shared
+// variant may read the next bytes of the warp's slot, the global one reads nothing past the end.
+struct SmemStream {
+    uint32_t p, e;
+    __device__ __forceinline__ uint32_t peek(uint32_t k) const { return lds8(p + k); }
+    __device__ __forceinline__ uint32_t left() const { return e - p; }
+    __device__ __forceinline__ void skip(uint32_t k) { p += k; }
+};
+struct GlobalStream {
+    const uint8_t* p; const uint8_t* e;
+    __device__ __forceinline__ uint32_t peek(uint32_t k) const { return p + k < e ? (uint32_t)__ldg(p + k) : 0u; }
+    __device__ __forceinline__ uint32_t left() const { return (uint32_t)(e - p); }
+    __device__ __forceinline__ void skip(uint32_t k) { p += k; }
+};
+// The decoder state is all scalar - the four-entry diagonal cache as named registers, indexed by selects - so that,
+// inlined, the block's serial rANS chain stays in registers and never round-trips through local memory.
+template <class S>
+struct Dec {
+    S st;
+    uint32_t x; int bad;
+    uint32_t o, li; int prevk, nc;
+    uint64_t c0, c1, c2, c3; uint32_t d0, d1, d2, d3;   // diagonal cache, most recent first
+};
+
+// byte renormalisation (refrel3.h:80,87); false when the stream ran out (the reference then sets bad and returns at
+// once). A step leaves x >= 16, so a well-formed stream needs at most two bytes: both are loaded before x is known
+// (their latency overlaps the symbol's table lookup) and taken branch-free; a state still below 2^16 after them
+// (only a corrupt stream, e.g. a zero initial state) continues byte by byte as the reference does.
+template <class S>
+__device__ __forceinline__ bool renorm(Dec<S>& d, uint32_t b0, uint32_t b1) {
+    uint32_t x = d.x;
+    const uint32_t left = d.st.left();
+    const uint32_t r1 = x < RANS_L;
+    x = r1 ? (x << 8) | b0 : x;
+    const uint32_t r2 = x < RANS_L;
+    x = r2 ? (x << 8) | b1 : x;
+    const uint32_t used = r1 + r2;
+    if (used > left) { d.st.skip(left); d.bad = 1; return false; }
+    d.st.skip(used);
+    while (x < RANS_L) {
+        if (d.st.left() == 0) { d.x = x; d.bad = 1; return false; }
+        x = (x << 8) | d.st.peek(0);
+        d.st.skip(1);
     }
+    d.x = x;
     return true;
 }
-__device__ __forceinline__ uint32_t rans_step(Dec& d, uint32_t slot, uint32_t s, uint32_t f, uint32_t cm) {
+template <class S>
+__device__ __forceinline__ uint32_t rans_step(Dec<S>& d, uint32_t slot, uint32_t s, uint32_t f, uint32_t cm, uint32_t b0, uint32_t b1) {
     if (!f) { d.bad = 1; return 0; }                        // a zero-frequency lookup (refrel3.h:78)
     d.x = f * (d.x >> PB) + slot - cm;
-    renorm(d);
+    renorm(d, b0, b1);
     return s;
 }
 // one symbol of a context with at most 6 symbols: the cum8 row of the staged table (T: its shared address)
-__device__ __forceinline__ uint32_t dsym_small(Dec& d, uint32_t T, int c) {
+template <class S>
+__device__ __forceinline__ uint32_t dsym_small(Dec<S>& d, uint32_t T, int c) {
+    const uint32_t b0 = d.st.peek(0), b1 = d.st.peek(1);
     const uint32_t slot = d.x & (MTOT - 1);
     const uint4 r = lds128(T + TAB_CUM8 + c * 16);
     const uint32_t s = (uint32_t)((r.x >> 16) <= slot) + (uint32_t)((r.y & 0xFFFFu) <= slot) + (uint32_t)((r.y >> 16) <= slot) +
                        (uint32_t)((r.z & 0xFFFFu) <= slot) + (uint32_t)((r.z >> 16) <= slot);
     const uint32_t cm = cum_at(r, s);
-    return rans_step(d, slot, s, cum_at(r, s + 1) - cm, cm);
+    return rans_step(d, slot, s, cum_at(r, s + 1) - cm, cm, b0, b1);
 }
 // one symbol of a 104-symbol context, bi its index among the 15 of them (pv_layout.h big_index)
-__device__ __forceinline__ uint32_t dsym_big(Dec& d, uint32_t T, int bi) {
+template <class S>
+__device__ __forceinline__ uint32_t dsym_big(Dec<S>& d, uint32_t T, int bi) {
+    const uint32_t b0 = d.st.peek(0), b1 = d.st.peek(1);
     const uint32_t slot = d.x & (MTOT - 1);
     const uint32_t dn = T + TAB_DENSE;
     uint32_t u = lds16(T + TAB_DOFF + 2 * bi) + lds8(T + TAB_BIDX + bi * (4096 / TAB_BUCKET) + slot / TAB_BUCKET);
     uint32_t e = lds32(dn + 4 * u);
     while (dense_freq(e) && slot >= dense_cum(e) + dense_freq(e)) e = lds32(dn + 4 * (++u));
-    return rans_step(d, slot, dense_sym(e), dense_freq(e), dense_cum(e));
+    return rans_step(d, slot, dense_sym(e), dense_freq(e), dense_cum(e), b0, b1);
 }
 // raw bits, at most 16 per step (refrel3.h:83-90)
-__device__ __forceinline__ uint64_t draw(Dec& d, uint32_t nb) {
+template <class S>
+__device__ __forceinline__ uint64_t draw(Dec<S>& d, uint32_t nb) {
     uint64_t v = 0; uint32_t sh = 0;
     while (nb) {
+        const uint32_t b0 = d.st.peek(0), b1 = d.st.peek(1);
         const uint32_t k = nb > 16 ? 16 : nb;
         const uint32_t b = d.x & ((1u << k) - 1);
         d.x >>= k;
-        if (!renorm(d)) return v;
+        if (!renorm(d, b0, b1)) return v;
         v |= (uint64_t)b << sh; sh += k; nb -= k;
     }
     return v;
@@ -150,7 +187,8 @@ __device__ __forceinline__ uint64_t unbucket(uint32_t s, uint64_t extra) {
     const uint32_t e = (s - 16) / 4 + 4, m = (s - 16) & 3;
     return (1ull << e) | ((uint64_t)m << (e - 2)) | extra;
 }
-__device__ __forceinline__ uint64_t dval_big(Dec& d, uint32_t T, int bi) {   // bucketed value (refrel3.h:91)
+template <class S>
+__device__ __forceinline__ uint64_t dval_big(Dec<S>& d, uint32_t T, int bi) {   // bucketed value (refrel3.h:91)
     const uint32_t s = dsym_big(d, T, bi);
     return unbucket(s, draw(d, s < 16 ? 0 : (s - 16) / 4 + 2));
 }
@@ -171,16 +209,19 @@ struct RefView {
 __device__ __forceinline__ int refbase(const RefView& R, uint64_t c, uint32_t dir, uint32_t o) {
     const int64_t q = dir ? (int64_t)c - (int64_t)o : (int64_t)c + (int64_t)o;
     if (q < 0 || (uint64_t)q >= R.n) return 4;
-    uint8_t b = (uint8_t)R.byte(q);
-    if (dir) b = comp_up(b);
-    return b == 'A' ? 0 : b == 'C' ? 1 : b == 'G' ? 2 : b == 'T' ? 3 : 4;
+    const uint32_t b = R.byte(q);
+    const uint32_t k = ((b >> 1) ^ (b >> 2)) & 3u;                 // A 0, C 1, G 2, T 3 for those letters
+    if (((0x54474341u >> (8 * k)) & 0xFFu) != b) return 4;         // not an upper-case A, C, G or T
+    return (int)(dir ? k ^ 3u : k);                                // the complement's code on the reverse strand
 }
-__device__ __forceinline__ void dget(const Dec& d, int k, uint64_t& c, uint32_t& dir) {
+template <class S>
+__device__ __forceinline__ void dget(const Dec<S>& d, int k, uint64_t& c, uint32_t& dir) {
     c = k == 0 ? d.c0 : k == 1 ? d.c1 : k == 2 ? d.c2 : d.c3;
     dir = k == 0 ? d.d0 : k == 1 ? d.d1 : k == 2 ? d.d2 : d.d3;
 }
 // move-to-front push of a diagonal (refrel3.h:98-102)
-__device__ __forceinline__ void dpush(Dec& d, uint64_t c, uint32_t dir) {
+template <class S>
+__device__ __forceinline__ void dpush(Dec<S>& d, uint64_t c, uint32_t dir) {
     int j = (d.nc > 0 && d.c0 == c && d.d0 == dir) ? 0 : (d.nc > 1 && d.c1 == c && d.d1 == dir) ? 1
           : (d.nc > 2 && d.c2 == c && d.d2 == dir) ? 2 : (d.nc > 3 && d.c3 == c && d.d3 == dir) ? 3 : -1;
     if (j < 0) { if (d.nc < 4) d.nc++; j = d.nc - 1; }
@@ -189,20 +230,21 @@ __device__ __forceinline__ void dpush(Dec& d, uint64_t c, uint32_t dir) {
     if (j >= 1) { d.c1 = d.c0; d.d1 = d.d0; }
     d.c0 = c; d.d0 = dir;
 }
-__device__ __forceinline__ void dec_init(Dec& d, const uint8_t* src, uint32_t n, int64_t st) {
-    d.p = src; d.e = src + n; d.bad = 0; d.x = 0;
+template <class S>
+__device__ __forceinline__ void dec_init(Dec<S>& d, const S& src, int64_t st) {
+    d.st = src; d.bad = 0; d.x = 0;
     d.o = 0; d.li = 0; d.prevk = -1; d.nc = 1;
     d.c0 = (uint64_t)(st >> 1); d.d0 = (uint32_t)(st & 1);
     d.c1 = d.c2 = d.c3 = 0; d.d1 = d.d2 = d.d3 = 0;
-    if (n < 3) { d.bad = 1; return; }
-    d.x = (uint32_t)src[0] | ((uint32_t)src[1] << 8) | ((uint32_t)src[2] << 16);
-    d.p += 3;
+    if (d.st.left() < 3) { d.bad = 1; return; }
+    d.x = d.st.peek(0) | (d.st.peek(1) << 8) | (d.st.peek(2) << 16);
+    d.st.skip(3);
 }
 
 // The event loop of refrel3.h:114-160. Sinks: more() is asked before each event (false pauses, resumable),
 // lit()/op() returning false abort the decode (the caller takes another path). Returns DEC_*.
-template <class Sink>
-__device__ __forceinline__ int decode_events(Dec& d, uint32_t T, const RefView& R, uint32_t blen, Sink& sk) {
+template <class S, class Sink>
+__device__ __forceinline__ int decode_events(Dec<S>& d, uint32_t T, const RefView& R, uint32_t blen, Sink& sk) {
     const uint64_t ref_n = R.n;
     if (d.bad) return DEC_ERR;
     while (d.o < blen) {
@@ -261,7 +303,7 @@ __device__ __forceinline__ int decode_events(Dec& d, uint32_t T, const RefView& 
         if (!sk.op(okind, osrc, d.o, (uint32_t)L)) return DEC_ABORT;
         d.o += (uint32_t)L; d.prevk = kind;
     }
-    if (d.bad || d.x != RANS_L || d.p != d.e) return DEC_ERR;
+    if (d.bad || d.x != RANS_L || d.st.left() != 0) return DEC_ERR;
     return DEC_DONE;
 }
 
@@ -298,17 +340,29 @@ struct BlockSink {
 };
 
 // ---------------------------------------------------------------- 16-byte register transforms
-__device__ __forceinline__ uint32_t comp4(uint32_t w) {        // ACGTacgt complemented, case kept (pv_v1.h:74-75)
-    const uint32_t l = w | 0x20202020u;
-    const uint32_t at = __vcmpeq4(l, 0x61616161u) | __vcmpeq4(l, 0x74747474u);
-    const uint32_t cg = __vcmpeq4(l, 0x63636363u) | __vcmpeq4(l, 0x67676767u);
-    return w ^ (at & 0x15151515u) ^ (cg & 0x04040404u);
+// Byte-parallel base classes on four bytes. code: A/a 0, C/c 1, G/g 2, T/t 3 for those letters (bits 1-2 of the
+// ASCII code, x ^ x>>1); the mask keeps the bytes that really are one of the eight letters: each byte, lower-cased,
+// is compared with the letter its code names ('a' 'c' 'g' 't' picked by a byte permute), with an exact zero-byte test.
+__device__ __forceinline__ uint32_t acgt4(uint32_t w, uint32_t& t) {
+    t = ((w >> 1) ^ (w >> 2)) & 0x03030303u;
+    const uint32_t e = __byte_perm(0x74676361u, 0u, t | (t >> 12));   // letters for bytes 0, 2, 1, 3 (selector order)
+    const uint32_t d = __byte_perm(w | 0x20202020u, 0u, 0x3120u) ^ e;  // the lower-cased bytes in that order
+    uint32_t z = ~(((d & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | d) & 0x80808080u;   // 0x80 where a byte matched
+    z = __byte_perm(z, 0u, 0x3120u);
+    return (z >> 7) * 0xFFu;
 }
-__device__ __forceinline__ uint32_t tok4(uint32_t w) {         // A/a 0, C/c 1, G/g 2, T/t 3, else 4 (pv_v1.h:76)
-    const uint32_t l = w | 0x20202020u;
-    const uint32_t ma = __vcmpeq4(l, 0x61616161u), mc = __vcmpeq4(l, 0x63636363u), mg = __vcmpeq4(l, 0x67676767u),
-                   mt = __vcmpeq4(l, 0x74747474u);
-    return (~(ma | mc | mg | mt) & 0x04040404u) | (mc & 0x01010101u) | (mg & 0x02020202u) | (mt & 0x03030303u);
+__device__ __forceinline__ uint32_t comp4(uint32_t w) {        // ACGTacgt complemented, case kept (pv_v1.h:74-75)
+    uint32_t t;
+    const uint32_t m = acgt4(w, t);
+    const uint32_t at = ~(t ^ (t >> 1)) & 0x01010101u;        // A and T (xor 0x15) vs C and G (xor 0x04)
+    return w ^ ((0x04040404u + at * 0x11u) & m);
+}
+// tokens A/a 0, C/c 1, G/g 2, T/t 3, else 4 (pv_v1.h:76); of the complemented bytes when rc (3 - code)
+__device__ __forceinline__ uint32_t tok4(uint32_t w, bool rc) {
+    uint32_t t;
+    const uint32_t m = acgt4(w, t);
+    if (rc) t ^= 0x03030303u;
+    return (t & m) | (0x04040404u & ~m);
 }
 __device__ __forceinline__ void rev16(uint32_t v[4]) {
     const uint32_t a = __byte_perm(v[3], 0, 0x0123), b = __byte_perm(v[2], 0, 0x0123), c = __byte_perm(v[1], 0, 0x0123),
@@ -360,8 +414,28 @@ __device__ __forceinline__ void ref16(const RefView& R, int64_t q, uint32_t v[4]
 }
 
 // ---------------------------------------------------------------- gathers: raw block bytes [blo, blo + 16)
+// 16 source bytes of op o for block offsets [blo, blo + 16), as if the op covered all of them (the caller keeps the
+// bytes the op does cover). Literal bytes come from the item's literal array in shared memory (lits_sm: its address;
+// the bytes around it are other fields of the slot, read but never used), reference bytes from the staged span or
+// global memory, reverse-complement copies byte-reversed and complemented.
+__device__ __forceinline__ void op_src16(const Item* it, const RefView& R, uint32_t lits_sm, const Op& o, int64_t blo, uint32_t v[4]) {
+    const int64_t dst = op_dst(o), len = o.len;
+    const uint32_t kind = op_kind(o);
+    if (kind == 1) {
+        ref16(R, (int64_t)o.src + (blo - dst), v);
+    } else if (kind == 3) {
+        ref16(R, (int64_t)o.src + len - 1 - (blo - dst) - 15, v);
+        rev16(v);
+#pragma unroll
+        for (int i = 0; i < 4; i++) v[i] = comp4(v[i]);
+    } else {
+        const int64_t first = dst > (int64_t)it->ox0 ? dst : (int64_t)it->ox0;
+        lds16u(lits_sm + (uint32_t)((int64_t)o.src + (blo - first)), v);
+    }
+}
+// any 16 bytes of an item's range: every op overlapping them, merged
 struct OpsGather {
-    const Item* it; RefView R;
+    const Item* it; RefView R; uint32_t lits_sm;
     __device__ void operator()(int64_t blo, uint32_t r[4]) const {
         r[0] = r[1] = r[2] = r[3] = 0;
         const int64_t klo = blo > (int64_t)it->ox0 ? blo : (int64_t)it->ox0;
@@ -378,24 +452,8 @@ struct OpsGather {
             if (dst >= khi) break;
             const int64_t a = dst > klo ? dst : klo, e = dst + len < khi ? dst + len : khi;
             if (a >= e) continue;
-            const uint32_t kind = op_kind(o);
             uint32_t v[4];
-            if (kind == 1) {
-                ref16(R, (int64_t)o.src + (blo - dst), v);
-            } else if (kind == 3) {
-                ref16(R, (int64_t)o.src + len - 1 - (blo - dst) - 15, v);
-                rev16(v);
-#pragma unroll
-                for (int i = 0; i < 4; i++) v[i] = comp4(v[i]);
-            } else {
-                const int64_t first = dst > (int64_t)it->ox0 ? dst : (int64_t)it->ox0;
-                v[0] = v[1] = v[2] = v[3] = 0;
-                for (int64_t q = a; q < e; q++) {
-                    const uint32_t byte = it->lits[o.src + (uint32_t)(q - first)];
-                    const int kb = (int)(q - blo);
-                    v[kb >> 2] |= byte << (8 * (kb & 3));
-                }
-            }
+            op_src16(it, R, lits_sm, o, blo, v);
             merge16(r, v, (int)(a - blo), (int)(e - blo));
         }
     }
@@ -441,47 +499,99 @@ __device__ __forceinline__ uint32_t case_mask(const Item* it, const uint64_t* __
     return m;
 }
 
+// An item's output: row = its window's output row, [A, B) = the bytes of the row it writes, delta = window start -
+// block start (block offset q is window position q - delta), rcw = the window is reverse-complemented.
+struct OutRange {
+    uint8_t* row; uintptr_t A, B; int64_t delta; int rcw; bool cased;
+};
+__device__ __forceinline__ OutRange out_range(const Params& P, const Item* it) {
+    OutRange g;
+    const int64_t W = (int64_t)P.W;
+    g.rcw = P.rc ? (P.rc[it->w] != 0) : 0;
+    g.row = P.out + (uint64_t)it->w * P.W;
+    g.delta = (int64_t)it->s - (int64_t)it->bst;
+    const int64_t wx0 = (int64_t)it->ox0 - g.delta, wx1 = (int64_t)it->ox1 - g.delta;
+    g.A = (uintptr_t)(g.row + (g.rcw ? W - wx1 : wx0));
+    g.B = (uintptr_t)(g.row + (g.rcw ? W - wx0 : wx1));
+    g.cased = P.apply_case && !P.tokens && it->run_cnt;
+    return g;
+}
+// the 16 forward bytes v of window positions [wpf, wpf + 16) -> the output chunk at ca (16-byte aligned): lower-case
+// runs, reverse complement, tokens, then one vector store (or, at the ends of the item's range, its bytes in [A, B))
+__device__ __forceinline__ void put16(const Params& P, const Item* it, const OutRange& g, uintptr_t ca, int64_t wpf, uint32_t v[4], bool whole) {
+    if (g.cased) {
+        const uint32_t m = case_mask(it, P.C.low, wpf);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t m4 = (m >> (4 * i)) & 15u;
+            const uint32_t bm = (m4 & 1u) * 0xFFu | (m4 & 2u) * 0x7F80u | (m4 & 4u) * 0x3FC000u | (m4 & 8u) * 0x1FE00000u;
+            v[i] |= bm & 0x20202020u;
+        }
+    }
+    if (P.tokens) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) v[i] = tok4(v[i], g.rcw);
+    } else if (g.rcw) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) v[i] = comp4(v[i]);
+    }
+    if (g.rcw) rev16(v);
+    if (whole || (ca >= g.A && ca + 16 <= g.B)) {
+        *(uint4*)ca = make_uint4(v[0], v[1], v[2], v[3]);
+    } else {
+        for (int k = 0; k < 16; k++) {
+            const uintptr_t q = ca + (uintptr_t)k;
+            if (q >= g.A && q < g.B) *(uint8_t*)q = (uint8_t)(v[k >> 2] >> (8 * (k & 3)));
+        }
+    }
+}
+
 // one item's output range in 16-byte chunks of the output row; lanes `lane` of `nl` share the chunks
 template <class Gather>
-__device__ void emit(const Params& P, const Item* it, const Gather& g, int lane, int nl) {
-    const uint64_t W = P.W;
-    const int rcw = P.rc ? (P.rc[it->w] != 0) : 0;
-    uint8_t* row = P.out + (uint64_t)it->w * W;
-    const int64_t wx0 = (int64_t)(it->bst + it->ox0 - it->s), wx1 = (int64_t)(it->bst + it->ox1 - it->s);
-    const int64_t o_lo = rcw ? (int64_t)W - wx1 : wx0, o_hi = rcw ? (int64_t)W - wx0 : wx1;
-    const uintptr_t A = (uintptr_t)(row + o_lo), B = (uintptr_t)(row + o_hi);
-    const bool cased = P.apply_case && !P.tokens && it->run_cnt;
-    for (uintptr_t ca = (A & ~(uintptr_t)15) + 16 * (uintptr_t)lane; ca < B; ca += 16 * (uintptr_t)nl) {
-        const int64_t opos = (int64_t)(ca - (uintptr_t)row);
-        const int64_t wpf = rcw ? (int64_t)W - 16 - opos : opos;      // window position of the first forward byte
+__device__ void emit(const Params& P, const Item* it, const Gather& gather, int lane, int nl) {
+    const OutRange g = out_range(P, it);
+    const int64_t W = (int64_t)P.W;
+    for (uintptr_t ca = (g.A & ~(uintptr_t)15) + 16 * (uintptr_t)lane; ca < g.B; ca += 16 * (uintptr_t)nl) {
+        const int64_t opos = (int64_t)(ca - (uintptr_t)g.row);
+        const int64_t wpf = g.rcw ? W - 16 - opos : opos;      // window position of the first forward byte
         uint32_t v[4];
-        g(wpf + (int64_t)it->s - (int64_t)it->bst, v);
-        if (cased) {
-            const uint32_t m = case_mask(it, P.C.low, wpf);
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint32_t m4 = (m >> (4 * i)) & 15u;
-                const uint32_t bm = (m4 & 1u) * 0xFFu | (m4 & 2u) * 0x7F80u | (m4 & 4u) * 0x3FC000u | (m4 & 8u) * 0x1FE00000u;
-                v[i] |= bm & 0x20202020u;
-            }
+        gather(wpf + g.delta, v);
+        put16(P, it, g, ca, wpf, v, false);
+    }
+}
+
+// A decoded item's output, op by op: for each op (warp-uniform, so no divergence between op kinds) the lanes write the
+// 16-byte output chunks that lie wholly inside the op's output bytes; then each chunk that holds a boundary (an op
+// start, or an end of the item's range, off a 16-byte boundary) is assembled from every op it overlaps by one lane.
+__device__ void emit_ops(const Params& P, const Item* it, const RefView& R, int lane) {
+    const OutRange g = out_range(P, it);
+    const int64_t W = (int64_t)P.W;
+    const int64_t base = (int64_t)(uintptr_t)g.row;    // chunks are 16-byte aligned in memory, not in the row
+    const uint32_t lits_sm = smem_addr(it->lits);
+    const int nops = it->nops;
+    const int64_t ox0 = it->ox0, ox1 = it->ox1;
+    for (int k = 0; k < nops; k++) {
+        const Op o = it->ops[k];
+        const int64_t dst = op_dst(o), a = dst > ox0 ? dst : ox0, e = dst + o.len < ox1 ? dst + o.len : ox1;
+        const int64_t lo = base + (g.rcw ? W - (e - g.delta) : a - g.delta), hi = base + (g.rcw ? W - (a - g.delta) : e - g.delta);
+        const int64_t c1 = hi & ~(int64_t)15;
+        for (int64_t c = ((lo + 15) & ~(int64_t)15) + 16 * lane; c < c1; c += 16 * 32) {
+            const int64_t wpf = g.rcw ? W - 16 - (c - base) : c - base;
+            uint32_t v[4];
+            op_src16(it, R, lits_sm, o, wpf + g.delta, v);
+            put16(P, it, g, (uintptr_t)c, wpf, v, true);
         }
-        if (rcw) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) v[i] = comp4(v[i]);
-            rev16(v);
-        }
-        if (P.tokens) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) v[i] = tok4(v[i]);
-        }
-        if (ca >= A && ca + 16 <= B) {
-            *(uint4*)ca = make_uint4(v[0], v[1], v[2], v[3]);
-        } else {
-            for (int k = 0; k < 16; k++) {
-                const uintptr_t q = ca + (uintptr_t)k;
-                if (q >= A && q < B) *(uint8_t*)q = (uint8_t)(v[k >> 2] >> (8 * (k & 3)));
-            }
-        }
+    }
+    const OpsGather gather{it, R, lits_sm};
+    for (int k = lane; k <= nops; k += 32) {
+        const int64_t b = k < nops ? (op_dst(it->ops[k]) > ox0 ? (int64_t)op_dst(it->ops[k]) : ox0) : ox1;
+        const int64_t p = base + (g.rcw ? W - (b - g.delta) : b - g.delta);     // the boundary's address in the row
+        if ((p & 15) == 0) continue;
+        const int64_t c = p & ~(int64_t)15;
+        const int64_t wpf = g.rcw ? W - 16 - (c - base) : c - base;
+        uint32_t v[4];
+        gather(wpf + g.delta, v);
+        put16(P, it, g, (uintptr_t)c, wpf, v, false);
     }
 }
 
@@ -525,13 +635,13 @@ __device__ __forceinline__ RefView slot_ref(const Params& P, uint8_t* slot) {
 __device__ bool item_locate(const Params& P, uint64_t item, Item* it) {
     it->state = ST_IDLE;
     if (item >= P.total) return false;
-    const uint64_t w = item / P.bpw, j = item % P.bpw;
+    const uint64_t w = item < 0xFFFFFFFFull ? (uint64_t)((uint32_t)item / (uint32_t)P.bpw) : item / P.bpw, j = item - w * P.bpw;
     const int64_t a = P.wasm[w], s = P.wstart[w];
     const pv_dev_cohort& C = P.C;
     if (a < 0 || a >= C.nasm) { if (j == 0) report(P, w, PV_STATUS_WINDOW); return false; }
     const pv_asm_rec& R = C.asms[a];
     if (s < 0 || (uint64_t)s + P.W > R.nbases) { if (j == 0) report(P, w, PV_STATUS_WINDOW); return false; }
-    const uint64_t Q = C.Q, b0 = (uint64_t)s / Q, b1 = ((uint64_t)s + P.W - 1) / Q, b = b0 + j;
+    const uint64_t Q = C.Q, b0 = (uint64_t)s >> P.qshift, b1 = ((uint64_t)s + P.W - 1) >> P.qshift, b = b0 + j;
     if (b > b1) return false;
     const uint64_t bst = b * Q, blen = R.nbases - bst < Q ? R.nbases - bst : Q;
     const uint64_t x0 = (uint64_t)s > bst ? (uint64_t)s : bst, x1 = (uint64_t)s + P.W < bst + blen ? (uint64_t)s + P.W : bst + blen;
@@ -599,9 +709,11 @@ __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
         }
     }
     if (P.force_block) { it->state = ST_HEAVY; return; }
-    Dec d;
-    dec_init(d, stage_pay ? pay + ((uintptr_t)src - pa) : src, plen, st);
+    if (!stage_pay) { it->state = ST_HEAVY; return; }   // a stream longer than the slot holds (uncached long block)
     WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
+    const uint32_t sp = smem_addr(pay) + (uint32_t)((uintptr_t)src - pa);
+    Dec<SmemStream> d;
+    dec_init(d, SmemStream{sp, sp + plen}, st);
     const int r = decode_events(d, smem_addr(tab), slot_ref(P, slot), it->blen, sk);
     it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     if (r == DEC_DONE) it->state = ST_OK;
@@ -612,18 +724,19 @@ __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
 // the CTA decodes a heavy item into its shared block buffer, ops in order, then emits it
 __device__ void heavy_item(const Params& P, uint8_t* slot, uint8_t* buf, Op* hops) {
     __shared__ int h_res, h_nops;
-    __shared__ Dec h_dec;
+    __shared__ Dec<GlobalStream> h_dec;
     const Item* it = slot_item(slot);
     const pv_dev_cohort& C = P.C;
     const uint32_t T = smem_addr(slot_tab(P, slot));
     if (threadIdx.x == 0) {
         const uint64_t loc = C.blocks[2 * it->gblk];
-        dec_init(h_dec, C.payload + loc_off(loc), loc_len(loc), (int64_t)C.blocks[2 * it->gblk + 1]);
+        const uint8_t* src = C.payload + loc_off(loc);
+        dec_init(h_dec, GlobalStream{src, src + loc_len(loc)}, (int64_t)C.blocks[2 * it->gblk + 1]);
     }
     for (;;) {
         __syncthreads();
         if (threadIdx.x == 0) {
-            Dec d = h_dec;
+            Dec<GlobalStream> d = h_dec;
             BlockSink sk{buf, hops, 0, it->ox1};
             h_res = decode_events(d, T, slot_ref(P, slot), it->blen, sk);
             h_nops = (int)sk.nops;
@@ -660,7 +773,7 @@ __device__ void heavy_item(const Params& P, uint8_t* slot, uint8_t* buf, Op* hop
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(CTA) pv_windows_kernel(const Params P) {
+__global__ void __launch_bounds__(CTA, 8) pv_windows_kernel(const Params P) {
     extern __shared__ uint4 smem_raw[];
     __shared__ __align__(8) uint64_t bars[WARPS];
     __shared__ Op hops[HOPS];
@@ -670,7 +783,7 @@ __global__ void __launch_bounds__(CTA) pv_windows_kernel(const Params P) {
     const uint64_t item = (uint64_t)blockIdx.x * WARPS + warp;
     if (lane == 0 && item_locate(P, item, it)) item_decode(P, slot, smem_addr(&bars[warp]));
     __syncwarp();
-    if (it->state == ST_OK) emit(P, it, OpsGather{it, slot_ref(P, slot)}, lane, 32);
+    if (it->state == ST_OK) emit_ops(P, it, slot_ref(P, slot), lane);
     else if (it->state == ST_CACHED) emit(P, it, CacheGather{it->cptr}, lane, 32);
     __syncthreads();
     uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
@@ -769,6 +882,8 @@ int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const i
     if (!work || work_bytes < grid * Q) { snprintf(g_cuda_err, sizeof g_cuda_err, "work buffer: %llu bytes needed", (unsigned long long)(grid * Q)); return PV_EARG; }
     P.work = (uint8_t*)work;
     P.tokens = tokens; P.apply_case = apply_case; P.force_block = (flags & PV_WIN_BLOCK_PATH) ? 1 : 0;
+    P.qshift = 0;
+    while ((1u << P.qshift) < Q) P.qshift++;
     P.tab_area = (uint32_t)((cohort->tab_max + 15) & ~15ull);
     P.pay_cap = ((Q / 32 + 32 < 160 ? 160 : Q / 32 + 32) + 15) & ~15u;
     P.span_cap = (Q + 2 * SPAN_MARGIN + 64 + 15) & ~15u;

@@ -1,0 +1,52 @@
+"""The N>1 bench path's host logic on CPU ranks (gloo, world size 2): rank 0 generates the cohort while rank 1 waits
+for it; the job's time is its slowest rank's; the job's rate counts every rank's windows (replicas, weak scaling)."""
+import datetime
+import os
+import socket
+import sys
+
+import torch.multiprocessing as mp
+
+from conftest import ROOT
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, data, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), PANVRAM_B200_DATA=data)
+    sys.path.insert(0, ROOT)
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        import bench
+        path, ds, _ = bench.ensure_cohort("cfg0", rank)
+        ready = os.path.exists(os.path.join(path, "READY"))
+        t = bench.max_over_ranks(0.5 + rank, world, "cpu")          # rank 1 is the slow one
+        rate = bench.whole_job_rate(1024 * 10, world, t)
+        dist.barrier()
+        q.put((rank, path, ds, ready, t, rate))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_cpu_ranks(tmp_path):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, str(tmp_path), q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = sorted(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    (r0, path0, ds0, ready0, t0, rate0), (r1, path1, ds1, ready1, t1, rate1) = got
+    assert (r0, r1) == (0, 1)
+    assert path0 == path1 == os.path.join(str(tmp_path), "cfg0") and ds0 == ds1 == "q4k"
+    assert ready0 and ready1
+    assert t0 == t1 == 1.5
+    assert rate0 == rate1 == 2 * 1024 * 10 / 1.5
