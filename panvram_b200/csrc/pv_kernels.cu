@@ -112,16 +112,30 @@ template <class S>
 struct Dec {
     S st;
     uint32_t x; int bad;
-    uint32_t o, li; int prevk, nc;
+    uint32_t o, li, pk; int nc;                          // pk: previous kind + 1 (0: none yet)
     uint64_t c0, c1, c2, c3; uint32_t d0, d1, d2, d3;   // diagonal cache, most recent first
 };
 
-// byte renormalisation (refrel3.h:80,87); false when the stream ran out (the reference then sets bad and returns at
-// once). A step leaves x >= 16, so a well-formed stream needs at most two bytes: both are loaded before x is known
-// (their latency overlaps the symbol's table lookup) and taken branch-free; a state still below 2^16 after them
-// (only a corrupt stream, e.g. a zero initial state) continues byte by byte as the reference does.
+// byte renormalisation (refrel3.h:80,87). A step leaves x >= 16, so a well-formed stream needs at most two bytes:
+// both are loaded before x is known (their latency overlaps the symbol's table lookup) and taken branch-free. Running
+// out of stream sets `bad` (sticky); the decoder then carries on with whatever state it has until the event's next
+// check, exactly where the reference's check catches it (refrel3.h:125,147), so the outcome - a failed block - is the
+// same. A state still below 2^16 after two bytes (only a corrupt stream, e.g. a zero initial state) continues byte by
+// byte as the reference does.
+struct SlowRenorm { uint32_t x, used; int bad; };
 template <class S>
-__device__ __forceinline__ bool renorm(Dec<S>& d, uint32_t b0, uint32_t b1) {
+__device__ __noinline__ SlowRenorm renorm_slow(uint32_t x, S st) {   // by value: the decoder state stays in registers
+    SlowRenorm r{x, 0, 0};
+    while (r.x < RANS_L) {
+        if (st.left() == 0) { r.bad = 1; break; }
+        r.x = (r.x << 8) | st.peek(0);
+        st.skip(1);
+        r.used++;
+    }
+    return r;
+}
+template <class S>
+__device__ __forceinline__ void renorm(Dec<S>& d, uint32_t b0, uint32_t b1) {
     uint32_t x = d.x;
     const uint32_t left = d.st.left();
     const uint32_t r1 = x < RANS_L;
@@ -129,19 +143,18 @@ __device__ __forceinline__ bool renorm(Dec<S>& d, uint32_t b0, uint32_t b1) {
     const uint32_t r2 = x < RANS_L;
     x = r2 ? (x << 8) | b1 : x;
     const uint32_t used = r1 + r2;
-    if (used > left) { d.st.skip(left); d.bad = 1; return false; }
-    d.st.skip(used);
-    while (x < RANS_L) {
-        if (d.st.left() == 0) { d.x = x; d.bad = 1; return false; }
-        x = (x << 8) | d.st.peek(0);
-        d.st.skip(1);
-    }
+    d.bad |= (int)(used > left);
+    d.st.skip(used > left ? left : used);
     d.x = x;
-    return true;
+    if (x < RANS_L) {
+        const SlowRenorm r = renorm_slow(x, d.st);
+        d.x = r.x; d.st.skip(r.used); d.bad |= r.bad;
+    }
 }
+// one rANS step: a zero-frequency lookup (refrel3.h:78) sets bad
 template <class S>
 __device__ __forceinline__ uint32_t rans_step(Dec<S>& d, uint32_t slot, uint32_t s, uint32_t f, uint32_t cm, uint32_t b0, uint32_t b1) {
-    if (!f) { d.bad = 1; return 0; }                        // a zero-frequency lookup (refrel3.h:78)
+    d.bad |= (int)(f == 0);
     d.x = f * (d.x >> PB) + slot - cm;
     renorm(d, b0, b1);
     return s;
@@ -168,33 +181,36 @@ __device__ __forceinline__ uint32_t dsym_big(Dec<S>& d, uint32_t T, int bi) {
     while (dense_freq(e) && slot >= dense_cum(e) + dense_freq(e)) e = lds32(dn + 4 * (++u));
     return rans_step(d, slot, dense_sym(e), dense_freq(e), dense_cum(e), b0, b1);
 }
-// raw bits, at most 16 per step (refrel3.h:83-90)
+// raw bits (at most 32), at most 16 per step (refrel3.h:83-90)
 template <class S>
-__device__ __forceinline__ uint64_t draw(Dec<S>& d, uint32_t nb) {
-    uint64_t v = 0; uint32_t sh = 0;
+__device__ __forceinline__ uint32_t draw(Dec<S>& d, uint32_t nb) {
+    uint32_t v = 0, sh = 0;
     while (nb) {
         const uint32_t b0 = d.st.peek(0), b1 = d.st.peek(1);
         const uint32_t k = nb > 16 ? 16 : nb;
         const uint32_t b = d.x & ((1u << k) - 1);
         d.x >>= k;
-        if (!renorm(d, b0, b1)) return v;
-        v |= (uint64_t)b << sh; sh += k; nb -= k;
+        renorm(d, b0, b1);
+        v |= b << sh; sh += k; nb -= k;
     }
     return v;
 }
-__device__ __forceinline__ uint64_t unbucket(uint32_t s, uint64_t extra) {
+// bucketed value (refrel3.h:91): 16 small buckets, then 4 per octave with (s - 16) / 4 + 2 raw bits; s < 104 keeps it
+// below 2^26
+__device__ __forceinline__ uint32_t unbucket(uint32_t s, uint32_t extra) {
     if (s < 16) return s;
     const uint32_t e = (s - 16) / 4 + 4, m = (s - 16) & 3;
-    return (1ull << e) | ((uint64_t)m << (e - 2)) | extra;
+    return (1u << e) | (m << (e - 2)) | extra;
 }
 template <class S>
-__device__ __forceinline__ uint64_t dval_big(Dec<S>& d, uint32_t T, int bi) {   // bucketed value (refrel3.h:91)
+__device__ __forceinline__ uint32_t dval_big(Dec<S>& d, uint32_t T, int bi) {
     const uint32_t s = dsym_big(d, T, bi);
     return unbucket(s, draw(d, s < 16 ? 0 : (s - 16) / 4 + 2));
 }
-__device__ __forceinline__ int kclass(int k) { return k < 0 ? 0 : k == K_CONT ? 1 : (k == K_DELTA || k == K_REP || k == K_FLIP) ? 2 : 3; }
-__device__ __forceinline__ int llc(uint64_t ll) { return ll == 0 ? 0 : ll == 1 ? 1 : ll <= 8 ? 2 : 3; }
-__device__ __forceinline__ int64_t unzz(uint64_t z) { return (int64_t)(z >> 1) ^ -(int64_t)(z & 1); }
+// class of the previous kind (none 0, CONT 1, DELTA / REP / FLIP 2, ABS / SELF 3) from pk = previous kind + 1
+__device__ __forceinline__ uint32_t kclass(uint32_t pk) { return (0x2332210u >> (4 * pk)) & 3u; }
+__device__ __forceinline__ uint32_t llc(uint32_t ll) { return (uint32_t)(ll > 0) + (uint32_t)(ll > 1) + (uint32_t)(ll > 8); }
+__device__ __forceinline__ int32_t unzz(uint32_t z) { return (int32_t)(z >> 1) ^ -(int32_t)(z & 1); }
 __device__ __forceinline__ uint8_t comp_up(uint8_t c) { return c == 'A' ? 'T' : c == 'C' ? 'G' : c == 'G' ? 'C' : c == 'T' ? 'A' : c; }
 // The reference as a block reads it: the span its start diagonal covers, staged in shared memory by the item's TMA
 // copy, and global memory (64 readable bytes on each side of the reference) for any position off that span.
@@ -233,7 +249,7 @@ __device__ __forceinline__ void dpush(Dec<S>& d, uint64_t c, uint32_t dir) {
 template <class S>
 __device__ __forceinline__ void dec_init(Dec<S>& d, const S& src, int64_t st) {
     d.st = src; d.bad = 0; d.x = 0;
-    d.o = 0; d.li = 0; d.prevk = -1; d.nc = 1;
+    d.o = 0; d.li = 0; d.pk = 0; d.nc = 1;
     d.c0 = (uint64_t)(st >> 1); d.d0 = (uint32_t)(st & 1);
     d.c1 = d.c2 = d.c3 = 0; d.d1 = d.d2 = d.d3 = 0;
     if (d.st.left() < 3) { d.bad = 1; return; }
@@ -249,32 +265,34 @@ __device__ __forceinline__ int decode_events(Dec<S>& d, uint32_t T, const RefVie
     if (d.bad) return DEC_ERR;
     while (d.o < blen) {
         if (!sk.more()) return DEC_PAUSE;
-        const uint64_t ll = dval_big(d, T, kclass(d.prevk));                 // LL x previous kind class
+        const uint32_t kc = kclass(d.pk);
+        const uint32_t ll = dval_big(d, T, (int)kc);                         // LL x previous kind class
         if (d.bad || ll > blen - d.o) return DEC_ERR;
         if (ll) {
             uint32_t p1 = 16, p2 = 16;
-            for (uint32_t j = 0; j < (uint32_t)ll; j++) {
+            for (uint32_t j = 0; j < ll; j++) {
                 int c;
                 if (ll <= 8) c = C_LITR + refbase(R, d.c0, d.d0, d.o + j) * 2 + (j == 0 ? 1 : 0);
                 else c = C_LIT2 + (p1 == 16 ? 16 : (int)((p2 == 16 ? p1 : p2 * 4 + p1) % 16));
-                const uint32_t s = dsym_small(d, T, c);
-                const uint8_t byte = s == 0 ? 'A' : s == 1 ? 'C' : s == 2 ? 'G' : s == 3 ? 'T' : s == 4 ? 'N' : (uint8_t)draw(d, 8);
-                if (!sk.lit(d.o + j, byte)) return DEC_ABORT;
-                p2 = p1; p1 = s < 4 ? s : 0;
+                const uint32_t sy = dsym_small(d, T, c);
+                uint32_t byte = sy < 4 ? (0x54474341u >> (8 * sy)) & 0xFFu : (uint32_t)'N';   // A C G T, N
+                if (sy >= 5) byte = draw(d, 8);                                              // escape: a raw byte
+                if (!sk.lit(d.o + j, (uint8_t)byte)) return DEC_ABORT;
+                p2 = p1; p1 = sy < 4 ? sy : 0;
             }
-            if (!sk.op(0, d.li, d.o, (uint32_t)ll)) return DEC_ABORT;
-            d.li += (uint32_t)ll; d.o += (uint32_t)ll;
+            if (!sk.op(0, d.li, d.o, ll)) return DEC_ABORT;
+            d.li += ll; d.o += ll;
         }
         if (d.o == blen) break;
-        const int kind = (int)dsym_small(d, T, C_KIND + llc(ll) * 4 + kclass(d.prevk));
-        uint64_t p = 0; uint32_t dir = 0; int ki = 0; int64_t dd = 0; uint64_t dist = 0;
+        const uint32_t kind = dsym_small(d, T, C_KIND + (int)(llc(ll) * 4 + kc));
+        uint64_t p = 0; uint32_t dir = 0, dist = 0; int ki = 0; int32_t dd = 0;
         if (kind == K_CONT || kind == K_DELTA) { if (kind == K_DELTA) dd = unzz(dval_big(d, T, 4 + (ll == 0 ? 0 : 1))); }
         else if (kind == K_REP) { ki = 1 + (int)dsym_small(d, T, C_REPK); dd = unzz(dval_big(d, T, 6)); if (ki >= d.nc) return DEC_ERR; }
         else if (kind == K_ABS) { dir = dsym_small(d, T, C_DIR); p = draw(d, 32); }
         else if (kind == K_SELF) dist = dval_big(d, T, 7);
         else if (kind == K_FLIP) { ki = (int)dsym_small(d, T, C_FLIPK); dd = unzz(dval_big(d, T, 14)); if (ki >= d.nc) return DEC_ERR; }
         else return DEC_ERR;
-        const uint64_t L = dval_big(d, T, 8 + kind) + MINL;                  // LEN x kind
+        const uint32_t L = dval_big(d, T, 8 + (int)kind) + MINL;            // LEN x kind
         if (d.bad || L > blen - d.o) return DEC_ERR;
         uint32_t okind; uint64_t osrc;
         if (kind == K_SELF) {
@@ -300,8 +318,8 @@ __device__ __forceinline__ int decode_events(Dec<S>& d, uint32_t T, const RefVie
             okind = dir ? 3 : 1; osrc = p;
             dpush(d, dir ? (uint64_t)((int64_t)p + (int64_t)L - 1 + (int64_t)d.o) : (uint64_t)((int64_t)p - (int64_t)d.o), dir);
         }
-        if (!sk.op(okind, osrc, d.o, (uint32_t)L)) return DEC_ABORT;
-        d.o += (uint32_t)L; d.prevk = kind;
+        if (!sk.op(okind, osrc, d.o, L)) return DEC_ABORT;
+        d.o += L; d.pk = kind + 1;
     }
     if (d.bad || d.x != RANS_L || d.st.left() != 0) return DEC_ERR;
     return DEC_DONE;
