@@ -12,6 +12,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "_build", "libpvoracle.so")
 REF_EXT = os.path.join(HERE, "_ref", "panvram_ref_C.so")
+REF_EXT_CUDA = os.path.join(HERE, "_ref", "panvram_ref_Ccu.so")
 REF_ENCODER = os.path.join(HERE, "_ref", "refrel3v1")
 
 _lib = None
@@ -171,13 +172,58 @@ def windows(arcs, ref, asm, start, W, rc=None, tokens=False, apply_case=True, ve
     return out
 
 
-def reference_extension():
-    """The reference's compiled CPU extension (panvram._C built from its own sources), or None when absent."""
-    if not os.path.exists(REF_EXT):
+def reference_extension(cuda=False):
+    """The reference's compiled extension (panvram._C built from its own sources), or None when absent. cuda: the build
+    with its GPU kernels (pv_cuda.cu, sm_100a), which adds windows_cuda / windows_cuda2."""
+    path, name = (REF_EXT_CUDA, "panvram_ref_Ccu") if cuda else (REF_EXT, "panvram_ref_C")
+    if not os.path.exists(path):
         return None
     import torch  # noqa: F401  (the extension links libtorch)
-    loader = importlib.machinery.ExtensionFileLoader("panvram_ref_C", REF_EXT)
-    spec = importlib.util.spec_from_loader("panvram_ref_C", loader)
+    loader = importlib.machinery.ExtensionFileLoader(name, path)
+    spec = importlib.util.spec_from_loader(name, loader)
     mod = importlib.util.module_from_spec(spec)
     loader.exec_module(mod)
     return mod
+
+
+class ReferenceGPU:
+    """The reference's own GPU path on a cohort directory: its Core, its pools copied to the device as its Cohort does
+    (panvram/cohort.py:25-38), its windows_cuda (pv_cuda.cu:153-161) and its sample() arithmetic
+    (panvram/cohort.py:165-194, restated with the same torch calls). Test infrastructure: the comparison side for the
+    reference's kernel, never part of panvram_b200."""
+
+    def __init__(self, ext, reference, paths, device, threads=0):
+        import torch
+        self.torch, self.ext, self.device = torch, ext, torch.device(device)
+        self.core = ext.Core(reference, list(paths), threads)
+        pools = self.core.pools()
+        self.dev = {k: v.to(self.device) for k, v in pools.items() if isinstance(v, torch.Tensor) and not k.startswith("ctg_")}
+        self.ctg = {k: pools[k].to(self.device) for k in ("ctg_asm", "ctg_local", "ctg_boff", "ctg_len")}
+        self.valid = {}
+
+    def windows(self, asm, start, W, rc=None, tokens=False):
+        d = self.dev
+        return self.ext.windows_cuda(d["P"], d["pay_base"], d["off"], d["st"], d["tab"], d["blk_base"], d["nbases"], d["low_s"],
+                                     d["low_l"], d["low_base"], d["low_cnt"], d["ref"], self.core.Q, asm, start, int(W), rc, tokens, True)
+
+    def sample(self, n, W, generator, reverse_complement=False, tokens=False):
+        torch = self.torch
+        if W not in self.valid:
+            v = (self.ctg["ctg_len"] - W + 1).clamp_min(0)
+            self.valid[W] = (torch.cumsum(v, 0), v)
+        cum, v = self.valid[W]
+        total = int(cum[-1].item())
+        gdev = generator.device
+        u = torch.randint(0, total, (n,), generator=generator, device=gdev, dtype=torch.int64).to(self.device)
+        k = torch.searchsorted(cum, u, right=True)
+        pos = u - (cum[k] - v[k])
+        asm = self.ctg["ctg_asm"][k]
+        start = self.ctg["ctg_boff"][k] + pos
+        rc = None
+        if reverse_complement is True:
+            rc = torch.ones(n, dtype=torch.bool, device=self.device)
+        elif reverse_complement:
+            rc = (torch.rand(n, generator=generator, device=gdev) < float(reverse_complement)).to(self.device)
+        out, status = self.windows(asm, start, W, rc, tokens)
+        strand = rc.to(torch.int64) if rc is not None else torch.zeros(n, dtype=torch.int64, device=self.device)
+        return out, status, torch.stack([asm, self.ctg["ctg_local"][k], pos, strand], 1)
