@@ -35,8 +35,36 @@ typedef struct pv_asm_rec {
     uint64_t low_cnt;     /* its lower-case run count */
     uint64_t tab_off;     /* its decode table: byte offset in pv_dev_cohort.tabs (16-byte aligned) */
     uint64_t tab_bytes;   /* and size (a multiple of 16) */
-    uint64_t pad;
+    uint64_t grp_base;    /* compact block table: its first group in pv_dev_cohort.groups */
 } pv_asm_rec;
+
+/* Opt-in compact resident forms (pv_core_open's packed_reference / compact_blocks; the reference's PackedRef and
+ * CompactTab, pv_compact.h:1-48): same archives, same output, less device memory. */
+
+/* packed reference: 2 bits per base (A 0, C 1, G 2, T 3; 16 bases per 32-bit word, base q at bits 2 (q mod 16) of word
+ * q / 16) plus the runs of any other byte (N, IUPAC codes), sorted and disjoint; a run is one byte repeated. The run
+ * array ends with a sentinel run starting at UINT64_MAX (not counted in pnruns). */
+typedef struct pv_ref_run {
+    uint64_t start;
+    uint32_t len;
+    uint32_t byte;
+} pv_ref_run;
+#define PV_REF_BUCKET_SHIFT 12     /* pv_dev_cohort.pidx[k]: the first run ending after position k << 12 */
+
+/* compact block table: per group of PV_BLK_GROUP consecutive blocks of one assembly a 32-byte record, per block 32
+ * bits: payload length (16 bits) | state code << 16. The state code of a block after the first of its group is its
+ * start diagonal's difference from the chain prediction (previous block's c + Q forward, - Q reverse) times 2 plus its
+ * strand, or PV_CODE_EXC: then the state is exception entry exc_base + (exceptions before it in the group). */
+#define PV_BLK_GROUP 32
+#define PV_CODE_EXC (-32768)
+typedef struct pv_blk_group {
+    uint64_t off;          /* payload offset of the group's first block in pv_dev_cohort.payload */
+    int64_t state;         /* its start state c << 1 | dir */
+    uint32_t exc_mask;     /* blocks of the group whose state is an exception entry */
+    uint32_t exc_base;     /* the first of them in pv_dev_cohort.bexc */
+    uint32_t cache_mask;   /* blocks of the group served from pv_dev_cohort.cache */
+    uint32_t cache_base;   /* cache slot of the first of them; the next ones follow in block order */
+} pv_blk_group;
 
 /* The pooled cohort as the window kernel reads it (device addresses). Built on the host by pv_core_pools() and
  * uploaded by the caller; it replaces the reference's pooled tensors P, pay_base, off, st, tab, blk_base, nbases,
@@ -54,6 +82,16 @@ typedef struct pv_dev_cohort {
     int64_t nasm;
     uint32_t Q;                  /* block size of the cohort: 1024, 2048, 4096 or 16384 */
     uint32_t pad;
+    /* packed reference (packed != 0; ref is then NULL) */
+    const uint32_t* pref;        /* ceil(ref_n / 16) words + 4 zero words */
+    const pv_ref_run* pruns;     /* [pnruns] */
+    const uint32_t* pidx;        /* [(ref_n >> PV_REF_BUCKET_SHIFT) + 2] */
+    uint64_t pnruns;
+    /* compact block table (compact != 0; blocks is then NULL) */
+    const pv_blk_group* groups;
+    const uint32_t* btab;        /* per pooled block: length | code << 16 */
+    const int64_t* bexc;         /* exception states, in block order */
+    uint32_t packed, compact;
 } pv_dev_cohort;
 
 /* Block table word 0 of a block served from pv_dev_cohort.cache: cache slot | PV_BLOCK_CACHED << 40 (the payload
@@ -70,6 +108,14 @@ typedef struct pv_host_pools {
     const uint8_t* tabs; uint64_t tabs_bytes; uint64_t tab_max;
     const uint64_t* low; uint64_t low_bytes;
     const int64_t* ctg_asm; const int64_t* ctg_local; const int64_t* ctg_boff; const int64_t* ctg_len; uint64_t ncontigs;
+    /* the compact forms, when opened with them (then ref_padded / blocks are NULL with 0 bytes) */
+    const uint32_t* pref; uint64_t pref_bytes;
+    const pv_ref_run* pruns; uint64_t pruns_bytes; uint64_t pnruns;
+    const uint32_t* pidx; uint64_t pidx_bytes;
+    const pv_blk_group* groups; uint64_t groups_bytes;
+    const uint32_t* btab; uint64_t btab_bytes;
+    const int64_t* bexc; uint64_t bexc_bytes;
+    uint32_t packed, compact;
 } pv_host_pools;
 
 typedef struct pv_asm_info {
@@ -87,7 +133,9 @@ const char* pv_last_error(void);
 /* Core(reference, paths, threads, packed_reference, compact_blocks) (pv_core.cpp:32-50, bound at :198-199): read the
  * reference FASTA (upper-cased, SHA-256), open every archive with all FORMAT section-5 checks (pv_v1.h:99-146),
  * one block size per cohort, pool the arrays into the device layout. threads 0 = all host threads.
- * packed_reference / compact_blocks: the reference's opt-in resident forms; refused (PV_EARG) in this build. */
+ * packed_reference: keep the reference as pv_ref_run runs + 2-bit words (pv_compact.h:19-28); compact_blocks: keep the
+ * block table as pv_blk_group records + 32 bits per block (pv_compact.h:30-46; a block payload over 65535 B is
+ * refused, pv_core.cpp:102). Windows are the same in every form. */
 int pv_core_open(const char* reference, const char* const* paths, int64_t npaths, int threads, int packed_reference,
                  int compact_blocks, pv_core** out);
 void pv_core_free(pv_core* c);

@@ -27,14 +27,17 @@ class FormatError(ValueError):
 
 class AsmRec(ctypes.Structure):
     _fields_ = [("nbases", ctypes.c_uint64), ("blk_base", ctypes.c_uint64), ("nb", ctypes.c_uint64), ("low_base", ctypes.c_uint64),
-                ("low_cnt", ctypes.c_uint64), ("tab_off", ctypes.c_uint64), ("tab_bytes", ctypes.c_uint64), ("pad", ctypes.c_uint64)]
+                ("low_cnt", ctypes.c_uint64), ("tab_off", ctypes.c_uint64), ("tab_bytes", ctypes.c_uint64), ("grp_base", ctypes.c_uint64)]
 
 
 class DevCohort(ctypes.Structure):
     _fields_ = [("ref", ctypes.c_void_p), ("ref_n", ctypes.c_uint64), ("payload", ctypes.c_void_p), ("blocks", ctypes.c_void_p),
                 ("asms", ctypes.c_void_p), ("tabs", ctypes.c_void_p), ("tab_max", ctypes.c_uint64), ("low", ctypes.c_void_p),
                 ("cache", ctypes.c_void_p), ("nasm", ctypes.c_int64),
-                ("Q", ctypes.c_uint32), ("pad", ctypes.c_uint32)]
+                ("Q", ctypes.c_uint32), ("pad", ctypes.c_uint32),
+                ("pref", ctypes.c_void_p), ("pruns", ctypes.c_void_p), ("pidx", ctypes.c_void_p), ("pnruns", ctypes.c_uint64),
+                ("groups", ctypes.c_void_p), ("btab", ctypes.c_void_p), ("bexc", ctypes.c_void_p),
+                ("packed", ctypes.c_uint32), ("compact", ctypes.c_uint32)]
 
 
 class HostPools(ctypes.Structure):
@@ -44,7 +47,17 @@ class HostPools(ctypes.Structure):
         ("tabs", ctypes.c_void_p), ("tabs_bytes", ctypes.c_uint64), ("tab_max", ctypes.c_uint64), ("low", ctypes.c_void_p),
         ("low_bytes", ctypes.c_uint64),
         ("ctg_asm", ctypes.c_void_p), ("ctg_local", ctypes.c_void_p), ("ctg_boff", ctypes.c_void_p), ("ctg_len", ctypes.c_void_p),
-        ("ncontigs", ctypes.c_uint64))]
+        ("ncontigs", ctypes.c_uint64),
+        ("pref", ctypes.c_void_p), ("pref_bytes", ctypes.c_uint64), ("pruns", ctypes.c_void_p), ("pruns_bytes", ctypes.c_uint64),
+        ("pnruns", ctypes.c_uint64), ("pidx", ctypes.c_void_p), ("pidx_bytes", ctypes.c_uint64),
+        ("groups", ctypes.c_void_p), ("groups_bytes", ctypes.c_uint64), ("btab", ctypes.c_void_p), ("btab_bytes", ctypes.c_uint64),
+        ("bexc", ctypes.c_void_p), ("bexc_bytes", ctypes.c_uint64), ("packed", ctypes.c_uint32), ("compact", ctypes.c_uint32))]
+
+# pv_blk_group (include/panvram_b200.h) as a numpy record
+BLK_GROUP = np.dtype([("off", "<u8"), ("state", "<i8"), ("exc_mask", "<u4"), ("exc_base", "<u4"), ("cache_mask", "<u4"),
+                      ("cache_base", "<u4")])
+PV_BLK_GROUP = 32
+PV_CODE_EXC = -32768
 
 
 class AsmInfo(ctypes.Structure):
@@ -113,7 +126,7 @@ class Core:
         _check(_lib.pv_core_open(os.fsencode(reference), arr, len(paths), int(threads), int(bool(packed_reference)),
                                  int(bool(compact_blocks)), ctypes.byref(h)))
         self._h, self._free = h, _lib.pv_core_free
-        self.packed_reference, self.compact_blocks = False, False
+        self.packed_reference, self.compact_blocks = bool(packed_reference), bool(compact_blocks)
 
     def __del__(self):
         if getattr(self, "_h", None):
@@ -144,6 +157,10 @@ class Core:
             "low": _host_array(p.low, p.low_bytes, np.uint64),
             "ctg_asm": _host_array(p.ctg_asm, n * 8, np.int64), "ctg_local": _host_array(p.ctg_local, n * 8, np.int64),
             "ctg_boff": _host_array(p.ctg_boff, n * 8, np.int64), "ctg_len": _host_array(p.ctg_len, n * 8, np.int64),
+            "pref": _host_array(p.pref, p.pref_bytes, np.uint32), "pruns": _host_array(p.pruns, p.pruns_bytes, np.uint8),
+            "pnruns": int(p.pnruns), "pidx": _host_array(p.pidx, p.pidx_bytes, np.uint32),
+            "groups": _host_array(p.groups, p.groups_bytes, np.uint8), "btab": _host_array(p.btab, p.btab_bytes, np.uint32),
+            "bexc": _host_array(p.bexc, p.bexc_bytes, np.int64),
         }
 
     def _asm_check(self, i):

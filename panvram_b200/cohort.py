@@ -43,13 +43,21 @@ class Cohort:
         self._index = {n: i for i, n in enumerate(self.names)}
         self._ctg_names = [{c[0]: k for k, c in enumerate(core.contigs(i))} for i in range(core.n)]
         pools = core.pools()
+        packed, compact = core.packed_reference, core.compact_blocks
         with torch.cuda.device(self.device):
-            self._dev = {k: torch.from_numpy(v).to(self.device) for k, v in pools.items() if not k.startswith("ctg_") and k != "tab_max"}
+            self._dev = {k: torch.from_numpy(v).to(self.device) for k, v in pools.items()
+                         if isinstance(v, np.ndarray) and v.size and not k.startswith("ctg_")}
             self._ctg = {k: torch.from_numpy(pools[k]).to(self.device) for k in ("ctg_asm", "ctg_local", "ctg_boff", "ctg_len")}
         d = self._dev
-        self._devc = _C.DevCohort(ref=d["ref_padded"].data_ptr() + 64, ref_n=core.ref_bases, payload=d["payload"].data_ptr(),
-                                  blocks=d["blocks"].data_ptr(), asms=d["asms"].data_ptr(), tabs=d["tabs"].data_ptr(),
-                                  tab_max=pools["tab_max"], low=d["low"].data_ptr(), cache=None, nasm=core.n, Q=core.Q, pad=0)
+        ptr = lambda k: d[k].data_ptr() if k in d else None
+        self._devc = _C.DevCohort(ref=None if packed else d["ref_padded"].data_ptr() + 64, ref_n=core.ref_bases,
+                                  payload=d["payload"].data_ptr(), blocks=None if compact else ptr("blocks"), asms=d["asms"].data_ptr(),
+                                  tabs=d["tabs"].data_ptr(), tab_max=pools["tab_max"], low=d["low"].data_ptr(), cache=None,
+                                  nasm=core.n, Q=core.Q, pad=0,
+                                  pref=ptr("pref") if packed else None, pruns=ptr("pruns") if packed else None,
+                                  pidx=ptr("pidx") if packed else None, pnruns=pools["pnruns"],
+                                  groups=ptr("groups") if compact else None, btab=ptr("btab") if compact else None,
+                                  bexc=ptr("bexc") if compact else None, packed=int(packed), compact=int(compact))
         self._valid = {}
         self._info = [core.info(i) for i in range(core.n)]
         # a list to collect (start, end) CUDA events around each window-kernel launch (measurement); None = off
@@ -67,8 +75,11 @@ class Cohort:
         decode stays uncached, so a window touching it still reports status 1. At most CACHE_BYTES (the longest
         streams first)."""
         Q = self._core.Q
-        loc = pools["blocks"][0::2]
-        plen = (loc >> np.uint64(40)).astype(np.int64)
+        compact = self._core.compact_blocks
+        if compact:
+            plen = (pools["btab"][: len(pools["btab"]) - _C.PV_BLK_GROUP] & np.uint32(0xFFFF)).astype(np.int64)
+        else:
+            plen = (pools["blocks"][0::2] >> np.uint64(40)).astype(np.int64)
         cand = np.nonzero((plen >= max(64, Q // 32)) & (plen < _C.PV_BLOCK_CACHED))[0]
         if len(cand) == 0:
             return
@@ -79,31 +90,50 @@ class Cohort:
         a = np.searchsorted(base, cand, side="right") - 1
         start = (cand - base[a]) * Q
         W = np.minimum(Q, nbases[a] - start)
-        order = np.concatenate([np.nonzero(W == Q)[0], np.nonzero(W < Q)[0]])
-        cand, a, start, W = cand[order], a[order], start[order], W[order]
-        n, nfull = len(cand), int((W == Q).sum())
+        n = len(cand)
+        full = np.nonzero(W == Q)[0]
         dev = self.device
         with torch.cuda.device(dev):
-            cache = torch.empty(64 + n * Q + 64, dtype=torch.uint8, device=dev)
+            # row i of the decode is block cand[i] (block order); the surviving blocks take cache slots in that order
+            rows = torch.empty((n, Q), dtype=torch.uint8, device=dev)
             ws = torch.zeros((n + 3) // 4 * 4, dtype=torch.uint8, device=dev)
             at = torch.from_numpy(a).to(dev)
             st = torch.from_numpy(start).to(dev)
-            if nfull:
-                _C.windows_cuda(self._devc, at[:nfull], st[:nfull], Q, None, False, False, out=cache[64:64 + nfull * Q].view(nfull, Q),
-                                wstatus=ws)
-            for i in range(nfull, n):
+            if len(full):
+                fi = torch.from_numpy(full).to(dev)
+                wf = torch.zeros((len(full) + 3) // 4 * 4, dtype=torch.uint8, device=dev)
+                out, _ = _C.windows_cuda(self._devc, at[fi], st[fi], Q, None, False, False, wstatus=wf)
+                rows[fi] = out
+                ws[fi] = wf[:len(full)]
+            for i in np.nonzero(W < Q)[0]:
                 w4 = torch.zeros(4, dtype=torch.uint8, device=dev)
                 _C.windows_cuda(self._devc, at[i:i + 1], st[i:i + 1], int(W[i]), None, False, False,
-                                out=cache[64 + i * Q:64 + i * Q + int(W[i])].view(1, -1), wstatus=w4)
+                                out=rows[i:i + 1, :int(W[i])], wstatus=w4)
                 ws[i:i + 1].copy_(w4[:1])
             ok = (ws[:n] == 0).cpu().numpy()
-            slots = np.nonzero(ok)[0]
-            if len(slots):
+            keep = np.nonzero(ok)[0]
+            cache = torch.zeros(64 + len(keep) * Q + 64, dtype=torch.uint8, device=dev)
+            if len(keep):
+                cache[64:64 + len(keep) * Q].view(len(keep), Q).copy_(rows[torch.from_numpy(keep).to(dev)])
+            del rows
+            blocks = cand[keep]
+            if len(blocks) and compact:
+                g = self._dev["groups"].cpu().numpy().view(_C.BLK_GROUP)
+                grp_base = asms[:, 7].astype(np.int64)
+                ab = a[keep]
+                k = blocks - base[ab]
+                gi = grp_base[ab] + k // _C.PV_BLK_GROUP
+                np.bitwise_or.at(g["cache_mask"], gi, (np.uint32(1) << (k % _C.PV_BLK_GROUP).astype(np.uint32)))
+                counts = np.zeros(len(g), np.int64)
+                np.add.at(counts, gi, 1)
+                g["cache_base"] = (np.cumsum(counts) - counts).astype(np.uint32)
+                self._dev["groups"].copy_(torch.from_numpy(g.view(np.uint8)).to(dev))
+            elif len(blocks):
                 blk = self._dev["blocks"].view(torch.int64)
-                vals = torch.from_numpy((slots.astype(np.uint64) | np.uint64(_C.PV_BLOCK_CACHED << 40)).view(np.int64)).to(dev)
-                blk[torch.from_numpy(2 * cand[slots]).to(dev)] = vals
+                vals = torch.from_numpy((np.arange(len(blocks), dtype=np.uint64) | np.uint64(_C.PV_BLOCK_CACHED << 40)).view(np.int64)).to(dev)
+                blk[torch.from_numpy(2 * blocks).to(dev)] = vals
             torch.cuda.synchronize(dev)
-        self._cache, self.cached_blocks = cache, int(len(slots))
+        self._cache, self.cached_blocks = cache, int(len(keep))
         self._devc.cache = cache.data_ptr() + 64
 
     @classmethod
@@ -114,7 +144,9 @@ class Cohort:
         `path/reference.fa`, else the file named in the archives' header in `path`. Every archive is checked before
         any decode (header XXH3, reference SHA-256 and size, sections, tables). One block size per cohort.
         device: "cuda" or "cuda:N". block_cache: decode the long (literal-heavy) blocks once at open and serve them
-        from HBM (same output; see _build_block_cache)."""
+        from HBM (same output; see _build_block_cache). Opt-in compact resident forms (same archives, same output):
+        packed_reference - the reference in 2 bits per base plus its runs of other bytes instead of a byte per base;
+        compact_blocks - the block table as 32-byte records per 32 blocks plus 4 bytes per block instead of 16."""
         if dataset is not None and not re.fullmatch(r"q\d+k", dataset):
             raise ValueError(f"dataset: {DATASETS} (or another q<N>k suffix), or None for every *.rr3")
         pat = f"*.{dataset}.rr3" if dataset else "*.rr3"
@@ -173,8 +205,10 @@ class Cohort:
         reference's off + st), low the lower-case runs (low_s + low_l), asm the per-assembly records, cache the decoded
         long blocks."""
         d = self._dev
-        r = {"P": d["payload"].numel(), "blocks": d["blocks"].numel() * 8, "tab": d["tabs"].numel(), "low": d["low"].numel() * 8,
-             "ref": d["ref_padded"].numel(), "asm": d["asms"].numel(), "cache": self._cache.numel() if self._cache is not None else 0}
+        nb = lambda *ks: sum(d[k].numel() * d[k].element_size() for k in ks if k in d)
+        r = {"P": nb("payload"), "blocks": nb("blocks", "groups", "btab", "bexc"), "tab": nb("tabs"), "low": nb("low"),
+             "ref": nb("ref_padded", "pref", "pruns", "pidx"), "asm": nb("asms"),
+             "cache": self._cache.numel() if self._cache is not None else 0}
         r["total"] = sum(r.values())
         return r
 

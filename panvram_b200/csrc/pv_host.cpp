@@ -291,6 +291,13 @@ struct pv_core {
     std::vector<uint8_t> tabs;
     uint64_t tab_max = 0;
     std::vector<int64_t> ctg_asm, ctg_local, ctg_boff, ctg_len;
+    // opt-in compact forms (pv_compact.h): then `ref` / `blocks` are empty
+    bool packed = false, compact = false;
+    std::vector<uint32_t> pref, pidx;
+    std::vector<pv_ref_run> pruns;
+    std::vector<pv_blk_group> groups;
+    std::vector<uint32_t> btab;
+    std::vector<int64_t> bexc;
 };
 
 namespace {
@@ -306,17 +313,88 @@ void load_reference(pv_core& C, const std::string& path) {
     SHA256(C.ref.data() + 64, C.ref_n, C.ref_sha);
 }
 
+// The reference in 2 bits per base plus its runs of other bytes (the reference's PackedRef, pv_compact.h:19-28, built
+// like pv_core.cpp:52-62), then the byte copy is dropped. Words are packed in parallel chunks; runs are collected per
+// chunk and joined where a run crosses a chunk boundary.
+void pack_reference(pv_core& C) {
+    const uint64_t n = C.ref_n, nw = (n + 15) / 16;
+    const uint8_t* R = C.ref.data() + 64;
+    C.pref.assign(nw + 4, 0);
+    const uint64_t chunk_words = 1u << 20;
+    const uint64_t nchunks = (nw + chunk_words - 1) / chunk_words;
+    std::vector<std::vector<pv_ref_run>> part(std::max<uint64_t>(1, nchunks));
+    parallel_for(nchunks, C.threads, [&](uint64_t t) {
+        const uint64_t q0 = t * chunk_words * 16, q1 = std::min(n, q0 + chunk_words * 16);
+        std::vector<pv_ref_run>& runs = part[t];
+        for (uint64_t q = q0; q < q1; q++) {
+            const uint8_t b = R[q];
+            const uint32_t code = b == 'A' ? 0 : b == 'C' ? 1 : b == 'G' ? 2 : b == 'T' ? 3 : 4;
+            if (code < 4) { C.pref[q >> 4] |= code << ((q & 15) * 2); continue; }
+            if (!runs.empty() && runs.back().byte == b && runs.back().start + runs.back().len == q) runs.back().len++;
+            else runs.push_back(pv_ref_run{q, 1, b});
+        }
+    });
+    C.pruns.clear();
+    for (auto& runs : part)
+        for (const pv_ref_run& r : runs) {
+            if (!C.pruns.empty() && C.pruns.back().byte == r.byte && C.pruns.back().start + C.pruns.back().len == r.start) C.pruns.back().len += r.len;
+            else C.pruns.push_back(r);
+        }
+    const uint64_t nreal = C.pruns.size();
+    C.pruns.push_back(pv_ref_run{~0ull, 0, 0});       // sentinel: every scan stops at it without a bound check
+    const uint64_t nbk = (n >> PV_REF_BUCKET_SHIFT) + 2;
+    C.pidx.assign(nbk, 0);
+    uint64_t i = 0;
+    for (uint64_t k = 0; k < nbk; k++) {
+        const uint64_t x = k << PV_REF_BUCKET_SHIFT;
+        while (i < nreal && C.pruns[i].start + C.pruns[i].len <= x) i++;
+        C.pidx[k] = (uint32_t)i;
+    }
+    if (C.pruns.size() >= (1ull << 32)) throw Err("reference with 2^32 runs of non-ACGT bytes: not packable");
+    std::vector<uint8_t>().swap(C.ref);
+}
+
+// The compact block table of one assembly (the reference's CompactTab, pv_compact.h:30-46, built like
+// pv_core.cpp:92-111): groups of PV_BLK_GROUP blocks, 32 bits per block, exception states in block order.
+void compact_blocks(pv_core& C, const Arc& X, uint64_t pay_base, uint64_t blk_base, uint64_t grp_base, std::vector<int64_t>& exc) {
+    const int64_t Q = (int64_t)C.Q;
+    for (uint64_t b = 0; b < X.nb; b++) {
+        const uint64_t len = (uint64_t)(X.off[b + 1] - X.off[b]);
+        if (len > 65535) throw Err(X.path + ": block payload over 65535 B - open without compact_blocks");
+        pv_blk_group& G = C.groups[grp_base + b / PV_BLK_GROUP];
+        const uint32_t k = (uint32_t)(b % PV_BLK_GROUP);
+        int32_t code = 0;
+        if (k == 0) {
+            G.off = pay_base + X.off[b]; G.state = X.st[b]; G.exc_mask = 0; G.exc_base = 0; G.cache_mask = 0; G.cache_base = 0;
+        } else {
+            const int64_t prev = X.st[b - 1], pc = prev >> 1;
+            const int64_t pred = (prev & 1) ? pc - Q : pc + Q;
+            const int64_t delta = (X.st[b] >> 1) - pred;
+            if (delta >= -16383 && delta <= 16383) code = (int32_t)(delta * 2 + (X.st[b] & 1));
+            else { code = PV_CODE_EXC; G.exc_mask |= 1u << k; exc.push_back(X.st[b]); }
+        }
+        C.btab[blk_base + b] = (uint32_t)len | ((uint32_t)(uint16_t)(int16_t)code << 16);
+    }
+}
+
 void pool(pv_core& C, const std::vector<std::string>& paths) {
     const size_t n = C.A.size();
-    std::vector<uint64_t> pb(n), bb(n), lb(n), cb(n), tb(n);
-    uint64_t sp = 0, sb = 0, sl = 0, sc = 0, st = 0;
+    std::vector<uint64_t> pb(n), bb(n), lb(n), cb(n), tb(n), gb(n);
+    uint64_t sp = 0, sb = 0, sl = 0, sc = 0, st = 0, sg = 0;
     for (size_t i = 0; i < n; i++) {
-        pb[i] = sp; bb[i] = sb; lb[i] = sl; cb[i] = sc; tb[i] = st;
+        pb[i] = sp; bb[i] = sb; lb[i] = sl; cb[i] = sc; tb[i] = st; gb[i] = sg;
         sp += C.A[i].payload_bytes; sb += C.A[i].nb; sl += C.A[i].low_s.size(); sc += C.A[i].rec.size(); st += C.A[i].tab.size();
+        sg += (C.A[i].nb + PV_BLK_GROUP - 1) / PV_BLK_GROUP;
         C.tab_max = std::max<uint64_t>(C.tab_max, C.A[i].tab.size());
     }
     C.payload.assign(sp + 64, 0);
-    C.blocks.assign(2 * std::max<uint64_t>(1, sb), 0);
+    std::vector<std::vector<int64_t>> exc(n);
+    if (C.compact) {
+        C.groups.assign(std::max<uint64_t>(1, sg), pv_blk_group{});
+        C.btab.assign(std::max<uint64_t>(1, sb) + PV_BLK_GROUP, 0);      // a warp reads a whole group past the last block
+    } else {
+        C.blocks.assign(2 * std::max<uint64_t>(1, sb), 0);
+    }
     C.low.assign(2 * std::max<uint64_t>(1, sl), 0);
     C.asms.assign(n, pv_asm_rec{});
     C.tabs.assign(std::max<uint64_t>(16, st), 0);
@@ -328,13 +406,17 @@ void pool(pv_core& C, const std::vector<std::string>& paths) {
             File f(paths[i]);
             if (f.size != X.file_bytes || !f.read_at(C.payload.data() + pb[i], X.payload_bytes, X.payload_at))
                 throw Err(X.path + ": short read");
-            for (uint64_t b = 0; b < X.nb; b++) {
-                C.blocks[2 * (bb[i] + b)] = pvb::block_loc(pb[i] + X.off[b], (uint64_t)(X.off[b + 1] - X.off[b]));
-                C.blocks[2 * (bb[i] + b) + 1] = (uint64_t)X.st[b];
+            if (C.compact) {
+                compact_blocks(C, X, pb[i], bb[i], gb[i], exc[i]);
+            } else {
+                for (uint64_t b = 0; b < X.nb; b++) {
+                    C.blocks[2 * (bb[i] + b)] = pvb::block_loc(pb[i] + X.off[b], (uint64_t)(X.off[b + 1] - X.off[b]));
+                    C.blocks[2 * (bb[i] + b) + 1] = (uint64_t)X.st[b];
+                }
             }
             pv_asm_rec& r = C.asms[i];
             r.nbases = X.nbases; r.blk_base = bb[i]; r.nb = X.nb; r.low_base = lb[i]; r.low_cnt = X.low_s.size();
-            r.tab_off = tb[i]; r.tab_bytes = X.tab.size();
+            r.tab_off = tb[i]; r.tab_bytes = X.tab.size(); r.grp_base = gb[i];
             for (size_t k = 0; k < X.low_s.size(); k++) { C.low[2 * (lb[i] + k)] = X.low_s[k]; C.low[2 * (lb[i] + k) + 1] = X.low_s[k] + X.low_l[k]; }
             memcpy(C.tabs.data() + tb[i], X.tab.data(), X.tab.size());
             for (size_t k = 0; k < X.rec.size(); k++) {
@@ -348,6 +430,19 @@ void pool(pv_core& C, const std::vector<std::string>& paths) {
         }
     });
     if (!first.empty()) throw Err(first);
+    if (C.compact) {                                  // exception states pooled in block order, group bases after
+        uint64_t e = 0;
+        for (size_t i = 0; i < n; i++) {
+            const uint64_t ng = (C.A[i].nb + PV_BLK_GROUP - 1) / PV_BLK_GROUP;
+            for (uint64_t g = 0; g < ng; g++) {
+                C.groups[gb[i] + g].exc_base = (uint32_t)e;
+                e += (uint64_t)__builtin_popcount(C.groups[gb[i] + g].exc_mask);
+            }
+            C.bexc.insert(C.bexc.end(), exc[i].begin(), exc[i].end());
+        }
+        if (C.bexc.size() >= (1ull << 32)) throw Err("more than 2^32 block-state exceptions: open without compact_blocks");
+        if (C.bexc.empty()) C.bexc.push_back(0);
+    }
 }
 
 const Arc* arc_at(const pv_core* c, int64_t i) {
@@ -368,9 +463,9 @@ const char* pv_last_error(void) { return g_err.c_str(); }
 int pv_core_open(const char* reference, const char* const* paths, int64_t npaths, int threads, int packed_reference,
                  int compact_blocks, pv_core** out) {
     *out = nullptr;
-    if (packed_reference || compact_blocks)
-        return fail_with(PV_EARG, "packed_reference / compact_blocks: the compact resident forms are not in this build");
     std::unique_ptr<pv_core> C(new pv_core());
+    C->packed = packed_reference != 0;
+    C->compact = compact_blocks != 0;
     try {
         if (npaths <= 0) throw Err("no archives");
         C->ref_path = reference;
@@ -390,6 +485,7 @@ int pv_core_open(const char* reference, const char* const* paths, int64_t npaths
             if (x.Q != C->Q)
                 throw Err(x.path + ": block size " + std::to_string(x.Q) + " differs from " + std::to_string(C->Q) + " (one dataset per cohort)");
         pool(*C, ps);
+        if (C->packed) pack_reference(*C);
     } catch (const Err& e) {
         return fail_with(PV_EFORMAT, e.what());
     } catch (const std::bad_alloc&) {
@@ -414,6 +510,15 @@ int pv_core_pools(const pv_core* c, pv_host_pools* o) {
     o->low = c->low.data(); o->low_bytes = c->low.size() * 8;
     o->ctg_asm = c->ctg_asm.data(); o->ctg_local = c->ctg_local.data(); o->ctg_boff = c->ctg_boff.data(); o->ctg_len = c->ctg_len.data();
     o->ncontigs = c->ctg_asm.size();
+    o->pref = c->pref.data(); o->pref_bytes = c->pref.size() * 4;
+    o->pruns = c->pruns.data(); o->pruns_bytes = c->pruns.size() * sizeof(pv_ref_run); o->pnruns = c->pruns.empty() ? 0 : c->pruns.size() - 1;
+    o->pidx = c->pidx.data(); o->pidx_bytes = c->pidx.size() * 4;
+    o->groups = c->groups.data(); o->groups_bytes = c->groups.size() * sizeof(pv_blk_group);
+    o->btab = c->btab.data(); o->btab_bytes = c->btab.size() * 4;
+    o->bexc = c->bexc.data(); o->bexc_bytes = c->bexc.size() * 8;
+    o->packed = c->packed; o->compact = c->compact;
+    if (c->packed) { o->ref_padded = nullptr; o->ref_padded_bytes = 0; }
+    if (c->compact) { o->blocks = nullptr; o->blocks_bytes = 0; }
     return PV_OK;
 }
 

@@ -32,7 +32,7 @@ constexpr int LIT_CAP = 128;   // literal bytes inside the window per item
 constexpr int RUN_CAP = 8;     // lower-case runs per item kept in shared memory
 constexpr int HOPS = 64;       // ops per chunk on the heavy path
 
-enum { ST_IDLE = 0, ST_OK = 1, ST_HEAVY = 2, ST_ERR = 3, ST_CACHED = 4 };
+enum { ST_IDLE = 0, ST_OK = 1, ST_HEAVY = 2, ST_ERR = 3, ST_CACHED = 4, ST_LOCATED = 5 };
 enum { DEC_DONE = 1, DEC_PAUSE = 0, DEC_ERR = -1, DEC_ABORT = -2 };
 
 struct Op { uint32_t src; uint16_t dk; uint16_t len; };   // dk: block offset | kind << 14
@@ -45,6 +45,12 @@ struct __align__(16) Item {
     uint64_t bst;           // block start in the stream
     uint64_t gblk;          // pooled block index
     const uint8_t* cptr;    // the block's decoded bytes in the cohort's block cache (ST_CACHED)
+    uint64_t poff;          // its stream: offset in the pooled payload
+    int64_t pst;            // its start state c << 1 | dir
+    uint64_t grp;           // compact block table: its group, its index in the group, the group's block count
+    uint32_t gj, gm;
+    uint32_t plen;          // its stream's length
+    uint32_t staged;        // the stream was copied into the slot
     uint64_t tab_off;       // the assembly's decode table in the pooled tables
     int32_t a;              // assembly
     uint32_t ox0, ox1, blen;
@@ -214,11 +220,24 @@ __device__ __forceinline__ int32_t unzz(uint32_t z) { return (int32_t)(z >> 1) ^
 __device__ __forceinline__ uint8_t comp_up(uint8_t c) { return c == 'A' ? 'T' : c == 'C' ? 'G' : c == 'G' ? 'C' : c == 'T' ? 'A' : c; }
 // The reference as a block reads it: the span its start diagonal covers, staged in shared memory by the item's TMA
 // copy, and global memory (64 readable bytes on each side of the reference) for any position off that span.
+// With the packed reference (pw != NULL) the off-span reads unpack 2-bit words and look the position up in the runs of
+// other bytes (bucket index, then a short forward scan that the sentinel run ends).
 struct RefView {
-    const uint8_t* g; uint64_t n;           // global reference and its length
+    const uint8_t* g; uint64_t n;           // global reference (byte form) and its length
     int64_t lo; uint32_t len; uint32_t sm;  // staged span: reference positions [lo, lo + len) at shared address sm
-    __device__ __forceinline__ uint32_t byte(int64_t q) const {
-        return (uint64_t)(q - lo) < (uint64_t)len ? lds8(sm + (uint32_t)(q - lo)) : (uint32_t)__ldg(g + q);
+    const uint32_t* pw; const pv_ref_run* runs; const uint32_t* pidx;   // packed form, or pw == NULL
+    __device__ __forceinline__ uint32_t packed_byte(int64_t q) const {   // 0 <= q < n
+        uint32_t b = (0x54474341u >> (8 * ((__ldg(pw + (q >> 4)) >> ((q & 15) * 2)) & 3u))) & 0xFFu;
+        for (uint32_t i = __ldg(pidx + (q >> PV_REF_BUCKET_SHIFT));; i++) {
+            const uint64_t rs = __ldg(&runs[i].start);
+            const uint32_t rl = __ldg(&runs[i].len);
+            if (rs + rl > (uint64_t)q) { if (rs <= (uint64_t)q) b = __ldg(&runs[i].byte); break; }
+        }
+        return b;
+    }
+    __device__ __forceinline__ uint32_t byte(int64_t q) const {        // 0 <= q < n
+        if ((uint64_t)(q - lo) < (uint64_t)len) return lds8(sm + (uint32_t)(q - lo));
+        return pw ? packed_byte(q) : (uint32_t)__ldg(g + q);
     }
 };
 // the reference base the diagonal predicts at block offset o: 0..3, 4 = none (refrel3.h:104-109)
@@ -426,8 +445,41 @@ __device__ __forceinline__ void lds16u(uint32_t a, uint32_t v[4]) {
     for (int i = 0; i < 4; i++) v[i] = __funnelshift_r(w[i], w[i + 1], sh);
 }
 // 16 reference bytes from position q: from the staged span when it holds all of them, else global memory
+// the four letters of four 2-bit codes (8 bits) as bytes
+__device__ __forceinline__ uint32_t letters4(uint32_t c8) {
+    const uint32_t sel = (c8 & 3u) | ((c8 & 0xCu) << 2) | ((c8 & 0x30u) << 4) | ((c8 & 0xC0u) << 6);
+    return __byte_perm(0x54474341u, 0u, sel);
+}
+// 16 bytes of the packed reference from position q (bytes outside [0, n) are 0, as the byte form's zero padding).
+// Out of line and by value, so that the byte form's callers keep their vectors in registers.
+__device__ __noinline__ uint4 packed16(const uint32_t* pw, const pv_ref_run* runs, const uint32_t* pidx, uint64_t n, int64_t q) {
+    const RefView R{nullptr, n, 0, 0, 0, pw, runs, pidx};
+    uint32_t v[4] = {0, 0, 0, 0};
+    if (q < 0 || q + 16 > (int64_t)n) {
+        for (int k = 0; k < 16; k++) {
+            const int64_t x = q + k;
+            const uint32_t b = (x >= 0 && x < (int64_t)n) ? R.packed_byte(x) : 0u;
+            if (k < 4) v[0] |= b << (8 * k); else if (k < 8) v[1] |= b << (8 * (k - 4)); else if (k < 12) v[2] |= b << (8 * (k - 8)); else v[3] |= b << (8 * (k - 12));
+        }
+        return make_uint4(v[0], v[1], v[2], v[3]);
+    }
+    const uint32_t codes = __funnelshift_r(__ldg(pw + (q >> 4)), __ldg(pw + (q >> 4) + 1), (uint32_t)(q & 15) * 2);
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] = letters4((codes >> (8 * i)) & 0xFFu);
+    uint32_t i = __ldg(pidx + (q >> PV_REF_BUCKET_SHIFT));
+    while (__ldg(&runs[i].start) + __ldg(&runs[i].len) <= (uint64_t)q) i++;
+    for (; __ldg(&runs[i].start) < (uint64_t)q + 16; i++) {
+        const int64_t rs = (int64_t)__ldg(&runs[i].start), re = rs + __ldg(&runs[i].len);
+        const int k0 = (int)((rs > q ? rs : q) - q), k1 = (int)((re < q + 16 ? re : q + 16) - q);
+        const uint32_t fill = __ldg(&runs[i].byte) * 0x01010101u;
+#pragma unroll
+        for (int w = 0; w < 4; w++) { const uint32_t m = bytes_mask(k0, k1, w); v[w] = (v[w] & ~m) | (fill & m); }
+    }
+    return make_uint4(v[0], v[1], v[2], v[3]);
+}
 __device__ __forceinline__ void ref16(const RefView& R, int64_t q, uint32_t v[4]) {
     if (q >= R.lo && q - R.lo + 16 <= (int64_t)R.len) lds16u(R.sm + (uint32_t)(q - R.lo), v);
+    else if (R.pw) { const uint4 u = packed16(R.pw, R.runs, R.pidx, R.n, q); v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; }
     else ldg16u(R.g + q, v);
 }
 
@@ -646,7 +698,8 @@ __device__ __forceinline__ uint8_t* slot_span(const Params& P, uint8_t* slot) { 
 constexpr int SPAN_MARGIN = 64;              // reference bases staged on each side of the block's start diagonal
 __device__ __forceinline__ RefView slot_ref(const Params& P, uint8_t* slot) {
     const Item* it = slot_item(slot);
-    return RefView{P.C.ref, P.C.ref_n, it->span_lo, it->span_len, smem_addr(slot_span(P, slot))};
+    return RefView{P.C.ref, P.C.ref_n, it->span_lo, it->span_len, smem_addr(slot_span(P, slot)),
+                   P.C.packed ? P.C.pref : nullptr, P.C.pruns, P.C.pidx};
 }
 
 // lane 0: the item's window and block; the ranges, its lower-case runs; false when there is nothing to decode
@@ -664,6 +717,9 @@ __device__ bool item_locate(const Params& P, uint64_t item, Item* it) {
     const uint64_t bst = b * Q, blen = R.nbases - bst < Q ? R.nbases - bst : Q;
     const uint64_t x0 = (uint64_t)s > bst ? (uint64_t)s : bst, x1 = (uint64_t)s + P.W < bst + blen ? (uint64_t)s + P.W : bst + blen;
     it->w = (int64_t)w; it->s = (uint64_t)s; it->bst = bst; it->gblk = R.blk_base + b; it->a = (int32_t)a;
+    it->grp = R.grp_base + (b >> 5); it->gj = (uint32_t)(b & 31);
+    it->gm = (uint32_t)(R.nb - (b & ~31ull) < 32 ? R.nb - (b & ~31ull) : 32);
+    it->staged = 0;
     it->tab_off = R.tab_off; it->tab_bytes = (uint32_t)R.tab_bytes; it->span_lo = 0; it->span_len = 0;
     it->ox0 = (uint32_t)(x0 - bst); it->ox1 = (uint32_t)(x1 - bst); it->blen = (uint32_t)blen;
     it->run_first = 0; it->run_cnt = 0; it->nops = 0; it->nlits = 0;
@@ -681,27 +737,63 @@ __device__ bool item_locate(const Params& P, uint64_t item, Item* it) {
                 it->runs[2 * (r - lo) + 1] = (int32_t)((re < x1 ? re : x1) - (uint64_t)s);
             }
     }
+    it->state = ST_LOCATED;
     return true;
 }
 
-// lane 0 of the item's warp: stage the assembly's decode table (and the block's stream when it fits) in the warp's
-// shared slot with TMA bulk copies, prefetch into L2 the reference span the block's diagonal covers up to the window's
-// end, then decode the block keeping the window's ops
-__device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
-    Item* it = slot_item(slot);
-    uint8_t* tab = slot_tab(P, slot);
-    uint8_t* pay = slot_pay(P, slot);
+// The block's stream (offset, length) and start state, into the Item; the state becomes ST_CACHED for a block served
+// from the cache and ST_ERR for a stream too long to be valid. All lanes call it: the full table is read by lane 0;
+// the compact table (the reference's CompactTab::get, pv_compact.h:37-48, a pass over up to 31 earlier blocks of the
+// group) is read by the warp at once: lane k holds block k of the group, the offset is a masked sum of the earlier
+// lengths and the state a masked sum of the chain increments since the last absolute state (the group's first block
+// or an exception).
+__device__ void item_block(const Params& P, Item* it, int lane) {
     const pv_dev_cohort& C = P.C;
-    const uint64_t loc = __ldg(C.blocks + 2 * it->gblk);
-    const int64_t st = (int64_t)__ldg(C.blocks + 2 * it->gblk + 1);
-    const uint32_t plen = loc_len(loc);
-    if (plen == (uint32_t)PV_BLOCK_CACHED) { it->state = ST_CACHED; it->cptr = C.cache + loc_off(loc) * C.Q; return; }
-    if (plen == (uint32_t)PV_BLEN_BAD) { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); return; }
-    const uint8_t* src = C.payload + loc_off(loc);
-    const uintptr_t pa = (uintptr_t)src & ~(uintptr_t)15, pe = ((uintptr_t)src + plen + 15) & ~(uintptr_t)15;
-    const bool stage_pay = pe - pa <= (uintptr_t)P.pay_cap;
-    // the reference span the block's start diagonal covers over the whole block, with a margin: the literal contexts
-    // and (most) copy sources of the block read it from shared memory
+    if (!C.compact) {
+        if (lane != 0) return;
+        const uint64_t loc = __ldg(C.blocks + 2 * it->gblk);
+        it->pst = (int64_t)__ldg(C.blocks + 2 * it->gblk + 1);
+        it->poff = loc_off(loc);
+        it->plen = loc_len(loc);
+        if (it->plen == (uint32_t)PV_BLOCK_CACHED) { it->state = ST_CACHED; it->cptr = C.cache + loc_off(loc) * C.Q; }
+        else if (it->plen == (uint32_t)PV_BLEN_BAD) { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
+        return;
+    }
+    const uint32_t j = it->gj, m = it->gm;
+    const pv_blk_group* G = C.groups + it->grp;
+    const uint64_t goff = __ldg(&G->off);
+    const int64_t gst = __ldg(&G->state);
+    const uint32_t emask = __ldg(&G->exc_mask), ebase = __ldg(&G->exc_base);
+    const uint32_t v = (uint32_t)lane < m ? __ldg(C.btab + (it->gblk - j) + lane) : 0u;
+    const uint32_t len = v & 0xFFFFu;
+    const int32_t code = (int32_t)(int16_t)(v >> 16);
+    const uint64_t off = goff + __reduce_add_sync(0xffffffffu, (uint32_t)lane < j ? len : 0u);
+    const int b = 31 - __clz((emask | 1u) & ((2u << j) - 1u));        // the last absolute state at or before block j
+    const int64_t base = b == 0 ? gst : __ldg(C.bexc + ebase + __popc(emask & ((1u << b) - 1u)));
+    const int32_t cprev = __shfl_up_sync(0xffffffffu, code, 1);
+    const uint32_t dprev = lane - 1 == b ? (uint32_t)(base & 1) : (uint32_t)(cprev & 1);
+    const int32_t inc = (lane > b && (uint32_t)lane <= j) ? (dprev ? -(int32_t)C.Q : (int32_t)C.Q) + (code >> 1) : 0;
+    const int32_t sum = (int32_t)__reduce_add_sync(0xffffffffu, (uint32_t)inc);
+    const int32_t cj = __shfl_sync(0xffffffffu, code, (int)j);
+    const uint32_t lj = __shfl_sync(0xffffffffu, len, (int)j);
+    if (lane != 0) return;
+    const int64_t c = (base >> 1) + sum;
+    const uint32_t dir = (int)j == b ? (uint32_t)(base & 1) : (uint32_t)(cj & 1);
+    it->poff = off; it->plen = lj; it->pst = (int64_t)((uint64_t)c << 1) | (int64_t)dir;
+    const uint32_t cmask = __ldg(&G->cache_mask);
+    if ((cmask >> j) & 1u) {
+        it->state = ST_CACHED;
+        it->cptr = C.cache + (uint64_t)(__ldg(&G->cache_base) + __popc(cmask & ((1u << j) - 1u))) * C.Q;
+    }
+}
+
+// lane 0: the reference span the block's start diagonal covers over the whole block, with a margin (the literal
+// contexts and most copy sources read it from shared memory), then TMA bulk copies into the warp's slot of the
+// assembly's decode table, the block's stream when it fits and, for the byte reference, the span
+__device__ void item_stage(const Params& P, uint8_t* slot, uint32_t bar) {
+    Item* it = slot_item(slot);
+    const pv_dev_cohort& C = P.C;
+    const int64_t st = it->pst;
     uint64_t ra = 0, re = 0;
     {
         const int64_t c0 = st >> 1, bl = (int64_t)it->blen;
@@ -711,12 +803,42 @@ __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
         if (re - ra + 16 > P.span_cap) re = ra;             // (cannot happen: span_cap holds Q + margins)
     }
     it->span_lo = (int64_t)ra; it->span_len = (uint32_t)(re - ra);
-    const uint32_t bytes = it->tab_bytes + (stage_pay ? (uint32_t)(pe - pa) : 0u) + it->span_len;
+    const uint8_t* src = C.payload + it->poff;
+    const uintptr_t pa = (uintptr_t)src & ~(uintptr_t)15, pe = ((uintptr_t)src + it->plen + 15) & ~(uintptr_t)15;
+    it->staged = pe - pa <= (uintptr_t)P.pay_cap;
+    const uint32_t span_tma = C.packed ? 0u : it->span_len;
     mbar_init(bar);
-    mbar_expect(bar, bytes);
-    bulk_g2s(smem_addr(tab), C.tabs + it->tab_off, it->tab_bytes, bar);
-    if (stage_pay) bulk_g2s(smem_addr(pay), (const void*)pa, (uint32_t)(pe - pa), bar);
-    if (it->span_len) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + ra, it->span_len, bar);
+    mbar_expect(bar, it->tab_bytes + (it->staged ? (uint32_t)(pe - pa) : 0u) + span_tma);
+    bulk_g2s(smem_addr(slot_tab(P, slot)), C.tabs + it->tab_off, it->tab_bytes, bar);
+    if (it->staged) bulk_g2s(smem_addr(slot_pay(P, slot)), (const void*)pa, (uint32_t)(pe - pa), bar);
+    if (span_tma) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + ra, span_tma, bar);
+}
+
+// the warp: the span unpacked from the packed reference into the slot (16 bases a lane-step), then the runs of other
+// bytes that overlap it written over
+__device__ void stage_span_packed(const Params& P, uint8_t* slot, int lane) {
+    const Item* it = slot_item(slot);
+    const pv_dev_cohort& C = P.C;
+    const uint64_t lo = (uint64_t)it->span_lo, hi = lo + it->span_len;
+    uint8_t* sp = slot_span(P, slot);
+    for (uint32_t i = lane; i < it->span_len / 16; i += 32) {
+        const uint32_t w = __ldg(C.pref + (lo >> 4) + i);
+        *(uint4*)(sp + 16 * i) = make_uint4(letters4(w & 0xFFu), letters4((w >> 8) & 0xFFu), letters4((w >> 16) & 0xFFu), letters4(w >> 24));
+    }
+    __syncwarp();
+    if (lo >= hi) return;
+    uint32_t r = __ldg(C.pidx + (lo >> PV_REF_BUCKET_SHIFT));
+    while (__ldg(&C.pruns[r].start) + __ldg(&C.pruns[r].len) <= lo) r++;
+    for (; __ldg(&C.pruns[r].start) < hi; r++) {
+        const uint64_t rs = __ldg(&C.pruns[r].start), re = rs + __ldg(&C.pruns[r].len);
+        const uint8_t byte = (uint8_t)__ldg(&C.pruns[r].byte);
+        for (uint64_t x = (rs > lo ? rs : lo) + lane; x < (re < hi ? re : hi); x += 32) sp[x - lo] = byte;
+    }
+}
+
+// lane 0 of the item's warp: wait (bounded) for the slot's copies, then decode the block keeping the window's ops
+__device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
+    Item* it = slot_item(slot);
     uint32_t spins = 0;
     while (!mbar_try(bar, 0)) {
         if (++spins == WAIT_SPINS) {                           // report, then wait (bounded) for the copies to land
@@ -726,13 +848,12 @@ __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
             return;
         }
     }
-    if (P.force_block) { it->state = ST_HEAVY; return; }
-    if (!stage_pay) { it->state = ST_HEAVY; return; }   // a stream longer than the slot holds (uncached long block)
+    if (P.force_block || !it->staged) { it->state = ST_HEAVY; return; }   // (a stream longer than the slot: uncached long block)
     WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
-    const uint32_t sp = smem_addr(pay) + (uint32_t)((uintptr_t)src - pa);
+    const uint32_t sp = smem_addr(slot_pay(P, slot)) + (uint32_t)((uintptr_t)(P.C.payload + it->poff) & 15);
     Dec<SmemStream> d;
-    dec_init(d, SmemStream{sp, sp + plen}, st);
-    const int r = decode_events(d, smem_addr(tab), slot_ref(P, slot), it->blen, sk);
+    dec_init(d, SmemStream{sp, sp + it->plen}, it->pst);
+    const int r = decode_events(d, smem_addr(slot_tab(P, slot)), slot_ref(P, slot), it->blen, sk);
     it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     if (r == DEC_DONE) it->state = ST_OK;
     else if (r == DEC_ABORT) it->state = ST_HEAVY;
@@ -746,17 +867,17 @@ __device__ void heavy_item(const Params& P, uint8_t* slot, uint8_t* buf, Op* hop
     const Item* it = slot_item(slot);
     const pv_dev_cohort& C = P.C;
     const uint32_t T = smem_addr(slot_tab(P, slot));
+    const RefView R = slot_ref(P, slot);
     if (threadIdx.x == 0) {
-        const uint64_t loc = C.blocks[2 * it->gblk];
-        const uint8_t* src = C.payload + loc_off(loc);
-        dec_init(h_dec, GlobalStream{src, src + loc_len(loc)}, (int64_t)C.blocks[2 * it->gblk + 1]);
+        const uint8_t* src = C.payload + it->poff;
+        dec_init(h_dec, GlobalStream{src, src + it->plen}, it->pst);
     }
     for (;;) {
         __syncthreads();
         if (threadIdx.x == 0) {
             Dec<GlobalStream> d = h_dec;
             BlockSink sk{buf, hops, 0, it->ox1};
-            h_res = decode_events(d, T, slot_ref(P, slot), it->blen, sk);
+            h_res = decode_events(d, T, R, it->blen, sk);
             h_nops = (int)sk.nops;
             h_dec = d;
         }
@@ -766,9 +887,9 @@ __device__ void heavy_item(const Params& P, uint8_t* slot, uint8_t* buf, Op* hop
             const Op o = hops[k];
             const uint32_t dst = op_dst(o), len = o.len, kind = op_kind(o);
             if (kind == 1) {
-                for (uint32_t i = threadIdx.x; i < len; i += CTA) buf[dst + i] = __ldg(C.ref + o.src + i);
+                for (uint32_t i = threadIdx.x; i < len; i += CTA) buf[dst + i] = (uint8_t)R.byte((int64_t)o.src + i);
             } else if (kind == 3) {
-                for (uint32_t i = threadIdx.x; i < len; i += CTA) buf[dst + i] = comp_up(__ldg(C.ref + o.src + len - 1 - i));
+                for (uint32_t i = threadIdx.x; i < len; i += CTA) buf[dst + i] = comp_up((uint8_t)R.byte((int64_t)o.src + len - 1 - i));
             } else {
                 const uint32_t dist = dst - o.src;
                 for (uint32_t c = 0; c < len;) {
@@ -791,7 +912,7 @@ __device__ void heavy_item(const Params& P, uint8_t* slot, uint8_t* buf, Op* hop
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(CTA, 8) pv_windows_kernel(const Params P) {
+__global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const Params P) {
     extern __shared__ uint4 smem_raw[];
     __shared__ __align__(8) uint64_t bars[WARPS];
     __shared__ Op hops[HOPS];
@@ -799,7 +920,20 @@ __global__ void __launch_bounds__(CTA, 8) pv_windows_kernel(const Params P) {
     uint8_t* slot = (uint8_t*)smem_raw + (size_t)warp * P.slot_bytes;
     Item* it = slot_item(slot);
     const uint64_t item = (uint64_t)blockIdx.x * WARPS + warp;
-    if (lane == 0 && item_locate(P, item, it)) item_decode(P, slot, smem_addr(&bars[warp]));
+    const uint32_t bar = smem_addr(&bars[warp]);
+    if (lane == 0) item_locate(P, item, it);
+    __syncwarp();
+    if (it->state == ST_LOCATED) {
+        item_block(P, it, lane);
+        __syncwarp();
+        if (it->state == ST_LOCATED) {
+            if (lane == 0) item_stage(P, slot, bar);
+            __syncwarp();
+            if (P.C.packed) stage_span_packed(P, slot, lane);
+            __syncwarp();
+            if (lane == 0) item_decode(P, slot, bar);
+        }
+    }
     __syncwarp();
     if (it->state == ST_OK) emit_ops(P, it, slot_ref(P, slot), lane);
     else if (it->state == ST_CACHED) emit(P, it, CacheGather{it->cptr}, lane, 32);
