@@ -188,6 +188,14 @@ int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const i
                   const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, uint8_t* wstatus,
                   void* work, size_t work_bytes, void* stream);
 
+/* pv_windows with the token map fused into the store. The reference maps tokens to a model's ids in a second pass
+ * over the decoded tokens (tools/megatron/panvram_loader.py:97, `lut5[raw.long()]`, after windows(tokens=True)); here
+ * out[i, 0:W] = ids[token] as int64, token as pv_windows computes it (A/a 0, C/c 1, G/g 2, T/t 3, else 4; of the
+ * complement where rc[i] != 0), written once. out: int64 [n * W] device, 16-byte aligned; ids: 5 values (host). */
+int pv_windows_ids(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
+                   const uint8_t* rc, const int64_t* ids, int64_t* out, int32_t* status, void* work, size_t work_bytes,
+                   void* stream);
+
 /* The coordinate arithmetic of Cohort.sample between its draws and its pv_windows call (panvram/cohort.py:177-189 and 193-194,
  * there six torch ops), as one launch. For window i: contig k = the first index with cum[k] > u[i] (searchsorted
  * right; u[i] in [0, cum[nctg-1]), cum the inclusive prefix sum of valid[], valid[k] = max(0, contig length - W + 1)),

@@ -89,6 +89,7 @@ for _name, _res, _args in (
         ("pv_windows_ex", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _U32, _P, _P, _P, _P, _SZ, _P]),
         ("pv_windows_work_bytes", _SZ, [ctypes.POINTER(DevCohort), _I64, _I64]),
         ("pv_windows_noalloc", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _P, _P, _P]),
+        ("pv_windows_ids", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, ctypes.POINTER(ctypes.c_int64), _P, _P, _P, _SZ, _P]),
         ("pv_sample_coords", _I32, [_P, _P, _P, _P, _P, _I64, _P, _P, ctypes.c_float, _I32, _I64, _P, _P, _P, _P, _P, _P]),
         ("pv_windows_launches", _I32, [_I64, _I64])):
     _f = getattr(_lib, _name)
@@ -253,7 +254,7 @@ def work_buffer(dev, device, n, W):
     return buf, need
 
 
-def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, out=None, status=None, flags=0, wstatus=None):
+def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, out=None, status=None, flags=0, wstatus=None, ids=None):
     """out uint8 [n, W], status int32 [1] on the cohort's device: the one-kernel window decode (pv_windows_ex).
     dev: the DevCohort of device pointers; wasm / wstart: int64 device tensors [n]; rc: None or a [n] bool/uint8 device
     tensor; wstatus: None or a zeroed uint8 device tensor of at least n bytes rounded up to 4 (per-window status).
@@ -265,7 +266,7 @@ def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, o
         raise RuntimeError("W")
     device = wasm.device
     if out is None:
-        out = torch.empty((n, W), dtype=torch.uint8, device=device)
+        out = torch.empty((n, W), dtype=torch.int64 if ids is not None else torch.uint8, device=device)
     if status is None:
         status = torch.zeros(1, dtype=torch.int32, device=device)
     rp = None
@@ -277,6 +278,15 @@ def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, o
     if wstatus is not None and wstatus.numel() < (n + 3) // 4 * 4:
         raise RuntimeError("wstatus: n bytes rounded up to a multiple of 4")
     work, need = work_buffer(dev, device, n, W)
+    if ids is not None:
+        if len(ids) != 5 or out.dtype != torch.int64:
+            raise RuntimeError("token ids: five values, int64 output")
+        idv = (ctypes.c_int64 * 5)(*[int(x) for x in ids])
+        code = _lib.pv_windows_ids(ctypes.byref(dev), wasm.data_ptr(), wstart.data_ptr(), n, W, rp, idv, out.data_ptr(), status.data_ptr(),
+                                   work.data_ptr() if work is not None else None, need, stream)
+        if code:
+            raise RuntimeError("panvram_b200 window launch: " + (_lib.pv_kernels_last_error() or b"").decode())
+        return out, status
     code = _lib.pv_windows_ex(ctypes.byref(dev), wasm.data_ptr(), wstart.data_ptr(), n, W, rp, int(bool(tokens)), int(bool(apply_case)),
                               int(flags), out.data_ptr(), status.data_ptr(), wstatus.data_ptr() if wstatus is not None else None,
                               work.data_ptr() if work is not None else None, need, stream)

@@ -41,6 +41,7 @@ class Cohort:
             raise RuntimeError("panvram_b200 needs a CUDA device (none is visible)")
         _arch_ok(self.device)
         self._index = {n: i for i, n in enumerate(self.names)}
+        self._ctg_tables = {}
         self._ctg_names = [{c[0]: k for k, c in enumerate(core.contigs(i))} for i in range(core.n)]
         pools = core.pools()
         packed, compact = core.packed_reference, core.compact_blocks
@@ -63,6 +64,7 @@ class Cohort:
         # a list to collect (start, end) CUDA events around each window-kernel launch (measurement); None = off
         self.kernel_events = None
         self._cache, self.cached_blocks = None, 0
+        self._fetch_host = self._fetch_rc = None
         if block_cache:
             self._build_block_cache(pools)
 
@@ -197,7 +199,10 @@ class Cohort:
 
     def contigs(self, assembly):
         """[(name, header, length, offset in the base stream, line width)] of an assembly."""
-        return self._core.contigs(self._asm(assembly))
+        a = self._asm(assembly)
+        if a not in self._ctg_tables:
+            self._ctg_tables[a] = self._core.contigs(a)
+        return list(self._ctg_tables[a])
 
     def resident_bytes(self):
         """Bytes of the cohort on its device (reference included), by component. Keys follow the reference's where
@@ -233,7 +238,7 @@ class Cohort:
             raise IndexError(f"contig index {c}")
         return c
 
-    def _launch(self, asm, start, W, reverse_complement, tokens, apply_case, out=None, status=None, flags=0, synced=False):
+    def _launch(self, asm, start, W, reverse_complement, tokens, apply_case, out=None, status=None, flags=0, synced=False, ids=None):
         """synced: the caller waits for the stream before it returns (windows with check), so host inputs may be
         copied without a wait of their own."""
         dev = self.device
@@ -247,22 +252,27 @@ class Cohort:
                     rc = rc.view(torch.uint8)                 # same bytes (0 / 1), no conversion kernel
                 rc = rc.to(dev, torch.uint8, non_blocking=synced).contiguous()
             if self.kernel_events is None:
-                return _C.windows_cuda(self._devc, asm, start, W, rc, tokens, apply_case, out=out, status=status, flags=flags)
+                return _C.windows_cuda(self._devc, asm, start, W, rc, tokens, apply_case, out=out, status=status, flags=flags, ids=ids)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            out = torch.empty((asm.numel(), int(W)), dtype=torch.uint8, device=dev) if out is None else out
+            out = torch.empty((asm.numel(), int(W)), dtype=torch.int64 if ids is not None else torch.uint8, device=dev) if out is None else out
             status = torch.zeros(1, dtype=torch.int32, device=dev) if status is None else status
             a.record()
-            r = _C.windows_cuda(self._devc, asm, start, W, rc, tokens, apply_case, out=out, status=status, flags=flags)
+            r = _C.windows_cuda(self._devc, asm, start, W, rc, tokens, apply_case, out=out, status=status, flags=flags, ids=ids)
             b.record()
             self.kernel_events.append((a, b))
             return r
 
-    def windows(self, asm, start, W, reverse_complement=None, tokens=False, check=True):
+    def windows(self, asm, start, W, reverse_complement=None, tokens=False, check=True, token_ids=None):
         """Bases [start, start + W) of assembly asm[i] (start = offset in the assembly's base stream: contigs
         concatenated in file order) for every i -> uint8 [n, W] on the cohort's device. reverse_complement: None or a
         bool tensor [n]. tokens: A/a 0, C/c 1, G/g 2, T/t 3, anything else 4; else the FASTA's bytes, case kept.
-        check: wait for the kernel and raise if any block failed to decode (one device sync)."""
-        out, status = self._launch(asm, start, int(W), reverse_complement, tokens, True, synced=bool(check))
+        check: wait for the kernel and raise if any block failed to decode (one device sync).
+        token_ids: five ids (for tokens 0..4) -> int64 [n, W] of those ids, mapped in the decode's store (what the
+        Megatron adapter does as lut5[windows(tokens=True).long()], tools/megatron/panvram_loader.py:96-97)."""
+        ids = None if token_ids is None else [int(x) for x in token_ids]
+        if ids is not None and len(ids) != 5:
+            raise ValueError("token_ids: five ids, for A C G T and anything else")
+        out, status = self._launch(asm, start, int(W), reverse_complement, tokens or ids is not None, True, synced=bool(check), ids=ids)
         if check:
             s = int(status.item())
             if s:
@@ -334,14 +344,20 @@ class Cohort:
         """Bases [start, start + length) of a contig (0-based) -> uint8 [length] on the cohort's device."""
         a = self._asm(assembly)
         c = self._contig(a, contig)
-        name, _, clen, boff, _ = self._core.contigs(a)[c]
+        if a not in self._ctg_tables:
+            self._ctg_tables[a] = self._core.contigs(a)
+        name, _, clen, boff, _ = self._ctg_tables[a][c]
         start, length = int(start), int(length)
         if start < 0 or length < 0 or start + length > clen:
             raise IndexError(f"{self.names[a]} {name}:{start}+{length} outside the contig ({clen} bases)")
-        asm = torch.tensor([a], dtype=torch.int64)
-        st = torch.tensor([boff + start], dtype=torch.int64)
-        rc = torch.tensor([bool(reverse_complement)]) if reverse_complement else None
-        return self.windows(asm, st, length, rc, tokens)[0]
+        if self._fetch_host is None:                       # one pinned (assembly, start) pair, one copy per call
+            self._fetch_host = torch.empty(2, dtype=torch.int64).pin_memory()
+            self._fetch_rc = torch.ones(1, dtype=torch.uint8, device=self.device)
+        self._fetch_host[0], self._fetch_host[1] = a, boff + start
+        with torch.cuda.device(self.device):
+            d = self._fetch_host.to(self.device, non_blocking=True)
+        # windows() waits for the stream before it returns, so the pinned pair is free again for the next call
+        return self.windows(d[0:1], d[1:2], length, self._fetch_rc if reverse_complement else None, tokens)[0]
 
     def _decode(self, a, chunk, out, apply_case):
         n = self._info[a]["bases"]

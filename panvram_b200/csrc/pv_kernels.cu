@@ -73,6 +73,8 @@ struct Params {
     uint32_t slot_bytes, tab_area, pay_cap, span_cap;   // a warp's shared slot: Item | table | payload | reference span
     int tokens, apply_case, force_block;
     uint32_t qshift;               // log2 of the block size
+    int64_t* out64;                // token-id output (pv_windows_ids): int64 [n, W]; then `out` is unused
+    int64_t ids[5];                // the ids of tokens 0..4
 };
 
 // status bits into the call's word and, when asked, into the window's byte (4-byte aligned, padded array)
@@ -570,7 +572,9 @@ __device__ __forceinline__ uint32_t case_mask(const Item* it, const uint64_t* __
 }
 
 // An item's output: row = its window's output row, [A, B) = the bytes of the row it writes, delta = window start -
-// block start (block offset q is window position q - delta), rcw = the window is reverse-complemented.
+// block start (block offset q is window position q - delta), rcw = the window is reverse-complemented. For the
+// token-id output the addresses are element indices of out64 (as if it were a byte array at address 0), so the same
+// 16-aligned chunking gives 16 ids per chunk, 16-byte aligned.
 struct OutRange {
     uint8_t* row; uintptr_t A, B; int64_t delta; int rcw; bool cased;
 };
@@ -578,13 +582,16 @@ __device__ __forceinline__ OutRange out_range(const Params& P, const Item* it) {
     OutRange g;
     const int64_t W = (int64_t)P.W;
     g.rcw = P.rc ? (P.rc[it->w] != 0) : 0;
-    g.row = P.out + (uint64_t)it->w * P.W;
+    g.row = P.out64 ? (uint8_t*)(uintptr_t)((uint64_t)it->w * P.W) : P.out + (uint64_t)it->w * P.W;
     g.delta = (int64_t)it->s - (int64_t)it->bst;
     const int64_t wx0 = (int64_t)it->ox0 - g.delta, wx1 = (int64_t)it->ox1 - g.delta;
     g.A = (uintptr_t)(g.row + (g.rcw ? W - wx1 : wx0));
     g.B = (uintptr_t)(g.row + (g.rcw ? W - wx0 : wx1));
     g.cased = P.apply_case && !P.tokens && it->run_cnt;
     return g;
+}
+__device__ __forceinline__ int64_t token_id(const Params& P, uint32_t t) {   // t in 0..4
+    return t == 0 ? P.ids[0] : t == 1 ? P.ids[1] : t == 2 ? P.ids[2] : t == 3 ? P.ids[3] : P.ids[4];
 }
 // the 16 forward bytes v of window positions [wpf, wpf + 16) -> the output chunk at ca (16-byte aligned): lower-case
 // runs, reverse complement, tokens, then one vector store (or, at the ends of the item's range, its bytes in [A, B))
@@ -607,11 +614,22 @@ __device__ __forceinline__ void put16(const Params& P, const Item* it, const Out
     }
     if (g.rcw) rev16(v);
     if (whole || (ca >= g.A && ca + 16 <= g.B)) {
-        *(uint4*)ca = make_uint4(v[0], v[1], v[2], v[3]);
+        if (P.out64) {
+            int64_t* o = P.out64 + ca;
+#pragma unroll
+            for (int k = 0; k < 16; k += 2)
+                *(longlong2*)(o + k) = make_longlong2(token_id(P, (v[k >> 2] >> (8 * (k & 3))) & 7u),
+                                                      token_id(P, (v[k >> 2] >> (8 * ((k + 1) & 3))) & 7u));
+        } else {
+            *(uint4*)ca = make_uint4(v[0], v[1], v[2], v[3]);
+        }
     } else {
         for (int k = 0; k < 16; k++) {
             const uintptr_t q = ca + (uintptr_t)k;
-            if (q >= g.A && q < g.B) *(uint8_t*)q = (uint8_t)(v[k >> 2] >> (8 * (k & 3)));
+            if (q < g.A || q >= g.B) continue;
+            const uint32_t b = (v[k >> 2] >> (8 * (k & 3))) & 0xFFu;
+            if (P.out64) P.out64[q] = token_id(P, b);
+            else *(uint8_t*)q = (uint8_t)b;
         }
     }
 }
@@ -1016,10 +1034,18 @@ int pv_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int6
     return pv_windows_ex(cohort, asm_index, start, n, W, rc, tokens, apply_case, 0u, out, status, nullptr, work, work_bytes, stream);
 }
 
-int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,
-                  int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, uint8_t* wstatus, void* work,
-                  size_t work_bytes, void* stream) {
+}  // extern "C"
+
+static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
+                          const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int64_t* out64,
+                          const int64_t* ids, int32_t* status, uint8_t* wstatus, void* work, size_t work_bytes, void* stream) {
     const uint32_t Q = cohort->Q;
+    if ((cohort->packed && (!cohort->pref || !cohort->pruns || !cohort->pidx)) ||
+        (cohort->compact && (!cohort->groups || !cohort->btab || !cohort->bexc)) || (!cohort->packed && !cohort->ref) ||
+        (!cohort->compact && !cohort->blocks)) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "cohort: the arrays of its resident form are missing");
+        return PV_EARG;
+    }
     if (!(Q == 1024 || Q == 2048 || Q == 4096 || Q == 16384)) { snprintf(g_cuda_err, sizeof g_cuda_err, "block size"); return PV_EARG; }
     if (W < 0 || W >= (1ll << 31)) { snprintf(g_cuda_err, sizeof g_cuda_err, "W"); return PV_EARG; }
     if (n < 0) { snprintf(g_cuda_err, sizeof g_cuda_err, "n"); return PV_EARG; }
@@ -1027,6 +1053,8 @@ int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const i
     if (n == 0 || W == 0) return PV_OK;
     Params P;
     P.C = *cohort; P.wasm = asm_index; P.wstart = start; P.rc = rc; P.out = out; P.status = status; P.wstatus = wstatus;
+    P.out64 = out64;
+    for (int k = 0; k < 5; k++) P.ids[k] = ids ? ids[k] : 0;
     P.n = (uint64_t)n; P.W = (uint64_t)W;
     if ((uint64_t)n > (1ull << 62) / (((uint64_t)W + Q - 1) / Q + 1)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
     const uint64_t grid = grid_of(Q, n, W, &P.total, &P.bpw);
@@ -1053,6 +1081,22 @@ int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const i
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
     return PV_OK;
+}
+
+extern "C" {
+
+int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,
+                  int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, uint8_t* wstatus, void* work,
+                  size_t work_bytes, void* stream) {
+    return launch_windows(cohort, asm_index, start, n, W, rc, tokens, apply_case, flags, out, nullptr, nullptr, status, wstatus,
+                          work, work_bytes, stream);
+}
+
+int pv_windows_ids(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,
+                   const int64_t* ids, int64_t* out, int32_t* status, void* work, size_t work_bytes, void* stream) {
+    if (!ids) { snprintf(g_cuda_err, sizeof g_cuda_err, "pv_windows_ids: the five token ids"); return PV_EARG; }
+    if (n > 0 && W > 0 && ((uintptr_t)out & 15)) { snprintf(g_cuda_err, sizeof g_cuda_err, "pv_windows_ids: out must be 16-byte aligned"); return PV_EARG; }
+    return launch_windows(cohort, asm_index, start, n, W, rc, 1, 0, 0u, nullptr, out, ids, status, nullptr, work, work_bytes, stream);
 }
 
 int pv_sample_coords(const int64_t* cum, const int64_t* valid, const int64_t* ctg_asm, const int64_t* ctg_boff,
