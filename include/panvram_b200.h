@@ -184,6 +184,11 @@ size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W);
  * it; the output is the same, it is for testing that path on every input. wstatus (NULL or uint8 [n], zeroed by the
  * caller) receives the PV_STATUS_* bits of each window; the cohort's block cache is filled this way at open. */
 #define PV_WIN_BLOCK_PATH 1u
+/* The kernels a call runs: by default the one-kernel form (one warp per item decodes on one lane and emits) while the
+ * call has fewer than 6,144 (window, block) items, else two launches (pv_decode_kernel: one item per lane;
+ * pv_emit_kernel: one item per warp). PV_WIN_FUSED / PV_WIN_SPLIT force one form; the output is the same. */
+#define PV_WIN_FUSED 2u
+#define PV_WIN_SPLIT 4u
 int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
                   const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, uint8_t* wstatus,
                   void* work, size_t work_bytes, void* stream);
@@ -223,7 +228,7 @@ int pv_sample_coords(const int64_t* cum, const int64_t* valid, const int64_t* ct
 int pv_windows_noalloc(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
                        const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* stream);
 
-/* number of kernel launches one pv_windows call with these sizes makes (0 for an empty call) */
+/* at most how many kernel launches one pv_windows call with these sizes makes (0 for an empty call) */
 int pv_windows_launches(int64_t n, int64_t W);
 /* message of the calling thread's last pv_windows / pv_windows_ex argument or launch failure */
 const char* pv_kernels_last_error(void);

@@ -236,6 +236,8 @@ def sha256_file_bases(path):
 
 
 PV_WIN_BLOCK_PATH = 1
+PV_WIN_FUSED = 2          # force the one-kernel form
+PV_WIN_SPLIT = 4          # force the decode + emission pair
 PV_BLOCK_CACHED = 0xFFFFFE
 
 

@@ -167,26 +167,41 @@ __device__ __forceinline__ uint32_t rans_step(Dec<S>& d, uint32_t slot, uint32_t
     renorm(d, b0, b1);
     return s;
 }
-// one symbol of a context with at most 6 symbols: the cum8 row of the staged table (T: its shared address)
-template <class S>
-__device__ __forceinline__ uint32_t dsym_small(Dec<S>& d, uint32_t T, int c) {
+// An assembly's decode table (pv_layout.h), staged in shared memory (32-bit shared address) or read in place from
+// global memory through the L1 cache.
+struct SmemTab {
+    uint32_t b;
+    __device__ __forceinline__ uint4 row(int c) const { return lds128(b + TAB_CUM8 + c * 16); }
+    __device__ __forceinline__ uint32_t doff(int bi) const { return lds16(b + TAB_DOFF + 2 * bi); }
+    __device__ __forceinline__ uint32_t bidx(int bi, uint32_t k) const { return lds8(b + TAB_BIDX + bi * (4096 / TAB_BUCKET) + k); }
+    __device__ __forceinline__ uint32_t dense(uint32_t u) const { return lds32(b + TAB_DENSE + 4 * u); }
+};
+struct GlobalTab {
+    const uint8_t* b;
+    __device__ __forceinline__ uint4 row(int c) const { return __ldg((const uint4*)(b + TAB_CUM8 + c * 16)); }
+    __device__ __forceinline__ uint32_t doff(int bi) const { return __ldg((const uint16_t*)(b + TAB_DOFF) + bi); }
+    __device__ __forceinline__ uint32_t bidx(int bi, uint32_t k) const { return __ldg(b + TAB_BIDX + bi * (4096 / TAB_BUCKET) + k); }
+    __device__ __forceinline__ uint32_t dense(uint32_t u) const { return __ldg((const uint32_t*)(b + TAB_DENSE) + u); }
+};
+// one symbol of a context with at most 6 symbols: the table's cum8 row
+template <class S, class Tb>
+__device__ __forceinline__ uint32_t dsym_small(Dec<S>& d, const Tb& T, int c) {
     const uint32_t b0 = d.st.peek(0), b1 = d.st.peek(1);
     const uint32_t slot = d.x & (MTOT - 1);
-    const uint4 r = lds128(T + TAB_CUM8 + c * 16);
+    const uint4 r = T.row(c);
     const uint32_t s = (uint32_t)((r.x >> 16) <= slot) + (uint32_t)((r.y & 0xFFFFu) <= slot) + (uint32_t)((r.y >> 16) <= slot) +
                        (uint32_t)((r.z & 0xFFFFu) <= slot) + (uint32_t)((r.z >> 16) <= slot);
     const uint32_t cm = cum_at(r, s);
     return rans_step(d, slot, s, cum_at(r, s + 1) - cm, cm, b0, b1);
 }
 // one symbol of a 104-symbol context, bi its index among the 15 of them (pv_layout.h big_index)
-template <class S>
-__device__ __forceinline__ uint32_t dsym_big(Dec<S>& d, uint32_t T, int bi) {
+template <class S, class Tb>
+__device__ __forceinline__ uint32_t dsym_big(Dec<S>& d, const Tb& T, int bi) {
     const uint32_t b0 = d.st.peek(0), b1 = d.st.peek(1);
     const uint32_t slot = d.x & (MTOT - 1);
-    const uint32_t dn = T + TAB_DENSE;
-    uint32_t u = lds16(T + TAB_DOFF + 2 * bi) + lds8(T + TAB_BIDX + bi * (4096 / TAB_BUCKET) + slot / TAB_BUCKET);
-    uint32_t e = lds32(dn + 4 * u);
-    while (dense_freq(e) && slot >= dense_cum(e) + dense_freq(e)) e = lds32(dn + 4 * (++u));
+    uint32_t u = T.doff(bi) + T.bidx(bi, slot / TAB_BUCKET);
+    uint32_t e = T.dense(u);
+    while (dense_freq(e) && slot >= dense_cum(e) + dense_freq(e)) e = T.dense(++u);
     return rans_step(d, slot, dense_sym(e), dense_freq(e), dense_cum(e), b0, b1);
 }
 // raw bits (at most 32), at most 16 per step (refrel3.h:83-90)
@@ -210,8 +225,8 @@ __device__ __forceinline__ uint32_t unbucket(uint32_t s, uint32_t extra) {
     const uint32_t e = (s - 16) / 4 + 4, m = (s - 16) & 3;
     return (1u << e) | (m << (e - 2)) | extra;
 }
-template <class S>
-__device__ __forceinline__ uint32_t dval_big(Dec<S>& d, uint32_t T, int bi) {
+template <class S, class Tb>
+__device__ __forceinline__ uint32_t dval_big(Dec<S>& d, const Tb& T, int bi) {
     const uint32_t s = dsym_big(d, T, bi);
     return unbucket(s, draw(d, s < 16 ? 0 : (s - 16) / 4 + 2));
 }
@@ -280,8 +295,8 @@ __device__ __forceinline__ void dec_init(Dec<S>& d, const S& src, int64_t st) {
 
 // The event loop of refrel3.h:114-160. Sinks: more() is asked before each event (false pauses, resumable),
 // lit()/op() returning false abort the decode (the caller takes another path). Returns DEC_*.
-template <class S, class Sink>
-__device__ __forceinline__ int decode_events(Dec<S>& d, uint32_t T, const RefView& R, uint32_t blen, Sink& sk) {
+template <class S, class Sink, class Tb>
+__device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefView& R, uint32_t blen, Sink& sk) {
     const uint64_t ref_n = R.n;
     if (d.bad) return DEC_ERR;
     while (d.o < blen) {
@@ -871,7 +886,7 @@ __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
     const uint32_t sp = smem_addr(slot_pay(P, slot)) + (uint32_t)((uintptr_t)(P.C.payload + it->poff) & 15);
     Dec<SmemStream> d;
     dec_init(d, SmemStream{sp, sp + it->plen}, it->pst);
-    const int r = decode_events(d, smem_addr(slot_tab(P, slot)), slot_ref(P, slot), it->blen, sk);
+    const int r = decode_events(d, SmemTab{smem_addr(slot_tab(P, slot))}, slot_ref(P, slot), it->blen, sk);
     it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     if (r == DEC_DONE) it->state = ST_OK;
     else if (r == DEC_ABORT) it->state = ST_HEAVY;
@@ -884,7 +899,7 @@ __device__ void heavy_item(const Params& P, uint8_t* slot, uint8_t* buf, Op* hop
     __shared__ Dec<GlobalStream> h_dec;
     const Item* it = slot_item(slot);
     const pv_dev_cohort& C = P.C;
-    const uint32_t T = smem_addr(slot_tab(P, slot));
+    const SmemTab T{smem_addr(slot_tab(P, slot))};
     const RefView R = slot_ref(P, slot);
     if (threadIdx.x == 0) {
         const uint8_t* src = C.payload + it->poff;
@@ -963,6 +978,136 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const Params P) {
     }
 }
 
+// ---------------------------------------------------------------- the split pipeline: decode lanes, then emission warps
+// pv_decode_kernel: one item per LANE. Each lane locates its window and block, looks the block up, warms L2 with the
+// reference span its emission will stage, and decodes its block's stream from global memory with its assembly's table
+// read through L1 - so a warp runs 32 independent rANS chains at once instead of one (their latencies overlap inside
+// the warp, and the other 31 lanes no longer idle). The result, the Item (ops and literal bytes inside the window),
+// goes to the plan array in global memory. pv_emit_kernel: one item per WARP, as the fused kernel's emission.
+
+// the compact table walked by one lane (the reference's chain, pv_compact.h:40-46): offset and state of block j of its group
+__device__ void item_block_lane(const Params& P, Item* it) {
+    const pv_dev_cohort& C = P.C;
+    if (!C.compact) {
+        const uint64_t loc = __ldg(C.blocks + 2 * it->gblk);
+        it->pst = (int64_t)__ldg(C.blocks + 2 * it->gblk + 1);
+        it->poff = loc_off(loc);
+        it->plen = loc_len(loc);
+        if (it->plen == (uint32_t)PV_BLOCK_CACHED) { it->state = ST_CACHED; it->cptr = C.cache + loc_off(loc) * C.Q; }
+        else if (it->plen == (uint32_t)PV_BLEN_BAD) { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
+        return;
+    }
+    const uint32_t j = it->gj;
+    const pv_blk_group* G = C.groups + it->grp;
+    const uint32_t* bt = C.btab + (it->gblk - j);
+    const uint32_t emask = __ldg(&G->exc_mask);
+    uint64_t off = __ldg(&G->off);
+    int64_t st = __ldg(&G->state);
+    uint32_t e = __ldg(&G->exc_base);
+    for (uint32_t k = 1; k <= j; k++) {
+        off += __ldg(bt + k - 1) & 0xFFFFu;
+        if ((emask >> k) & 1u) { st = __ldg(C.bexc + e++); continue; }
+        const int32_t code = (int32_t)(int16_t)(__ldg(bt + k) >> 16);
+        const int64_t pc = st >> 1, pred = (st & 1) ? pc - (int64_t)C.Q : pc + (int64_t)C.Q;
+        st = (int64_t)((uint64_t)(pred + (code >> 1)) << 1) | (int64_t)(code & 1);
+    }
+    it->poff = off; it->pst = st; it->plen = __ldg(bt + j) & 0xFFFFu;
+    const uint32_t cmask = __ldg(&G->cache_mask);
+    if ((cmask >> j) & 1u) {
+        it->state = ST_CACHED;
+        it->cptr = C.cache + (uint64_t)(__ldg(&G->cache_base) + __popc(cmask & ((1u << j) - 1u))) * C.Q;
+    }
+}
+
+// the reference span of an item (its block's start diagonal over the whole block, with a margin), 16-byte aligned
+__device__ __forceinline__ void item_span(const Params& P, Item* it) {
+    const int64_t st = it->pst, c0 = st >> 1, bl = (int64_t)it->blen;
+    int64_t lo = (st & 1) ? c0 - bl + 1 - SPAN_MARGIN : c0 - SPAN_MARGIN, hi = (st & 1) ? c0 + 1 + SPAN_MARGIN : c0 + bl + SPAN_MARGIN;
+    lo = lo < 0 ? 0 : lo; hi = hi > (int64_t)P.C.ref_n ? (int64_t)P.C.ref_n : hi;
+    uint64_t ra = 0, re = 0;
+    if (lo < hi) { ra = (uint64_t)lo & ~15ull; re = ((uint64_t)hi + 15) & ~15ull; }
+    if (re - ra + 16 > P.span_cap) re = ra;
+    it->span_lo = (int64_t)ra; it->span_len = (uint32_t)(re - ra);
+}
+
+constexpr int DEC_THREADS = 128;
+__global__ void __launch_bounds__(DEC_THREADS) pv_decode_kernel(const Params P, Item* plan) {
+    const uint64_t i = (uint64_t)blockIdx.x * DEC_THREADS + threadIdx.x;
+    if (i >= P.total) return;
+    Item* it = plan + i;
+    if (!item_locate(P, i, it)) return;
+    item_block_lane(P, it);
+    if (it->state != ST_LOCATED) return;
+    item_span(P, it);
+    const pv_dev_cohort& C = P.C;
+    if (!C.packed && it->span_len)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(C.ref + it->span_lo), "r"(it->span_len) : "memory");
+    if (P.force_block) { it->state = ST_HEAVY; return; }
+    const uint8_t* src = C.payload + it->poff;
+    WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
+    Dec<GlobalStream> d;
+    dec_init(d, GlobalStream{src, src + it->plen}, it->pst);
+    const RefView R{C.ref, C.ref_n, 0, 0, 0, C.packed ? C.pref : nullptr, C.pruns, C.pidx};
+    const int r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, sk);
+    it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
+    if (r == DEC_DONE) it->state = ST_OK;
+    else if (r == DEC_ABORT) it->state = ST_HEAVY;
+    else { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
+}
+
+__global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const Params P, const Item* plan) {
+    extern __shared__ uint4 smem_raw[];
+    __shared__ __align__(8) uint64_t bars[WARPS];
+    __shared__ Op hops[HOPS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* slot = (uint8_t*)smem_raw + (size_t)warp * P.slot_bytes;
+    Item* it = slot_item(slot);
+    const uint64_t item = (uint64_t)blockIdx.x * WARPS + warp;
+    const uint32_t bar = smem_addr(&bars[warp]);
+    if (item < P.total) {
+        const uint4* src = (const uint4*)(plan + item);
+        uint4* dst = (uint4*)it;
+        for (uint32_t k = lane; k < sizeof(Item) / 16; k += 32) dst[k] = src[k];
+    } else if (lane == 0) {
+        it->state = ST_IDLE;
+    }
+    __syncwarp();
+    const int st0 = it->state;
+    if (st0 == ST_OK || st0 == ST_HEAVY) {
+        const pv_dev_cohort& C = P.C;
+        const bool heavy = st0 == ST_HEAVY;
+        if (lane == 0) {
+            const uint32_t span_tma = C.packed ? 0u : it->span_len;
+            mbar_init(bar);
+            mbar_expect(bar, (heavy ? it->tab_bytes : 0u) + span_tma);
+            if (heavy) bulk_g2s(smem_addr(slot_tab(P, slot)), C.tabs + it->tab_off, it->tab_bytes, bar);
+            if (span_tma) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + it->span_lo, span_tma, bar);
+        }
+        __syncwarp();
+        if (C.packed) stage_span_packed(P, slot, lane);
+        if (lane == 0) {
+            uint32_t spins = 0;
+            while (!mbar_try(bar, 0)) {
+                if (++spins == WAIT_SPINS) {
+                    report(P, it->w, PV_STATUS_WAIT);
+                    it->state = ST_ERR;
+                    for (uint32_t k = 0; k < WAIT_SPINS && !mbar_try(bar, 0); k++) {}
+                    break;
+                }
+            }
+        }
+    }
+    __syncwarp();
+    if (it->state == ST_OK) emit_ops(P, it, slot_ref(P, slot), lane);
+    else if (it->state == ST_CACHED) emit(P, it, CacheGather{it->cptr}, lane, 32);
+    __syncthreads();
+    uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
+    for (int t = 0; t < WARPS; t++) {
+        uint8_t* sl = (uint8_t*)smem_raw + (size_t)t * P.slot_bytes;
+        if (slot_item(sl)->state == ST_HEAVY) heavy_item(P, sl, buf, hops);
+    }
+}
+
 // ---------------------------------------------------------------- sample() coordinates
 // The arithmetic between sample()'s draws and its window decode (panvram/cohort.py:177-189, 193-194): u uniform over all valid
 // starts -> contig k = searchsorted(cum, u, right=True), pos = u - (cum[k] - v[k]), assembly and base-stream start,
@@ -1015,7 +1160,7 @@ extern "C" {
 
 const char* pv_kernels_last_error(void) { return g_cuda_err; }
 
-int pv_windows_launches(int64_t n, int64_t W) { return (n > 0 && W > 0) ? 1 : 0; }
+int pv_windows_launches(int64_t n, int64_t W) { return (n > 0 && W > 0) ? 2 : 0; }   // (at most: 1 when fused)
 
 static uint64_t grid_of(uint32_t Q, int64_t n, int64_t W, uint64_t* total, uint64_t* bpw) {
     *bpw = ((uint64_t)W + Q - 1) / Q + 1;
@@ -1023,10 +1168,14 @@ static uint64_t grid_of(uint32_t Q, int64_t n, int64_t W, uint64_t* total, uint6
     return (*total + WARPS - 1) / WARPS;
 }
 
+// scratch: the plan (one Item per item, the split pipeline's decode results), then a Q-byte general-path buffer per CTA
+constexpr uint64_t SPLIT_MIN_ITEMS = 6144;
+static uint64_t plan_bytes(uint64_t total) { return (total * sizeof(Item) + 255) & ~255ull; }
 size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W) {
     if (n <= 0 || W <= 0) return 0;
     uint64_t total, bpw;
-    return (size_t)grid_of(cohort->Q, n, W, &total, &bpw) * cohort->Q;
+    const uint64_t grid = grid_of(cohort->Q, n, W, &total, &bpw);
+    return (size_t)(plan_bytes(total) + grid * cohort->Q);
 }
 
 int pv_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,
@@ -1059,8 +1208,16 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     if ((uint64_t)n > (1ull << 62) / (((uint64_t)W + Q - 1) / Q + 1)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
     const uint64_t grid = grid_of(Q, n, W, &P.total, &P.bpw);
     if (grid >= (1ull << 31)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
-    if (!work || work_bytes < grid * Q) { snprintf(g_cuda_err, sizeof g_cuda_err, "work buffer: %llu bytes needed", (unsigned long long)(grid * Q)); return PV_EARG; }
-    P.work = (uint8_t*)work;
+    // the fused kernel while a call's items fit in about one wave of it (its warps then overlap their chains well);
+    // the decode + emission pair beyond (32 chains per warp amortise the decode when there are many items)
+    const bool fused = (flags & PV_WIN_FUSED) ? true : (flags & PV_WIN_SPLIT) ? false : P.total < SPLIT_MIN_ITEMS;
+    const uint64_t need = plan_bytes(P.total) + grid * Q;
+    if (!work || work_bytes < need || ((uintptr_t)work & 15)) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "work buffer: %llu bytes needed, 16-byte aligned", (unsigned long long)need);
+        return PV_EARG;
+    }
+    Item* plan = (Item*)work;
+    P.work = (uint8_t*)work + plan_bytes(P.total);
     P.tokens = tokens; P.apply_case = apply_case; P.force_block = (flags & PV_WIN_BLOCK_PATH) ? 1 : 0;
     P.qshift = 0;
     while ((1u << P.qshift) < Q) P.qshift++;
@@ -1069,15 +1226,21 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     P.span_cap = (Q + 2 * SPAN_MARGIN + 64 + 15) & ~15u;
     P.slot_bytes = (uint32_t)sizeof(Item) + P.tab_area + P.pay_cap + P.span_cap;
     const size_t smem = (size_t)WARPS * P.slot_bytes;
-    static size_t smem_set[64] = {0};                    // the attribute is per device
+    static size_t smem_set[2][64] = {{0}};               // the attribute is per kernel and device
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || smem > smem_set[dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(pv_windows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (dev < 0 || dev >= 64 || smem > smem_set[fused][dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(fused ? (const void*)pv_windows_kernel : (const void*)pv_emit_kernel,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
-        if (dev >= 0 && dev < 64) smem_set[dev] = smem;
+        if (dev >= 0 && dev < 64) smem_set[fused][dev] = smem;
     }
-    pv_windows_kernel<<<(unsigned)grid, CTA, smem, (cudaStream_t)stream>>>(P);
+    if (fused) {
+        pv_windows_kernel<<<(unsigned)grid, CTA, smem, (cudaStream_t)stream>>>(P);
+    } else {
+        pv_decode_kernel<<<(unsigned)((P.total + DEC_THREADS - 1) / DEC_THREADS), DEC_THREADS, 0, (cudaStream_t)stream>>>(P, plan);
+        pv_emit_kernel<<<(unsigned)grid, CTA, smem, (cudaStream_t)stream>>>(P, plan);
+    }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
     return PV_OK;

@@ -53,7 +53,7 @@ def test_forms_give_the_same_windows(sources, src, form, cuda):
                 start = torch.from_numpy(s.astype(np.int64)).to(cuda)
                 rc = torch.from_numpy(rng.random(200) < rcp).to(cuda) if rcp else None
                 want, st_w = plain._launch(asm, start, W, rc, tokens, True)
-                for flags in (0, _C.PV_WIN_BLOCK_PATH):
+                for flags in (_C.PV_WIN_FUSED, _C.PV_WIN_SPLIT, _C.PV_WIN_BLOCK_PATH | _C.PV_WIN_FUSED, _C.PV_WIN_BLOCK_PATH | _C.PV_WIN_SPLIT):
                     got, st_g = c._launch(asm, start, W, rc, tokens, True, flags=flags)
                     torch.cuda.synchronize(cuda)
                     assert int(st_g.item()) == int(st_w.item()) == 0, (src, form, cache, W, flags)

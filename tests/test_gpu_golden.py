@@ -25,7 +25,7 @@ def _hashes(x):
     return np.array([xxhash.xxh3_64_intdigest(r.tobytes()) for r in x], dtype=np.uint64)
 
 
-@pytest.mark.parametrize("flags", [0, 1], ids=["fast-path", "block-path"])
+@pytest.mark.parametrize("flags", [2, 3, 4, 5], ids=["fused", "fused-block-path", "split", "split-block-path"])
 def test_golden_windows(golden, cohorts, flags):
     win = golden["windows"]
     for (di, W, tok, case), rows in golden_cases(win).items():
@@ -134,15 +134,16 @@ def test_corrupt_payload_parity(golden, oracle, tmp_path, cuda):
         Q, n = c.block_size, arc.nbases
         for blk in range(arc.nblocks):
             s, W = blk * Q, min(Q, n - blk * Q)
-            x, status = c._launch(torch.tensor([0]), torch.tensor([s]), W, None, False, False)
             try:
                 want = arc.window(s, W, apply_case=False)
             except oracle.OracleError:
                 want = None
-            st = int(status.item())
-            if want is None:
-                assert st == 1, (k, blk)
-                caught += 1
-            else:
-                assert st == 0 and np.array_equal(x[0].cpu().numpy(), want), (k, blk)
+            for flags in (2, 4):                            # the fused kernel, and the decode + emission pair
+                x, status = c._launch(torch.tensor([0]), torch.tensor([s]), W, None, False, False, flags=flags)
+                st = int(status.item())
+                if want is None:
+                    assert st == 1, (k, blk, flags)
+                    caught += 1
+                else:
+                    assert st == 0 and np.array_equal(x[0].cpu().numpy(), want), (k, blk, flags)
     assert caught > 0

@@ -46,7 +46,7 @@ def test_cfg0_golden(cfg0):
     c, _, _ = cfg0
     gw = dict(np.load(os.path.join(GOLDEN, "cfg0", "windows.npz")))
     for tag, rc, tok in (("plain", None, False), ("rc_tokens", gw["rc"], True), ("rc", gw["rc"], False)):
-        for flags in (0, 1):
+        for flags in (2, 3, 4, 5):                            # fused / split, each also on the block path
             x, st = c._launch(torch.from_numpy(gw["asm"]), torch.from_numpy(gw["start"]), 8192,
                               torch.from_numpy(rc) if rc is not None else None, tok, True, flags=flags)
             assert int(st.item()) == 0
@@ -103,8 +103,9 @@ def test_synth_cohort_parity(tmp_path_factory, oracle, cuda, Q):
             start = np.array([c.contigs(int(a))[int(ci)][3] + int(s) for a, ci, s, _ in co])
             want = oracle.windows(arcs, ref, co[:, 0], start, W, rc=co[:, 3], tokens=tok, threads=8)
             assert np.array_equal(x.cpu().numpy(), want), (Q, W, rcp, tok)
-            xb, st = c._launch(torch.from_numpy(co[:, 0]), torch.from_numpy(start), W, torch.from_numpy(co[:, 3]), tok, True, flags=1)
-            assert int(st.item()) == 0 and np.array_equal(xb.cpu().numpy(), want), ("block path", Q, W)
+            for flags, tag in ((3, "fused block path"), (2, "fused"), (4, "split"), (5, "split block path")):
+                xb, st = c._launch(torch.from_numpy(co[:, 0]), torch.from_numpy(start), W, torch.from_numpy(co[:, 3]), tok, True, flags=flags)
+                assert int(st.item()) == 0 and np.array_equal(xb.cpu().numpy(), want), (tag, Q, W)
     for a in range(len(c)):
         ok, _ = c.check_full(a)
         assert ok
