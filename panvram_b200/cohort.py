@@ -65,6 +65,9 @@ class Cohort:
         self.kernel_events = None
         self._cache, self.cached_blocks = None, 0
         self._fetch_host = self._fetch_rc = None
+        # PV_WIN_* flags added to every window launch: _C.PV_WIN_FUSED / PV_WIN_SPLIT pin the kernel form (default: by
+        # call size); the output is the same
+        self.launch_flags = 0
         if block_cache:
             self._build_block_cache(pools)
 
@@ -251,6 +254,7 @@ class Cohort:
                 if rc.dtype == torch.bool:
                     rc = rc.view(torch.uint8)                 # same bytes (0 / 1), no conversion kernel
                 rc = rc.to(dev, torch.uint8, non_blocking=synced).contiguous()
+            flags |= self.launch_flags
             if self.kernel_events is None:
                 return _C.windows_cuda(self._devc, asm, start, W, rc, tokens, apply_case, out=out, status=status, flags=flags, ids=ids)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -1,21 +1,25 @@
 // pv_kernels.cu - the refrel3 v1 window decode on sm_100a (pv_windows of include/panvram_b200.h).
 //
 // Replaces the reference's three-kernel path (pv_queue_kernel -> pv_case_kernel -> pv_rc_tok_kernel,
-// pv_cuda.cu:38-147) with one kernel that writes every output byte once:
-//   * work item = (window, one block the window touches); one item per warp, WARPS warps per CTA.
+// pv_cuda.cu:38-147) with kernels that write every output byte once. Work item = (window, one block it touches).
+//
+// The fused form, pv_windows_kernel (calls of fewer than 6,144 items), one item per warp, WARPS warps per CTA:
 //   * lane 0 stages into the warp's shared slot, with TMA bulk copies completing on one mbarrier (bounded wait:
 //     status 4), the assembly's compact decode table (pv_layout.h), the block's rANS stream and the reference span the
-//     block's start diagonal covers; then it decodes the stream in full (every validity check of refrel3.h:114-160, so
-//     a corrupt block reports status 1 exactly as the reference does) with the decoder state in registers, keeping
-//     only the ops and literal bytes that land inside the window. Each block's serial rANS chain runs in its own warp,
-//     so the chains' latencies overlap across warps.
-//   * the warp then writes the item's output range in 16-byte vector stores; each lane gathers its 16 bytes from the
-//     ops (reference copies realigned with funnel shifts, reverse-complement copies byte-reversed, from the staged span
-//     when it holds them), then applies lower-case runs, reverse complement and the token map in registers.
+//     block's start diagonal covers (for windows shorter than a block, only the span under the output range, the rest
+//     warmed in L2); then it decodes the stream in full (every validity check of refrel3.h:114-160, so a corrupt block
+//     reports status 1 exactly as the reference does) with the decoder state in registers, keeping only the ops and
+//     literal bytes that land inside the window. Each block's serial rANS chain runs in its own warp, so the chains'
+//     latencies overlap across warps.
+//   * the warp then writes the item's output range op by op in 16-byte vector stores (reference copies realigned with
+//     funnel shifts, reverse-complement copies byte-reversed, literals from the item's array), then lower-case runs,
+//     reverse complement and the token map (or the fused token-id map) in registers.
 //   * blocks in the cohort's block cache (decoded once at open) are copied from it like a reference span.
 //   * items needing the general path (a self copy inside the window, or more ops / literals than a slot holds) are
 //     decoded again by the whole CTA into a Q-byte block buffer in the caller's scratch, ops executed in order, then
 //     emitted the same way.
+// The split form (larger calls): pv_decode_kernel decodes one item per lane (32 chains per warp, tables through L1)
+// into a plan in the caller's scratch, then pv_emit_kernel emits one item per warp as above.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -73,6 +77,7 @@ struct Params {
     uint32_t slot_bytes, tab_area, pay_cap, span_cap;   // a warp's shared slot: Item | table | payload | reference span
     int tokens, apply_case, force_block;
     uint32_t qshift;               // log2 of the block size
+    int narrow;                    // windows shorter than a block: stage only the span under the output range
     int64_t* out64;                // token-id output (pv_windows_ids): int64 [n, W]; then `out` is unused
     int64_t ids[5];                // the ids of tokens 0..4
 };
@@ -820,22 +825,36 @@ __device__ void item_block(const Params& P, Item* it, int lane) {
     }
 }
 
+// the reference span of an item, 16-byte aligned: its block's start diagonal over the whole block, or (out_only) under
+// the item's output range only, with a margin either way; empty when it would not fit `cap` bytes
+__device__ __forceinline__ void item_span(const Params& P, Item* it, bool out_only, uint64_t cap) {
+    const int64_t st = it->pst, c0 = st >> 1;
+    const int64_t o0 = out_only ? (int64_t)it->ox0 : 0, o1 = out_only ? (int64_t)it->ox1 : (int64_t)it->blen;
+    int64_t lo = (st & 1) ? c0 - o1 + 1 - SPAN_MARGIN : c0 + o0 - SPAN_MARGIN, hi = (st & 1) ? c0 - o0 + 1 + SPAN_MARGIN : c0 + o1 + SPAN_MARGIN;
+    lo = lo < 0 ? 0 : lo; hi = hi > (int64_t)P.C.ref_n ? (int64_t)P.C.ref_n : hi;
+    uint64_t ra = 0, re = 0;
+    if (lo < hi) { ra = (uint64_t)lo & ~15ull; re = ((uint64_t)hi + 15) & ~15ull; }
+    if (re - ra + 16 > cap) re = ra;
+    it->span_lo = (int64_t)ra; it->span_len = (uint32_t)(re - ra);
+}
+
 // lane 0: the reference span the block's start diagonal covers over the whole block, with a margin (the literal
 // contexts and most copy sources read it from shared memory), then TMA bulk copies into the warp's slot of the
 // assembly's decode table, the block's stream when it fits and, for the byte reference, the span
 __device__ void item_stage(const Params& P, uint8_t* slot, uint32_t bar) {
     Item* it = slot_item(slot);
     const pv_dev_cohort& C = P.C;
-    const int64_t st = it->pst;
-    uint64_t ra = 0, re = 0;
-    {
-        const int64_t c0 = st >> 1, bl = (int64_t)it->blen;
-        int64_t lo = (st & 1) ? c0 - bl + 1 - SPAN_MARGIN : c0 - SPAN_MARGIN, hi = (st & 1) ? c0 + 1 + SPAN_MARGIN : c0 + bl + SPAN_MARGIN;
-        lo = lo < 0 ? 0 : lo; hi = hi > (int64_t)C.ref_n ? (int64_t)C.ref_n : hi;
-        if (lo < hi) { ra = (uint64_t)lo & ~15ull; re = ((uint64_t)hi + 15) & ~15ull; }
-        if (re - ra + 16 > P.span_cap) re = ra;             // (cannot happen: span_cap holds Q + margins)
+    if (P.narrow) {
+        // windows shorter than a block: the slot holds the diagonal under the output range only (what the emission
+        // reads); the whole block's span is warmed in L2 for the literal contexts the decode reads off it
+        item_span(P, it, false, ~0ull);
+        if (!C.packed && it->span_len)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(C.ref + it->span_lo), "r"(it->span_len) : "memory");
+        item_span(P, it, true, P.span_cap);
+    } else {
+        item_span(P, it, false, P.span_cap);
     }
-    it->span_lo = (int64_t)ra; it->span_len = (uint32_t)(re - ra);
+    const uint64_t ra = (uint64_t)it->span_lo;
     const uint8_t* src = C.payload + it->poff;
     const uintptr_t pa = (uintptr_t)src & ~(uintptr_t)15, pe = ((uintptr_t)src + it->plen + 15) & ~(uintptr_t)15;
     it->staged = pe - pa <= (uintptr_t)P.pay_cap;
@@ -1019,18 +1038,7 @@ __device__ void item_block_lane(const Params& P, Item* it) {
     }
 }
 
-// the reference span of an item (its block's start diagonal over the whole block, with a margin), 16-byte aligned
-__device__ __forceinline__ void item_span(const Params& P, Item* it) {
-    const int64_t st = it->pst, c0 = st >> 1, bl = (int64_t)it->blen;
-    int64_t lo = (st & 1) ? c0 - bl + 1 - SPAN_MARGIN : c0 - SPAN_MARGIN, hi = (st & 1) ? c0 + 1 + SPAN_MARGIN : c0 + bl + SPAN_MARGIN;
-    lo = lo < 0 ? 0 : lo; hi = hi > (int64_t)P.C.ref_n ? (int64_t)P.C.ref_n : hi;
-    uint64_t ra = 0, re = 0;
-    if (lo < hi) { ra = (uint64_t)lo & ~15ull; re = ((uint64_t)hi + 15) & ~15ull; }
-    if (re - ra + 16 > P.span_cap) re = ra;
-    it->span_lo = (int64_t)ra; it->span_len = (uint32_t)(re - ra);
-}
-
-constexpr int DEC_THREADS = 128;
+constexpr int DEC_THREADS = 32;            // one warp per CTA: the few decode warps of a call spread over all SMs
 __global__ void __launch_bounds__(DEC_THREADS) pv_decode_kernel(const Params P, Item* plan) {
     const uint64_t i = (uint64_t)blockIdx.x * DEC_THREADS + threadIdx.x;
     if (i >= P.total) return;
@@ -1038,7 +1046,7 @@ __global__ void __launch_bounds__(DEC_THREADS) pv_decode_kernel(const Params P, 
     if (!item_locate(P, i, it)) return;
     item_block_lane(P, it);
     if (it->state != ST_LOCATED) return;
-    item_span(P, it);
+    item_span(P, it, false, ~0ull);              // (L2 only: any length)
     const pv_dev_cohort& C = P.C;
     if (!C.packed && it->span_len)
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(C.ref + it->span_lo), "r"(it->span_len) : "memory");
@@ -1077,6 +1085,9 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const Params P, const I
         const pv_dev_cohort& C = P.C;
         const bool heavy = st0 == ST_HEAVY;
         if (lane == 0) {
+            // the span the emission reads: the start diagonal under the item's output range only (the decode has
+            // finished; anything off it comes from global memory), so the slot holds min(W, Q) bases, not Q
+            item_span(P, it, true, P.span_cap);
             const uint32_t span_tma = C.packed ? 0u : it->span_len;
             mbar_init(bar);
             mbar_expect(bar, (heavy ? it->tab_bytes : 0u) + span_tma);
@@ -1223,23 +1234,31 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     while ((1u << P.qshift) < Q) P.qshift++;
     P.tab_area = (uint32_t)((cohort->tab_max + 15) & ~15ull);
     P.pay_cap = ((Q / 32 + 32 < 160 ? 160 : Q / 32 + 32) + 15) & ~15u;
-    P.span_cap = (Q + 2 * SPAN_MARGIN + 64 + 15) & ~15u;
+    P.narrow = W < (int64_t)Q;
+    P.span_cap = (uint32_t)(((uint64_t)(P.narrow ? W : Q) + 2 * SPAN_MARGIN + 64 + 15) & ~15ull);
     P.slot_bytes = (uint32_t)sizeof(Item) + P.tab_area + P.pay_cap + P.span_cap;
     const size_t smem = (size_t)WARPS * P.slot_bytes;
+    // the emission kernel's slot: no stream, and a span of the output range's diagonal only (min(W, Q) + margins)
+    Params PE = P;
+    PE.pay_cap = 0;
+    PE.span_cap = P.span_cap;
+    PE.slot_bytes = (uint32_t)sizeof(Item) + PE.tab_area + PE.span_cap;
+    const size_t smem_e = (size_t)WARPS * PE.slot_bytes;
     static size_t smem_set[2][64] = {{0}};               // the attribute is per kernel and device
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || smem > smem_set[fused][dev]) {
+    const size_t smem_k = fused ? smem : smem_e;
+    if (dev < 0 || dev >= 64 || smem_k > smem_set[fused][dev]) {
         const cudaError_t e = cudaFuncSetAttribute(fused ? (const void*)pv_windows_kernel : (const void*)pv_emit_kernel,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_k);
         if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
-        if (dev >= 0 && dev < 64) smem_set[fused][dev] = smem;
+        if (dev >= 0 && dev < 64) smem_set[fused][dev] = smem_k;
     }
     if (fused) {
         pv_windows_kernel<<<(unsigned)grid, CTA, smem, (cudaStream_t)stream>>>(P);
     } else {
         pv_decode_kernel<<<(unsigned)((P.total + DEC_THREADS - 1) / DEC_THREADS), DEC_THREADS, 0, (cudaStream_t)stream>>>(P, plan);
-        pv_emit_kernel<<<(unsigned)grid, CTA, smem, (cudaStream_t)stream>>>(P, plan);
+        pv_emit_kernel<<<(unsigned)grid, CTA, smem_e, (cudaStream_t)stream>>>(PE, plan);
     }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
