@@ -9,9 +9,9 @@ slices decoded on the card by one sm_100a kernel.
 import torch  # noqa: F401  (CUDA context and caching allocator come from torch)
 
 from . import _C
-from .cohort import DATASETS, Cohort
+from .cohort import DATASETS, Cohort, global_batch
 
 FormatError = _C.FormatError
 with_cuda = _C.with_cuda
 __version__ = "0.1.0"
-__all__ = ["Cohort", "DATASETS", "FormatError", "with_cuda"]
+__all__ = ["Cohort", "DATASETS", "FormatError", "with_cuda", "global_batch"]

@@ -449,3 +449,19 @@ class Sampler:
         s = int(self._acc.item())
         self._acc.zero_()
         return s
+
+
+def global_batch(x, coords=None, group=None):
+    """One global batch from every rank's windows: all-gather along dim 0 in rank order (NCCL over NVLink / NVSwitch
+    when the tensors are on GPUs; any torch.distributed backend works). The ranks are replicas that never exchange
+    data otherwise - call this only when a single global batch is wanted. x: [n, ...] (the same n on every rank);
+    coords: None or [n, 4]. Returns (X [world * n, ...], C or None)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+
+    def gather(t):
+        t = t.contiguous()
+        out = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t, group=group)
+        return out
+    return gather(x), (gather(coords) if coords is not None else None)

@@ -1,5 +1,6 @@
 """The N>1 bench path's host logic on CPU ranks (gloo, world size 2): rank 0 generates the cohort while rank 1 waits
-for it; the job's time is its slowest rank's; the job's rate counts every rank's windows (replicas, weak scaling)."""
+for it; the job's time is its slowest rank's; the job's rate counts every rank's windows (replicas, weak scaling);
+global_batch gathers every rank's windows and coordinates in rank order."""
 import datetime
 import os
 import socket
@@ -27,8 +28,14 @@ def _rank(rank, world, port, data, q):
         ready = os.path.exists(os.path.join(path, "READY"))
         t = bench.max_over_ranks(0.5 + rank, world, "cpu")          # rank 1 is the slow one
         rate = bench.whole_job_rate(1024 * 10, world, t)
+        import torch
+        from panvram_b200.cohort import global_batch
+        x = torch.full((3, 5), rank + 1, dtype=torch.uint8)
+        co = torch.arange(12, dtype=torch.int64).view(3, 4) + 100 * rank
+        X, Co = global_batch(x, co)
+        gathered = (X[:, 0].tolist(), Co[:, 0].tolist())
         dist.barrier()
-        q.put((rank, path, ds, ready, t, rate))
+        q.put((rank, path, ds, ready, t, rate, gathered))
     finally:
         dist.destroy_process_group()
 
@@ -44,9 +51,11 @@ def test_two_cpu_ranks(tmp_path):
     for p in procs:
         p.join(60)
         assert p.exitcode == 0
-    (r0, path0, ds0, ready0, t0, rate0), (r1, path1, ds1, ready1, t1, rate1) = got
+    (r0, path0, ds0, ready0, t0, rate0, g0), (r1, path1, ds1, ready1, t1, rate1, g1) = got
     assert (r0, r1) == (0, 1)
     assert path0 == path1 == os.path.join(str(tmp_path), "cfg0") and ds0 == ds1 == "q4k"
     assert ready0 and ready1
     assert t0 == t1 == 1.5
     assert rate0 == rate1 == 2 * 1024 * 10 / 1.5
+    # the global batch: every rank's rows, in rank order, on every rank
+    assert g0 == g1 == ([1, 1, 1, 2, 2, 2], [0, 4, 8, 100, 104, 108])
