@@ -326,13 +326,20 @@ __device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefVi
         }
         if (d.o == blen) break;
         const uint32_t kind = dsym_small(d, T, C_KIND + (int)(llc(ll) * 4 + kc));
-        uint64_t p = 0; uint32_t dir = 0, dist = 0; int ki = 0; int32_t dd = 0;
-        if (kind == K_CONT || kind == K_DELTA) { if (kind == K_DELTA) dd = unzz(dval_big(d, T, 4 + (ll == 0 ? 0 : 1))); }
-        else if (kind == K_REP) { ki = 1 + (int)dsym_small(d, T, C_REPK); dd = unzz(dval_big(d, T, 6)); if (ki >= d.nc) return DEC_ERR; }
-        else if (kind == K_ABS) { dir = dsym_small(d, T, C_DIR); p = draw(d, 32); }
-        else if (kind == K_SELF) dist = dval_big(d, T, 7);
-        else if (kind == K_FLIP) { ki = (int)dsym_small(d, T, C_FLIPK); dd = unzz(dval_big(d, T, 14)); if (ki >= d.nc) return DEC_ERR; }
-        else return DEC_ERR;
+        if (kind > K_FLIP) return DEC_ERR;
+        // the kind's arguments, in stream order: at most one small symbol (REP: cache index - 1, ABS: strand, FLIP: cache
+        // index), then one bucketed value (DELTA / REP / FLIP: zig-zag delta, SELF: distance) or, for ABS, 32 raw bits.
+        // Each read appears once here, so the decoder's inlined code stays small (it shares the instruction cache).
+        uint64_t p = 0;
+        uint32_t sarg = 0, varg = 0;
+        if (kind == K_REP || kind == K_ABS || kind == K_FLIP) sarg = dsym_small(d, T, kind == K_REP ? C_REPK : kind == K_ABS ? C_DIR : C_FLIPK);
+        if (kind == K_ABS) p = draw(d, 32);
+        else if (kind != K_CONT) varg = dval_big(d, T, kind == K_DELTA ? 4 + (ll == 0 ? 0 : 1) : kind == K_REP ? 6 : kind == K_SELF ? 7 : 14);
+        const uint32_t dist = kind == K_SELF ? varg : 0;
+        uint32_t dir = kind == K_ABS ? sarg : 0;
+        const int ki = kind == K_REP ? 1 + (int)sarg : kind == K_FLIP ? (int)sarg : 0;
+        const int32_t dd = (kind == K_DELTA || kind == K_REP || kind == K_FLIP) ? unzz(varg) : 0;
+        if ((kind == K_REP || kind == K_FLIP) && ki >= d.nc) return DEC_ERR;
         const uint32_t L = dval_big(d, T, 8 + (int)kind) + MINL;            // LEN x kind
         if (d.bad || L > blen - d.o) return DEC_ERR;
         uint32_t okind; uint64_t osrc;
@@ -610,8 +617,17 @@ __device__ __forceinline__ OutRange out_range(const Params& P, const Item* it) {
     g.cased = P.apply_case && !P.tokens && it->run_cnt;
     return g;
 }
-__device__ __forceinline__ int64_t token_id(const Params& P, uint32_t t) {   // t in 0..4
-    return t == 0 ? P.ids[0] : t == 1 ? P.ids[1] : t == 2 ? P.ids[2] : t == 3 ? P.ids[3] : P.ids[4];
+// the token-id store (pv_windows_ids): 16 tokens -> 16 int64 ids at element index ca of out64 (those in [A, B) when not
+// whole). Out of line, with plain arguments, so the byte stores' hot loop stays small.
+__device__ __noinline__ void store_ids(int64_t* out64, int64_t i0, int64_t i1, int64_t i2, int64_t i3, int64_t i4, uintptr_t A,
+                                      uintptr_t B, uintptr_t ca, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3, bool whole) {
+    const uint32_t v[4] = {v0, v1, v2, v3};
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+        const uint32_t t = (v[k >> 2] >> (8 * (k & 3))) & 7u;
+        const int64_t id = t == 0 ? i0 : t == 1 ? i1 : t == 2 ? i2 : t == 3 ? i3 : i4;
+        if (whole || (ca + k >= A && ca + k < B)) out64[ca + k] = id;
+    }
 }
 // the 16 forward bytes v of window positions [wpf, wpf + 16) -> the output chunk at ca (16-byte aligned): lower-case
 // runs, reverse complement, tokens, then one vector store (or, at the ends of the item's range, its bytes in [A, B))
@@ -633,23 +649,17 @@ __device__ __forceinline__ void put16(const Params& P, const Item* it, const Out
         for (int i = 0; i < 4; i++) v[i] = comp4(v[i]);
     }
     if (g.rcw) rev16(v);
+    if (P.out64) {
+        store_ids(P.out64, P.ids[0], P.ids[1], P.ids[2], P.ids[3], P.ids[4], g.A, g.B, ca, v[0], v[1], v[2], v[3],
+                  whole || (ca >= g.A && ca + 16 <= g.B));
+        return;
+    }
     if (whole || (ca >= g.A && ca + 16 <= g.B)) {
-        if (P.out64) {
-            int64_t* o = P.out64 + ca;
-#pragma unroll
-            for (int k = 0; k < 16; k += 2)
-                *(longlong2*)(o + k) = make_longlong2(token_id(P, (v[k >> 2] >> (8 * (k & 3))) & 7u),
-                                                      token_id(P, (v[k >> 2] >> (8 * ((k + 1) & 3))) & 7u));
-        } else {
-            *(uint4*)ca = make_uint4(v[0], v[1], v[2], v[3]);
-        }
+        *(uint4*)ca = make_uint4(v[0], v[1], v[2], v[3]);
     } else {
         for (int k = 0; k < 16; k++) {
             const uintptr_t q = ca + (uintptr_t)k;
-            if (q < g.A || q >= g.B) continue;
-            const uint32_t b = (v[k >> 2] >> (8 * (k & 3))) & 0xFFu;
-            if (P.out64) P.out64[q] = token_id(P, b);
-            else *(uint8_t*)q = (uint8_t)b;
+            if (q >= g.A && q < g.B) *(uint8_t*)q = (uint8_t)(v[k >> 2] >> (8 * (k & 3)));
         }
     }
 }
@@ -734,10 +744,13 @@ __device__ __forceinline__ uint8_t* slot_tab(const Params& P, uint8_t* slot) { (
 __device__ __forceinline__ uint8_t* slot_pay(const Params& P, uint8_t* slot) { return slot + sizeof(Item) + P.tab_area; }
 __device__ __forceinline__ uint8_t* slot_span(const Params& P, uint8_t* slot) { return slot + sizeof(Item) + P.tab_area + P.pay_cap; }
 constexpr int SPAN_MARGIN = 64;              // reference bases staged on each side of the block's start diagonal
+// PK / CP: the cohort keeps the packed reference / the compact block table. The kernels are instantiated per form, so
+// the plain form's code carries neither (smaller code for the instruction cache, no runtime checks).
+template <bool PK>
 __device__ __forceinline__ RefView slot_ref(const Params& P, uint8_t* slot) {
     const Item* it = slot_item(slot);
     return RefView{P.C.ref, P.C.ref_n, it->span_lo, it->span_len, smem_addr(slot_span(P, slot)),
-                   P.C.packed ? P.C.pref : nullptr, P.C.pruns, P.C.pidx};
+                   PK ? P.C.pref : nullptr, P.C.pruns, P.C.pidx};
 }
 
 // lane 0: the item's window and block; the ranges, its lower-case runs; false when there is nothing to decode
@@ -785,9 +798,10 @@ __device__ bool item_locate(const Params& P, uint64_t item, Item* it) {
 // group) is read by the warp at once: lane k holds block k of the group, the offset is a masked sum of the earlier
 // lengths and the state a masked sum of the chain increments since the last absolute state (the group's first block
 // or an exception).
+template <bool CP>
 __device__ void item_block(const Params& P, Item* it, int lane) {
     const pv_dev_cohort& C = P.C;
-    if (!C.compact) {
+    if (!CP) {
         if (lane != 0) return;
         const uint64_t loc = __ldg(C.blocks + 2 * it->gblk);
         it->pst = (int64_t)__ldg(C.blocks + 2 * it->gblk + 1);
@@ -841,6 +855,7 @@ __device__ __forceinline__ void item_span(const Params& P, Item* it, bool out_on
 // lane 0: the reference span the block's start diagonal covers over the whole block, with a margin (the literal
 // contexts and most copy sources read it from shared memory), then TMA bulk copies into the warp's slot of the
 // assembly's decode table, the block's stream when it fits and, for the byte reference, the span
+template <bool PK>
 __device__ void item_stage(const Params& P, uint8_t* slot, uint32_t bar) {
     Item* it = slot_item(slot);
     const pv_dev_cohort& C = P.C;
@@ -848,7 +863,7 @@ __device__ void item_stage(const Params& P, uint8_t* slot, uint32_t bar) {
         // windows shorter than a block: the slot holds the diagonal under the output range only (what the emission
         // reads); the whole block's span is warmed in L2 for the literal contexts the decode reads off it
         item_span(P, it, false, ~0ull);
-        if (!C.packed && it->span_len)
+        if (!PK && it->span_len)
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(C.ref + it->span_lo), "r"(it->span_len) : "memory");
         item_span(P, it, true, P.span_cap);
     } else {
@@ -858,7 +873,7 @@ __device__ void item_stage(const Params& P, uint8_t* slot, uint32_t bar) {
     const uint8_t* src = C.payload + it->poff;
     const uintptr_t pa = (uintptr_t)src & ~(uintptr_t)15, pe = ((uintptr_t)src + it->plen + 15) & ~(uintptr_t)15;
     it->staged = pe - pa <= (uintptr_t)P.pay_cap;
-    const uint32_t span_tma = C.packed ? 0u : it->span_len;
+    const uint32_t span_tma = PK ? 0u : it->span_len;
     mbar_init(bar);
     mbar_expect(bar, it->tab_bytes + (it->staged ? (uint32_t)(pe - pa) : 0u) + span_tma);
     bulk_g2s(smem_addr(slot_tab(P, slot)), C.tabs + it->tab_off, it->tab_bytes, bar);
@@ -889,6 +904,7 @@ __device__ void stage_span_packed(const Params& P, uint8_t* slot, int lane) {
 }
 
 // lane 0 of the item's warp: wait (bounded) for the slot's copies, then decode the block keeping the window's ops
+template <bool PK>
 __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
     Item* it = slot_item(slot);
     uint32_t spins = 0;
@@ -905,21 +921,23 @@ __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
     const uint32_t sp = smem_addr(slot_pay(P, slot)) + (uint32_t)((uintptr_t)(P.C.payload + it->poff) & 15);
     Dec<SmemStream> d;
     dec_init(d, SmemStream{sp, sp + it->plen}, it->pst);
-    const int r = decode_events(d, SmemTab{smem_addr(slot_tab(P, slot))}, slot_ref(P, slot), it->blen, sk);
+    const int r = decode_events(d, SmemTab{smem_addr(slot_tab(P, slot))}, slot_ref<PK>(P, slot), it->blen, sk);
     it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     if (r == DEC_DONE) it->state = ST_OK;
     else if (r == DEC_ABORT) it->state = ST_HEAVY;
     else { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
 }
 
-// the CTA decodes a heavy item into its shared block buffer, ops in order, then emits it
-__device__ void heavy_item(const Params& P, uint8_t* slot, uint8_t* buf, Op* hops) {
+// the CTA decodes a heavy item into its shared block buffer, ops in order, then emits it. Out of line: it is rare, and
+// its code (a second decoder and an emission) would otherwise share the instruction cache with the common path.
+template <bool PK>
+__device__ __noinline__ void heavy_item(const Params& P, uint8_t* slot, uint8_t* buf, Op* hops) {
     __shared__ int h_res, h_nops;
     __shared__ Dec<GlobalStream> h_dec;
     const Item* it = slot_item(slot);
     const pv_dev_cohort& C = P.C;
     const SmemTab T{smem_addr(slot_tab(P, slot))};
-    const RefView R = slot_ref(P, slot);
+    const RefView R = slot_ref<PK>(P, slot);
     if (threadIdx.x == 0) {
         const uint8_t* src = C.payload + it->poff;
         dec_init(h_dec, GlobalStream{src, src + it->plen}, it->pst);
@@ -964,7 +982,8 @@ __device__ void heavy_item(const Params& P, uint8_t* slot, uint8_t* buf, Op* hop
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const Params P) {
+template <bool PK, bool CP>
+__global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constant__ Params P) {
     extern __shared__ uint4 smem_raw[];
     __shared__ __align__(8) uint64_t bars[WARPS];
     __shared__ Op hops[HOPS];
@@ -976,24 +995,24 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const Params P) {
     if (lane == 0) item_locate(P, item, it);
     __syncwarp();
     if (it->state == ST_LOCATED) {
-        item_block(P, it, lane);
+        item_block<CP>(P, it, lane);
         __syncwarp();
         if (it->state == ST_LOCATED) {
-            if (lane == 0) item_stage(P, slot, bar);
+            if (lane == 0) item_stage<PK>(P, slot, bar);
             __syncwarp();
-            if (P.C.packed) stage_span_packed(P, slot, lane);
+            if (PK) stage_span_packed(P, slot, lane);
             __syncwarp();
-            if (lane == 0) item_decode(P, slot, bar);
+            if (lane == 0) item_decode<PK>(P, slot, bar);
         }
     }
     __syncwarp();
-    if (it->state == ST_OK) emit_ops(P, it, slot_ref(P, slot), lane);
+    if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
     else if (it->state == ST_CACHED) emit(P, it, CacheGather{it->cptr}, lane, 32);
     __syncthreads();
     uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
     for (int t = 0; t < WARPS; t++) {
         uint8_t* sl = (uint8_t*)smem_raw + (size_t)t * P.slot_bytes;
-        if (slot_item(sl)->state == ST_HEAVY) heavy_item(P, sl, buf, hops);
+        if (slot_item(sl)->state == ST_HEAVY) heavy_item<PK>(P, sl, buf, hops);
     }
 }
 
@@ -1005,9 +1024,10 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const Params P) {
 // goes to the plan array in global memory. pv_emit_kernel: one item per WARP, as the fused kernel's emission.
 
 // the compact table walked by one lane (the reference's chain, pv_compact.h:40-46): offset and state of block j of its group
+template <bool CP>
 __device__ void item_block_lane(const Params& P, Item* it) {
     const pv_dev_cohort& C = P.C;
-    if (!C.compact) {
+    if (!CP) {
         const uint64_t loc = __ldg(C.blocks + 2 * it->gblk);
         it->pst = (int64_t)__ldg(C.blocks + 2 * it->gblk + 1);
         it->poff = loc_off(loc);
@@ -1039,23 +1059,24 @@ __device__ void item_block_lane(const Params& P, Item* it) {
 }
 
 constexpr int DEC_THREADS = 32;            // one warp per CTA: the few decode warps of a call spread over all SMs
-__global__ void __launch_bounds__(DEC_THREADS) pv_decode_kernel(const Params P, Item* plan) {
+template <bool PK, bool CP>
+__global__ void __launch_bounds__(DEC_THREADS) pv_decode_kernel(const __grid_constant__ Params P, Item* plan) {
     const uint64_t i = (uint64_t)blockIdx.x * DEC_THREADS + threadIdx.x;
     if (i >= P.total) return;
     Item* it = plan + i;
     if (!item_locate(P, i, it)) return;
-    item_block_lane(P, it);
+    item_block_lane<CP>(P, it);
     if (it->state != ST_LOCATED) return;
     item_span(P, it, false, ~0ull);              // (L2 only: any length)
     const pv_dev_cohort& C = P.C;
-    if (!C.packed && it->span_len)
+    if (!PK && it->span_len)
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(C.ref + it->span_lo), "r"(it->span_len) : "memory");
     if (P.force_block) { it->state = ST_HEAVY; return; }
     const uint8_t* src = C.payload + it->poff;
     WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
     Dec<GlobalStream> d;
     dec_init(d, GlobalStream{src, src + it->plen}, it->pst);
-    const RefView R{C.ref, C.ref_n, 0, 0, 0, C.packed ? C.pref : nullptr, C.pruns, C.pidx};
+    const RefView R{C.ref, C.ref_n, 0, 0, 0, PK ? C.pref : nullptr, C.pruns, C.pidx};
     const int r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, sk);
     it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     if (r == DEC_DONE) it->state = ST_OK;
@@ -1063,7 +1084,8 @@ __global__ void __launch_bounds__(DEC_THREADS) pv_decode_kernel(const Params P, 
     else { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
 }
 
-__global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const Params P, const Item* plan) {
+template <bool PK>
+__global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__ Params P, const Item* plan) {
     extern __shared__ uint4 smem_raw[];
     __shared__ __align__(8) uint64_t bars[WARPS];
     __shared__ Op hops[HOPS];
@@ -1088,14 +1110,14 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const Params P, const I
             // the span the emission reads: the start diagonal under the item's output range only (the decode has
             // finished; anything off it comes from global memory), so the slot holds min(W, Q) bases, not Q
             item_span(P, it, true, P.span_cap);
-            const uint32_t span_tma = C.packed ? 0u : it->span_len;
+            const uint32_t span_tma = PK ? 0u : it->span_len;
             mbar_init(bar);
             mbar_expect(bar, (heavy ? it->tab_bytes : 0u) + span_tma);
             if (heavy) bulk_g2s(smem_addr(slot_tab(P, slot)), C.tabs + it->tab_off, it->tab_bytes, bar);
             if (span_tma) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + it->span_lo, span_tma, bar);
         }
         __syncwarp();
-        if (C.packed) stage_span_packed(P, slot, lane);
+        if (PK) stage_span_packed(P, slot, lane);
         if (lane == 0) {
             uint32_t spins = 0;
             while (!mbar_try(bar, 0)) {
@@ -1109,13 +1131,13 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const Params P, const I
         }
     }
     __syncwarp();
-    if (it->state == ST_OK) emit_ops(P, it, slot_ref(P, slot), lane);
+    if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
     else if (it->state == ST_CACHED) emit(P, it, CacheGather{it->cptr}, lane, 32);
     __syncthreads();
     uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
     for (int t = 0; t < WARPS; t++) {
         uint8_t* sl = (uint8_t*)smem_raw + (size_t)t * P.slot_bytes;
-        if (slot_item(sl)->state == ST_HEAVY) heavy_item(P, sl, buf, hops);
+        if (slot_item(sl)->state == ST_HEAVY) heavy_item<PK>(P, sl, buf, hops);
     }
 }
 
@@ -1196,6 +1218,50 @@ int pv_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int6
 
 }  // extern "C"
 
+// kernel launches per resident form (packed reference / compact block table), each with its dynamic shared memory
+// attribute set once per device and size
+static cudaError_t smem_attr(const void* fn, int slot, size_t smem) {
+    static size_t set[12][64] = {{0}};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && smem <= set[slot][dev]) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess && dev >= 0 && dev < 64) set[slot][dev] = smem;
+    return e;
+}
+template <bool PK, bool CP>
+static cudaError_t fused_form(uint64_t grid, size_t smem, cudaStream_t st, const Params& P) {
+    const cudaError_t e = smem_attr((const void*)pv_windows_kernel<PK, CP>, (PK ? 1 : 0) | (CP ? 2 : 0), smem);
+    if (e != cudaSuccess) return e;
+    pv_windows_kernel<PK, CP><<<(unsigned)grid, CTA, smem, st>>>(P);
+    return cudaGetLastError();
+}
+template <bool PK, bool CP>
+static cudaError_t split_form(uint64_t total, uint64_t grid, size_t smem_e, cudaStream_t st, const Params& P, const Params& PE, Item* plan) {
+    const cudaError_t e = smem_attr((const void*)pv_emit_kernel<PK>, 4 + (PK ? 1 : 0), smem_e);
+    if (e != cudaSuccess) return e;
+    pv_decode_kernel<PK, CP><<<(unsigned)((total + DEC_THREADS - 1) / DEC_THREADS), DEC_THREADS, 0, st>>>(P, plan);
+    pv_emit_kernel<PK><<<(unsigned)grid, CTA, smem_e, st>>>(PE, plan);
+    return cudaGetLastError();
+}
+static cudaError_t launch_fused(int form, uint64_t grid, size_t smem, cudaStream_t st, const Params& P) {
+    switch (form) {
+    case 0: return fused_form<false, false>(grid, smem, st, P);
+    case 1: return fused_form<true, false>(grid, smem, st, P);
+    case 2: return fused_form<false, true>(grid, smem, st, P);
+    default: return fused_form<true, true>(grid, smem, st, P);
+    }
+}
+static cudaError_t launch_split(int form, uint64_t total, uint64_t grid, size_t smem_e, cudaStream_t st, const Params& P,
+                                const Params& PE, Item* plan) {
+    switch (form) {
+    case 0: return split_form<false, false>(total, grid, smem_e, st, P, PE, plan);
+    case 1: return split_form<true, false>(total, grid, smem_e, st, P, PE, plan);
+    case 2: return split_form<false, true>(total, grid, smem_e, st, P, PE, plan);
+    default: return split_form<true, true>(total, grid, smem_e, st, P, PE, plan);
+    }
+}
+
 static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
                           const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int64_t* out64,
                           const int64_t* ids, int32_t* status, uint8_t* wstatus, void* work, size_t work_bytes, void* stream) {
@@ -1244,22 +1310,10 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     PE.span_cap = P.span_cap;
     PE.slot_bytes = (uint32_t)sizeof(Item) + PE.tab_area + PE.span_cap;
     const size_t smem_e = (size_t)WARPS * PE.slot_bytes;
-    static size_t smem_set[2][64] = {{0}};               // the attribute is per kernel and device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const size_t smem_k = fused ? smem : smem_e;
-    if (dev < 0 || dev >= 64 || smem_k > smem_set[fused][dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(fused ? (const void*)pv_windows_kernel : (const void*)pv_emit_kernel,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_k);
-        if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
-        if (dev >= 0 && dev < 64) smem_set[fused][dev] = smem_k;
-    }
-    if (fused) {
-        pv_windows_kernel<<<(unsigned)grid, CTA, smem, (cudaStream_t)stream>>>(P);
-    } else {
-        pv_decode_kernel<<<(unsigned)((P.total + DEC_THREADS - 1) / DEC_THREADS), DEC_THREADS, 0, (cudaStream_t)stream>>>(P, plan);
-        pv_emit_kernel<<<(unsigned)grid, CTA, smem_e, (cudaStream_t)stream>>>(PE, plan);
-    }
+    const int form = (cohort->packed ? 1 : 0) | (cohort->compact ? 2 : 0);
+    const cudaError_t le = fused ? launch_fused(form, grid, smem, (cudaStream_t)stream, P)
+                                 : launch_split(form, P.total, grid, smem_e, (cudaStream_t)stream, P, PE, plan);
+    if (le != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(le)); return PV_ECUDA; }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
     return PV_OK;
