@@ -241,22 +241,22 @@ PV_WIN_SPLIT = 4          # force the decode + emission pair
 PV_BLOCK_CACHED = 0xFFFFFE
 
 
-_work = {}
+
+
+def work_bytes(dev, n, W):
+    """Bytes of device scratch a window call with these sizes needs (pv_windows_work_bytes)."""
+    return int(_lib.pv_windows_work_bytes(ctypes.byref(dev), int(n), int(W)))
 
 
 def work_buffer(dev, device, n, W):
-    """The device scratch a window call needs (grown and kept per device; calls on one device share it in stream
-    order, as torch's own caching allocator would)."""
-    need = int(_lib.pv_windows_work_bytes(ctypes.byref(dev), int(n), int(W)))
-    key = (device.type, device.index)
-    buf = _work.get(key)
-    if need and (buf is None or buf.numel() < need):
-        buf = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=device)
-        _work[key] = buf
-    return buf, need
+    """Fresh device scratch for one window call, from torch's caching allocator on the current stream (so calls on
+    different streams never share it, and a captured graph keeps the one it was captured with alive)."""
+    need = work_bytes(dev, n, W)
+    return (torch.empty(need, dtype=torch.uint8, device=device) if need else None), need
 
 
-def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, out=None, status=None, flags=0, wstatus=None, ids=None):
+def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, out=None, status=None, flags=0, wstatus=None, ids=None,
+                 work=None):
     """out uint8 [n, W], status int32 [1] on the cohort's device: the one-kernel window decode (pv_windows_ex).
     dev: the DevCohort of device pointers; wasm / wstart: int64 device tensors [n]; rc: None or a [n] bool/uint8 device
     tensor; wstatus: None or a zeroed uint8 device tensor of at least n bytes rounded up to 4 (per-window status).
@@ -279,7 +279,12 @@ def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, o
     stream = torch.cuda.current_stream(device).cuda_stream
     if wstatus is not None and wstatus.numel() < (n + 3) // 4 * 4:
         raise RuntimeError("wstatus: n bytes rounded up to a multiple of 4")
-    work, need = work_buffer(dev, device, n, W)
+    if work is None:
+        work, need = work_buffer(dev, device, n, W)
+    else:
+        need = work_bytes(dev, n, W)
+        if work.numel() < need:
+            raise RuntimeError("scratch buffer too small")
     if ids is not None:
         if len(ids) != 5 or out.dtype != torch.int64:
             raise RuntimeError("token ids: five values, int64 output")

@@ -576,16 +576,9 @@ struct CacheGather {
 };
 
 // lower-case mask of window positions [wp, wp + 16) (bit k = position wp + k)
-__device__ __forceinline__ uint32_t case_mask(const Item* it, const uint64_t* __restrict__ low, int64_t wp) {
+// (the runs of an item with more than RUN_CAP of them, from global memory: rare, out of line)
+__device__ __noinline__ uint32_t case_mask_global(const Item* it, const uint64_t* __restrict__ low, int64_t wp) {
     uint32_t m = 0;
-    if (it->run_cnt <= (uint32_t)RUN_CAP) {
-        for (uint32_t r = 0; r < it->run_cnt; r++) {
-            const int64_t lo = it->runs[2 * r] > wp ? it->runs[2 * r] : wp;
-            const int64_t hi = it->runs[2 * r + 1] < wp + 16 ? it->runs[2 * r + 1] : wp + 16;
-            if (lo < hi) m |= ((1u << (hi - lo)) - 1) << (lo - wp);
-        }
-        return m;
-    }
     const int64_t x = (int64_t)it->s + wp;              // stream position of bit 0
     uint32_t lo = 0, hi = it->run_cnt;
     while (lo < hi) { const uint32_t mid = (lo + hi) >> 1; if ((int64_t)__ldg(low + 2 * (it->run_first + mid) + 1) <= x) lo = mid + 1; else hi = mid; }
@@ -594,6 +587,16 @@ __device__ __forceinline__ uint32_t case_mask(const Item* it, const uint64_t* __
         if (rs >= x + 16) break;
         const int64_t a = rs > x ? rs : x, e = re < x + 16 ? re : x + 16;
         if (a < e) m |= ((1u << (e - a)) - 1) << (a - x);
+    }
+    return m;
+}
+__device__ __forceinline__ uint32_t case_mask(const Item* it, const uint64_t* __restrict__ low, int64_t wp) {
+    if (it->run_cnt > (uint32_t)RUN_CAP) return case_mask_global(it, low, wp);
+    uint32_t m = 0;
+    for (uint32_t r = 0; r < it->run_cnt; r++) {
+        const int64_t lo = it->runs[2 * r] > wp ? it->runs[2 * r] : wp;
+        const int64_t hi = it->runs[2 * r + 1] < wp + 16 ? it->runs[2 * r + 1] : wp + 16;
+        if (lo < hi) m |= ((1u << (hi - lo)) - 1) << (lo - wp);
     }
     return m;
 }
@@ -677,6 +680,10 @@ __device__ void emit(const Params& P, const Item* it, const Gather& gather, int 
         put16(P, it, g, ca, wpf, v, false);
     }
 }
+
+// a block served from the block cache: out of line (rare, and it would add a third copy of the store path to the
+// kernels' instruction cache footprint)
+__device__ __noinline__ void emit_cached(const Params& P, const Item* it, int lane) { emit(P, it, CacheGather{it->cptr}, lane, 32); }
 
 // A decoded item's output, op by op: for each op (warp-uniform, so no divergence between op kinds) the lanes write the
 // 16-byte output chunks that lie wholly inside the op's output bytes; then each chunk that holds a boundary (an op
@@ -1007,7 +1014,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constan
     }
     __syncwarp();
     if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
-    else if (it->state == ST_CACHED) emit(P, it, CacheGather{it->cptr}, lane, 32);
+    else if (it->state == ST_CACHED) emit_cached(P, it, lane);
     __syncthreads();
     uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
     for (int t = 0; t < WARPS; t++) {
@@ -1060,7 +1067,7 @@ __device__ void item_block_lane(const Params& P, Item* it) {
 
 constexpr int DEC_THREADS = 32;            // one warp per CTA: the few decode warps of a call spread over all SMs
 template <bool PK, bool CP>
-__global__ void __launch_bounds__(DEC_THREADS) pv_decode_kernel(const __grid_constant__ Params P, Item* plan) {
+__global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid_constant__ Params P, Item* plan) {
     const uint64_t i = (uint64_t)blockIdx.x * DEC_THREADS + threadIdx.x;
     if (i >= P.total) return;
     Item* it = plan + i;
@@ -1132,7 +1139,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
     }
     __syncwarp();
     if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
-    else if (it->state == ST_CACHED) emit(P, it, CacheGather{it->cptr}, lane, 32);
+    else if (it->state == ST_CACHED) emit_cached(P, it, lane);
     __syncthreads();
     uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
     for (int t = 0; t < WARPS; t++) {

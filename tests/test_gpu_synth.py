@@ -127,3 +127,28 @@ def test_sampler_graph_equals_sample(cfg0, cuda):
             else:
                 assert torch.equal(got, want)
         assert s.status() == 0
+
+
+def test_samplers_on_two_streams_after_a_larger_call(cfg0, cuda):
+    """Two captured samplers replayed concurrently on two streams, after a larger eager call, give what eager sample()
+    gives with identically seeded generators: every call has its own scratch (torch's allocator; a graph keeps the one
+    it was captured with), so neither concurrency nor a later, larger call can disturb a captured sampler."""
+    c, _, _ = cfg0
+    s1 = c.sampler(256, 8192, torch.Generator(device=cuda).manual_seed(11), reverse_complement=0.5, tokens=True)
+    s2 = c.sampler(256, 8192, torch.Generator(device=cuda).manual_seed(12), reverse_complement=0.5)
+    e1, e2 = torch.Generator(device=cuda).manual_seed(11), torch.Generator(device=cuda).manual_seed(12)
+    nb = c.info(0)["bases"]
+    big = c.windows(torch.zeros(4096, dtype=torch.int64), torch.arange(4096, dtype=torch.int64) * 100, 20000)
+    assert big.shape == (4096, 20000) and nb > 4096 * 100 + 20000
+    st1, st2 = torch.cuda.Stream(cuda), torch.cuda.Stream(cuda)
+    for _ in range(3):
+        st1.wait_stream(torch.cuda.current_stream(cuda))
+        st2.wait_stream(torch.cuda.current_stream(cuda))
+        with torch.cuda.stream(st1):
+            x1 = s1().clone()
+        with torch.cuda.stream(st2):
+            x2 = s2().clone()
+        torch.cuda.synchronize(cuda)
+        assert torch.equal(x1, c.sample(256, 8192, generator=e1, reverse_complement=0.5, tokens=True))
+        assert torch.equal(x2, c.sample(256, 8192, generator=e2, reverse_complement=0.5))
+    assert s1.status() == 0 and s2.status() == 0
