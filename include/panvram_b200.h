@@ -171,8 +171,9 @@ int pv_sha256_file_bases(const char* path, char hex[65]);
  * tokens), reverse-complemented where rc[i] != 0 (rc may be NULL), then mapped to tokens A/a 0 C/c 1 G/g 2 T/t 3
  * else 4 when tokens. asm, start: int64 [n] device; out: uint8 [n * W] device; status: int32 device word that the
  * call ORs PV_STATUS_* bits into (the caller zeroes it); work: device scratch of at least pv_windows_work_bytes()
- * bytes (the general path's block buffers). Launches on `stream` (a cudaStream_t), asynchronous. Same argument checks
- * as pv_cuda.cu:119-128: W in [0, 2^31), n >= 0. */
+ * bytes, 16-byte aligned (the split form's plan and the general path's block buffers; calls running at the same time
+ * need their own). Launches on `stream` (a cudaStream_t), asynchronous. Same argument checks as pv_cuda.cu:119-128:
+ * W in [0, 2^31), n >= 0. */
 int pv_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
                const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* work, size_t work_bytes,
                void* stream);

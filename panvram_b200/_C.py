@@ -257,7 +257,8 @@ def work_buffer(dev, device, n, W):
 
 def windows_cuda(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, out=None, status=None, flags=0, wstatus=None, ids=None,
                  work=None):
-    """out uint8 [n, W], status int32 [1] on the cohort's device: the one-kernel window decode (pv_windows_ex).
+    """out uint8 [n, W] (int64 [n, W] of ids when ids are given), status int32 [1] on the cohort's device: the window
+    decode (pv_windows_ex / pv_windows_ids).
     dev: the DevCohort of device pointers; wasm / wstart: int64 device tensors [n]; rc: None or a [n] bool/uint8 device
     tensor; wstatus: None or a zeroed uint8 device tensor of at least n bytes rounded up to 4 (per-window status).
     Asynchronous on torch's current stream of that device."""

@@ -1,7 +1,7 @@
 """panvram_b200.Cohort - the reference's public API (panvram/cohort.py:21-234) over the B200 decode path.
 
 A cohort of refrel3 v1 archives against one decoded reference, resident on one GPU; windows and coordinate slices are
-decoded on the card by the one-kernel window decode (include/panvram_b200.h pv_windows). Same methods, arguments,
+decoded on the card by the window kernels (include/panvram_b200.h pv_windows). Same methods, arguments,
 coordinates, errors and status text as the reference. Differences, by design:
   * GPU only: device="cpu" is refused (the reference's CPU decoder is this repository's test oracle, not a product
     path); fasta() decodes on the GPU and rebuilds / verifies the FASTA on the host.
