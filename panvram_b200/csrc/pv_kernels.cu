@@ -685,9 +685,9 @@ __device__ void emit(const Params& P, const Item* it, const Gather& gather, int 
 // kernels' instruction cache footprint)
 __device__ __noinline__ void emit_cached(const Params& P, const Item* it, int lane) { emit(P, it, CacheGather{it->cptr}, lane, 32); }
 
-// A decoded item's output, op by op: for each op (warp-uniform, so no divergence between op kinds) the lanes write the
-// 16-byte output chunks that lie wholly inside the op's output bytes; then each chunk that holds a boundary (an op
-// start, or an end of the item's range, off a 16-byte boundary) is assembled from every op it overlaps by one lane.
+// A decoded item's output: first every 16-byte output chunk that lies wholly inside one op (pass 1, chunk-major), then
+// each chunk that holds a boundary (an op start, or an end of the item's range, off a 16-byte boundary), assembled from
+// every op it overlaps by one lane (pass 2).
 __device__ void emit_ops(const Params& P, const Item* it, const RefView& R, int lane) {
     const OutRange g = out_range(P, it);
     const int64_t W = (int64_t)P.W;
@@ -695,17 +695,23 @@ __device__ void emit_ops(const Params& P, const Item* it, const RefView& R, int 
     const uint32_t lits_sm = smem_addr(it->lits);
     const int nops = it->nops;
     const int64_t ox0 = it->ox0, ox1 = it->ox1;
-    for (int k = 0; k < nops; k++) {
+    // pass 1, chunk-major: the 16-byte chunks wholly inside [A, B); lane i takes every 32nd, in the order of the block
+    // offsets they read (the output order reversed for a reverse-complemented window), with a cursor into the ops that
+    // only moves forward. A chunk inside one op is written here; one that holds an op boundary is left to pass 2.
+    const int64_t c0 = ((int64_t)g.A + 15) & ~(int64_t)15, c1 = (int64_t)g.B & ~(int64_t)15;
+    const int64_t nch = c1 > c0 ? (c1 - c0) >> 4 : 0;
+    int k = 0;
+    for (int64_t i = lane; i < nch; i += 32) {
+        const int64_t c = g.rcw ? c1 - 16 - 16 * i : c0 + 16 * i;
+        const int64_t wpf = g.rcw ? W - 16 - (c - base) : c - base;
+        const int64_t blo = wpf + g.delta;                  // block offset of the chunk's first forward byte
+        while (k < nops && (int64_t)op_dst(it->ops[k]) + it->ops[k].len <= blo) k++;
+        if (k >= nops) break;
         const Op o = it->ops[k];
-        const int64_t dst = op_dst(o), a = dst > ox0 ? dst : ox0, e = dst + o.len < ox1 ? dst + o.len : ox1;
-        const int64_t lo = base + (g.rcw ? W - (e - g.delta) : a - g.delta), hi = base + (g.rcw ? W - (a - g.delta) : e - g.delta);
-        const int64_t c1 = hi & ~(int64_t)15;
-        for (int64_t c = ((lo + 15) & ~(int64_t)15) + 16 * lane; c < c1; c += 16 * 32) {
-            const int64_t wpf = g.rcw ? W - 16 - (c - base) : c - base;
-            uint32_t v[4];
-            op_src16(it, R, lits_sm, o, wpf + g.delta, v);
-            put16(P, it, g, (uintptr_t)c, wpf, v, true);
-        }
+        if ((int64_t)op_dst(o) > blo || (int64_t)op_dst(o) + o.len < blo + 16) continue;
+        uint32_t v[4];
+        op_src16(it, R, lits_sm, o, blo, v);
+        put16(P, it, g, (uintptr_t)c, wpf, v, true);
     }
     const OpsGather gather{it, R, lits_sm};
     for (int k = lane; k <= nops; k += 32) {
