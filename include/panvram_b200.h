@@ -229,6 +229,63 @@ int pv_sample_coords(const int64_t* cum, const int64_t* valid, const int64_t* ct
 int pv_windows_noalloc(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
                        const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* stream);
 
+/* ---- device: the whole-assembly checks (Cohort.check_full / fasta, panvram/cohort.py:224-234, whose FASTA rebuild
+ * and XXH3 run on the host in the reference, pv_core.cpp:138-176) ---- */
+
+/* One FASTA record (contig) over a decoded base stream: at fasta_off, '>' + the header's hdr_len bytes (at hdr_off in
+ * the header blob) + '\n', then bases [boff, boff + len) of the stream in lines of line_width bases, each followed
+ * by '\n' (the layout pv_core_fasta_write writes). */
+typedef struct pv_fasta_rec {
+    uint64_t fasta_off, boff, len, hdr_off;
+    uint32_t hdr_len, line_width;
+} pv_fasta_rec;
+/* A FASTA file described over a device base stream (all pointers device). keys: XXH3's default secret as the device
+ * reads it (24 little-endian words, then the last stripe's 8 and the merge's 8 keys; pv_xxh3.h). */
+typedef struct pv_fasta_view {
+    const pv_fasta_rec* recs; const uint8_t* hdrs; const uint8_t* bases;
+    uint64_t nrec, nbases, fasta_len;
+    uint64_t keys[40];
+} pv_fasta_view;
+/* contrib[8 k + j] (device uint64 [8 nblk], 16-byte aligned) = word j of the sum of XXH3's accumulate steps over the
+ * FASTA's 1024-byte block blk0 + k, from zero accumulators: the data-parallel half of XXH3's long-input loop. Blocks
+ * must lie wholly inside the FASTA. Asynchronous on `stream`. */
+int pv_fasta_xxh3_blocks(const pv_fasta_view* view, uint64_t blk0, uint64_t nblk, uint64_t* contrib, void* stream);
+/* out[0 : p1 - p0] (device, 16-byte aligned) = FASTA bytes [p0, p1), p1 <= fasta_len. Asynchronous on `stream`. */
+int pv_fasta_bytes(const pv_fasta_view* view, uint64_t p0, uint64_t p1, uint8_t* out, void* stream);
+/* Per-block XXH3 of a decoded upper-case base stream (device, 16-byte aligned) against want[] (device uint64 [nb]):
+ * *first_bad (a device int64 the caller sets to INT64_MAX) is lowered to the first block that differs. Blocks of 240
+ * bases or fewer (only an assembly's last block can be one) are skipped: the caller checks those on the host. */
+int pv_block_xxh3_check(const uint8_t* bases, uint64_t nbases, uint32_t Q, const uint64_t* want, const uint64_t* keys40,
+                        int64_t* first_bad, void* stream);
+/* lower-case runs of assembly asm_index applied in place to its decoded stream on the device (pv_core_apply_case's
+ * device twin): the runs as the window kernel reads them from the uploaded cohort; max_runs >= the assembly's run
+ * count (pv_asm_info.lower_case_runs) sizes the launch. */
+int pv_apply_case_device(const pv_dev_cohort* cohort, int64_t asm_index, uint64_t max_runs, uint8_t* bases, uint64_t nbases,
+                         void* stream);
+
+/* assembly asm_index's FASTA layout (host arrays; with recs == NULL only the three sizes): records in file order,
+ * header bytes concatenated. A contig with bases and line width 0 is refused (PV_EFORMAT). */
+int pv_core_fasta_layout(const pv_core* c, int64_t asm_index, pv_fasta_rec* recs, uint64_t rec_cap, uint8_t* hdrs,
+                         uint64_t hdr_cap, uint64_t* nrec, uint64_t* hdr_bytes, uint64_t* fasta_len);
+/* the archive's per-block XXH3 values as read at open (a view into the core; NULL and 0 without flag bit 0) */
+int pv_core_block_hashes(const pv_core* c, int64_t asm_index, const uint64_t** hashes, uint64_t* n, uint32_t* Q);
+/* Host drivers of the above for assembly asm_index of a Core (they upload the record table, run the kernels on
+ * `stream` and wait for them). work: device scratch of pv_core_device_check_work_bytes() bytes, 16-byte aligned.
+ * pv_core_fasta_xxh3_device: XXH3 of the FASTA rebuilt from a decoded stream with case applied (bases: device), equal
+ * to pv_core_fasta_xxh3 of the same stream; the serial scramble chain runs on the host while the device forms the
+ * next chunk's block sums (chunk_blocks 1024-byte blocks per round trip, at most and by default (0) 65,536). pv_core_fasta_write_device: the FASTA bytes into out (device, 16-byte aligned; size
+ * query with out == NULL). pv_core_check_block_hashes_device: pv_core_check_block_hashes of a device stream. */
+size_t pv_core_device_check_work_bytes(const pv_core* c, int64_t asm_index);
+int pv_core_fasta_xxh3_device(const pv_core* c, int64_t asm_index, const uint8_t* bases, uint64_t nbases, uint64_t chunk_blocks,
+                              void* work, size_t work_bytes, void* stream, uint64_t* out_hash);
+int pv_core_fasta_write_device(const pv_core* c, int64_t asm_index, const uint8_t* bases, uint64_t nbases, uint8_t* out,
+                               uint64_t cap, void* work, size_t work_bytes, void* stream, uint64_t* size);
+int pv_core_check_block_hashes_device(const pv_core* c, int64_t asm_index, const uint8_t* upper_bases, uint64_t nbases,
+                                      void* work, size_t work_bytes, void* stream, int64_t* first_bad);
+/* XXH3_64bits of a host buffer longer than 240 bytes by the same block sums, scramble chain and finish that the
+ * device path splits (host only; it checks that restatement against the xxHash library) */
+int pv_xxh3_64_long_host(const void* data, uint64_t len, uint64_t* out_hash);
+
 /* at most how many kernel launches one pv_windows call with these sizes makes (0 for an empty call) */
 int pv_windows_launches(int64_t n, int64_t W);
 /* message of the calling thread's last pv_windows / pv_windows_ex argument or launch failure */

@@ -91,7 +91,13 @@ for _name, _res, _args in (
         ("pv_windows_noalloc", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _P, _P, _P]),
         ("pv_windows_ids", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, ctypes.POINTER(ctypes.c_int64), _P, _P, _P, _SZ, _P]),
         ("pv_sample_coords", _I32, [_P, _P, _P, _P, _P, _I64, _P, _P, ctypes.c_float, _I32, _I64, _P, _P, _P, _P, _P, _P]),
-        ("pv_windows_launches", _I32, [_I64, _I64])):
+        ("pv_windows_launches", _I32, [_I64, _I64]),
+        ("pv_core_device_check_work_bytes", _SZ, [_P, _I64]),
+        ("pv_core_fasta_xxh3_device", _I32, [_P, _I64, _P, _U64, _U64, _P, _SZ, _P, ctypes.POINTER(_U64)]),
+        ("pv_core_fasta_write_device", _I32, [_P, _I64, _P, _U64, _P, _U64, _P, _SZ, _P, ctypes.POINTER(_U64)]),
+        ("pv_core_check_block_hashes_device", _I32, [_P, _I64, _P, _U64, _P, _SZ, _P, ctypes.POINTER(_I64)]),
+        ("pv_apply_case_device", _I32, [ctypes.POINTER(DevCohort), _I64, _U64, _P, _U64, _P]),
+        ("pv_xxh3_64_long_host", _I32, [_P, _U64, ctypes.POINTER(_U64)])):
     _f = getattr(_lib, _name)
     _f.restype, _f.argtypes = _res, _args
 
@@ -227,6 +233,69 @@ class Core:
             raise FormatError("bases must be contiguous")
         _check(_lib.pv_core_apply_case(self._h, i, b.data_ptr(), b.numel()))
         return b
+
+    # ---- the same checks over a decoded stream in device memory (kernels on torch's current stream of its device)
+    @staticmethod
+    def _dev_u8(bases):
+        if not isinstance(bases, torch.Tensor) or bases.device.type != "cuda" or bases.dtype != torch.uint8 or not bases.is_contiguous():
+            raise FormatError("bases: contiguous uint8 CUDA tensor of the assembly's length")
+        return bases
+
+    def _dev_call(self, fn, i, b, *args):
+        work = torch.empty(max(16, _lib.pv_core_device_check_work_bytes(self._h, i)), dtype=torch.uint8, device=b.device)
+        code = fn(self._h, i, b.data_ptr(), b.numel(), *args[:-1], work.data_ptr(), work.numel(),
+                  torch.cuda.current_stream(b.device).cuda_stream, args[-1])
+        if code:
+            msg = (_lib.pv_kernels_last_error() or b"").decode(errors="replace")
+            raise (RuntimeError if code == PV_ECUDA else FormatError)(msg)
+
+    def fasta_xxh3_device(self, i, bases, chunk_blocks=0):
+        """fasta_xxh3 of a decoded stream (case applied) in device memory: the FASTA is read over the stream on the
+        device (nothing copied back but XXH3's per-block sums, chunk_blocks of them per round trip; 0: 65,536),
+        "%016x"."""
+        i, b = self._asm_check(i), self._dev_u8(bases)
+        h = _U64()
+        with torch.cuda.device(b.device):
+            self._dev_call(_lib.pv_core_fasta_xxh3_device, i, b, int(chunk_blocks), ctypes.byref(h))
+        return "%016x" % h.value
+
+    def fasta_device(self, i, bases):
+        """The FASTA file's bytes rebuilt on the device from a decoded stream (case applied) -> uint8 CUDA tensor."""
+        i, b = self._asm_check(i), self._dev_u8(bases)
+        sz = _U64()
+        _check(_lib.pv_core_fasta_write_device(self._h, i, None, b.numel(), None, 0, None, 0, None, ctypes.byref(sz)))
+        out = torch.empty(max(1, sz.value), dtype=torch.uint8, device=b.device)
+        with torch.cuda.device(b.device):
+            self._dev_call(_lib.pv_core_fasta_write_device, i, b, out.data_ptr(), out.numel(), ctypes.byref(sz))
+        return out[:sz.value]
+
+    def first_bad_block_device(self, i, upper_bases):
+        """first_bad_block of a decoded upper-case stream in device memory (per-block XXH3 on the device)."""
+        i, b = self._asm_check(i), self._dev_u8(upper_bases)
+        r = _I64()
+        with torch.cuda.device(b.device):
+            self._dev_call(_lib.pv_core_check_block_hashes_device, i, b, ctypes.byref(r))
+        return r.value
+
+
+def xxh3_64_long_host(data):
+    """XXH3_64bits of bytes longer than 240, by the block sums, scramble chain and finish the device path splits."""
+    b = bytes(data)
+    h = _U64()
+    buf = ctypes.create_string_buffer(b, len(b))
+    code = _lib.pv_xxh3_64_long_host(ctypes.cast(buf, ctypes.c_void_p), len(b), ctypes.byref(h))
+    if code:
+        raise ValueError((_lib.pv_kernels_last_error() or b"").decode())
+    return h.value
+
+
+def apply_case_device(dev, a, runs, bases):
+    """Lower-case runs of assembly a (as uploaded in the DevCohort dev) applied in place to its device stream."""
+    code = _lib.pv_apply_case_device(ctypes.byref(dev), int(a), int(runs), bases.data_ptr(), bases.numel(),
+                                     torch.cuda.current_stream(bases.device).cuda_stream)
+    if code:
+        raise RuntimeError("panvram_b200 apply_case: " + (_lib.pv_kernels_last_error() or b"").decode())
+    return bases
 
 
 def sha256_file_bases(path):

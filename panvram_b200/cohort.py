@@ -378,6 +378,23 @@ class Cohort:
             out[s:s + k].copy_(x[0], non_blocking=False)
         return out
 
+    def _decode_device(self, a, chunk, apply_case):
+        """Assembly a's whole base stream decoded into one uint8 CUDA tensor on the cohort's device (chunked
+        launches, one status word, one wait); raises on a failed block as windows(check=True) does."""
+        n = self._info[a]["bases"]
+        out = torch.empty(max(1, n), dtype=torch.uint8, device=self.device)[:n]
+        asm = torch.tensor([a], dtype=torch.int64)
+        with torch.cuda.device(self.device):
+            status = torch.zeros(1, dtype=torch.int32, device=self.device)
+            for s in range(0, n, chunk):
+                k = min(chunk, n - s)
+                self._launch(asm, torch.tensor([s], dtype=torch.int64), k, None, False, apply_case, out=out[s:s + k].view(1, k),
+                             status=status)
+            st = int(status.item())
+        if st:
+            raise RuntimeError(STATUS_TEXT.format(st))
+        return out
+
     def decode(self, assembly, chunk=1 << 28, out=None):
         """The whole base stream of an assembly (contigs concatenated, case as in the FASTA) decoded on the cohort's
         device in chunks of `chunk` bases -> uint8 [bases] on the host (pinned; `out` reused if given)."""
@@ -385,29 +402,30 @@ class Cohort:
 
     def check_full(self, assembly, out=None):
         """Full decode on the cohort's device, the FASTA rebuilt from it (layout from the contig table) hashed with
-        XXH3 -> (equal to the header's source XXH3, the hash "%016llx")."""
+        XXH3 -> (equal to the header's source XXH3, the hash "%016llx"). The stream stays on the device: the FASTA is
+        read over it there and only XXH3's per-block sums come back (`out`, the reference's host buffer for the stream,
+        is accepted and not needed)."""
         a = self._asm(assembly)
-        h = self._core.fasta_xxh3(a, self.decode(a, out=out))
+        h = self._core.fasta_xxh3_device(a, self._decode_device(a, 1 << 28, True))
         return h == self._info[a]["fasta_xxh3"], h
 
     def fasta(self, assembly, verify=True):
         """Full decode of an assembly -> the FASTA file's bytes. verify: every block XXH3 (if present) and the XXH3 of
-        the rebuilt FASTA against the header's (the source file's). Decoded on the GPU, rebuilt on the host."""
+        the rebuilt FASTA against the header's (the source file's). Decode, checks, case and FASTA layout run on the
+        cohort's device; the FASTA's bytes are copied back once."""
         a = self._asm(assembly)
         path = self._info[a]["path"]
         try:
-            b = self._decode(a, 1 << 28, None, False)
+            b = self._decode_device(a, 1 << 28, False)
         except RuntimeError:
             raise _C.FormatError(path + ": block decode failed")
-        if verify and self._core.first_bad_block(a, b) >= 0:
+        if verify and self._core.first_bad_block_device(a, b) >= 0:
             raise _C.FormatError(path + ": block XXH3 mismatch")
-        self._core.apply_case(a, b)
-        fa = self._core.fasta_bytes(a, b)
-        if verify:
-            import xxhash
-            if "%016x" % xxhash.xxh3_64_intdigest(fa) != self._info[a]["fasta_xxh3"]:
-                raise _C.FormatError(path + ": FASTA XXH3 differs from the header")
-        return fa
+        with torch.cuda.device(self.device):
+            _C.apply_case_device(self._devc, a, self._info[a]["lower_case_runs"], b)
+        if verify and self._core.fasta_xxh3_device(a, b) != self._info[a]["fasta_xxh3"]:
+            raise _C.FormatError(path + ": FASTA XXH3 differs from the header")
+        return self._core.fasta_device(a, b).cpu().numpy().tobytes()
 
 
 class Sampler:

@@ -589,6 +589,36 @@ int pv_core_fasta_write(const pv_core* c, int64_t i, const uint8_t* B, uint64_t 
     return PV_OK;
 }
 
+int pv_core_fasta_layout(const pv_core* c, int64_t i, pv_fasta_rec* recs, uint64_t rec_cap, uint8_t* hdrs, uint64_t hdr_cap,
+                         uint64_t* nrec, uint64_t* hdr_bytes, uint64_t* fasta_len) {
+    const Arc* X = arc_at(c, i);
+    if (!X) return PV_EARG;
+    uint64_t fo = 0, ho = 0;
+    for (auto& r : X->rec) {
+        if (r.len && !r.lw) return fail_with(PV_EFORMAT, X->path + ": contig with bases and line width 0");
+        if (recs && ho + r.hdr.size() <= hdr_cap && (uint64_t)(&r - X->rec.data()) < rec_cap) {
+            pv_fasta_rec& o = recs[&r - X->rec.data()];
+            o.fasta_off = fo; o.boff = r.boff; o.len = r.len; o.hdr_off = ho; o.hdr_len = (uint32_t)r.hdr.size(); o.line_width = r.lw;
+            memcpy(hdrs + ho, r.hdr.data(), r.hdr.size());
+        } else if (recs) {
+            return fail_with(PV_EARG, "FASTA layout: arrays too small");
+        }
+        fo += 2 + r.hdr.size() + r.len + (r.lw ? (r.len + r.lw - 1) / r.lw : 0);
+        ho += r.hdr.size();
+    }
+    *nrec = X->rec.size(); *hdr_bytes = ho; *fasta_len = fo;
+    return PV_OK;
+}
+
+int pv_core_block_hashes(const pv_core* c, int64_t i, const uint64_t** hashes, uint64_t* n, uint32_t* Q) {
+    const Arc* X = arc_at(c, i);
+    if (!X) return PV_EARG;
+    *hashes = X->hashes.empty() ? nullptr : X->hashes.data();
+    *n = X->hashes.size();
+    *Q = X->Q;
+    return PV_OK;
+}
+
 int pv_core_check_block_hashes(const pv_core* c, int64_t i, const uint8_t* B, uint64_t nbases, int64_t* first_bad) {
     const Arc* X = arc_at(c, i);
     if (!X) return PV_EARG;

@@ -1198,9 +1198,10 @@ __global__ void __launch_bounds__(COORD_WARPS * 32) pv_sample_coords_kernel(cons
     }
 }
 
-thread_local char g_cuda_err[256];
-
 }  // namespace
+
+namespace pvb { thread_local char g_cuda_err[256]; }   // pv_kernels_last_error (also set by pv_fasta.cu's launchers)
+using pvb::g_cuda_err;
 
 extern "C" {
 

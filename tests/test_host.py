@@ -196,3 +196,16 @@ def test_cohort_is_gpu_only(golden):
     shutil.copytree(golden["dirs"]["q4k"], d, dirs_exist_ok=True)
     with pytest.raises(FileNotFoundError, match="not in"):
         P.Cohort.open(d, device="cuda", reference=golden["ref"], assemblies=["nope"])
+
+
+def test_xxh3_restatement_equals_the_library():
+    """The XXH3 steps the device path splits (block sums from zero accumulators, the scramble chain, the partial block,
+    the last stripe, the merge; panvram_b200/csrc/pv_xxh3.h), run on the host, against the xxHash library at every
+    length class of the long-input path: block edges, stripe edges, one and many blocks."""
+    rng = np.random.default_rng(3)
+    lens = list(range(241, 1300)) + [2047, 2048, 2049, 3 * 1024, 3 * 1024 + 1, 16384, 16385, 1 << 20, (1 << 20) + 63]
+    for n in lens:
+        d = rng.integers(0, 256, n, dtype=np.uint8).tobytes()
+        assert _C.xxh3_64_long_host(d) == xxhash.xxh3_64_intdigest(d), n
+    with pytest.raises(ValueError):
+        _C.xxh3_64_long_host(b"x" * 240)
