@@ -186,10 +186,15 @@ size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W);
  * caller) receives the PV_STATUS_* bits of each window; the cohort's block cache is filled this way at open. */
 #define PV_WIN_BLOCK_PATH 1u
 /* The kernels a call runs: by default the one-kernel form (one warp per item decodes on one lane and emits) while the
- * call has fewer than 6,144 (window, block) items, else two launches (pv_decode_kernel: one item per lane;
- * pv_emit_kernel: one item per warp). PV_WIN_FUSED / PV_WIN_SPLIT force one form; the output is the same. */
+ * call has fewer than 6,144 (window, block) items, else two launches (pv_decode_kernel: one item per lane, as many
+ * per warp as keep about 3,072 decode warps busy, at most 32; pv_emit_kernel: one item per warp). PV_WIN_FUSED /
+ * PV_WIN_SPLIT force one form; the output is the same. */
 #define PV_WIN_FUSED 2u
 #define PV_WIN_SPLIT 4u
+/* the split form's decode warps: PV_WIN_DEC_LANES(k) runs k items per warp (one per lane, k in 1..32) instead of
+ * the size rule's choice; the output is the same */
+#define PV_WIN_DEC_LANES_SHIFT 8
+#define PV_WIN_DEC_LANES(k) ((uint32_t)(k) << PV_WIN_DEC_LANES_SHIFT)
 int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
                   const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, uint8_t* wstatus,
                   void* work, size_t work_bytes, void* stream);

@@ -307,6 +307,11 @@ def sha256_file_bases(path):
 PV_WIN_BLOCK_PATH = 1
 PV_WIN_FUSED = 2          # force the one-kernel form
 PV_WIN_SPLIT = 4          # force the decode + emission pair
+
+
+def PV_WIN_DEC_LANES(k):
+    """flag: the split form's decode kernel runs k items per warp (1..32) instead of its size rule's choice"""
+    return int(k) << 8
 PV_BLOCK_CACHED = 0xFFFFFE
 
 

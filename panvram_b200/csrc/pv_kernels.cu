@@ -18,11 +18,14 @@
 //   * items needing the general path (a self copy inside the window, or more ops / literals than a slot holds) are
 //     decoded again by the whole CTA into a Q-byte block buffer in the caller's scratch, ops executed in order, then
 //     emitted the same way.
-// The split form (larger calls): pv_decode_kernel decodes one item per lane (32 chains per warp, tables through L1)
-// into a plan in the caller's scratch, then pv_emit_kernel emits one item per warp as above.
+// The split form (larger calls): pv_decode_kernel decodes one item per lane (up to 32 chains per warp, as many as keep
+// about 3,072 decode warps in flight; tables through L1) into a plan in the caller's scratch, then pv_emit_kernel
+// emits one item per warp as above.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
+
+#include <algorithm>
 
 #include "pv_layout.h"
 
@@ -80,6 +83,7 @@ struct Params {
     int narrow;                    // windows shorter than a block: stage only the span under the output range
     int64_t* out64;                // token-id output (pv_windows_ids): int64 [n, W]; then `out` is unused
     int64_t ids[5];                // the ids of tokens 0..4
+    uint32_t dec_lanes;            // split form: items per decode warp (one per lane, lanes 0 .. dec_lanes - 1)
 };
 
 // status bits into the call's word and, when asked, into the window's byte (4-byte aligned, padded array)
@@ -1072,9 +1076,11 @@ __device__ void item_block_lane(const Params& P, Item* it) {
 }
 
 constexpr int DEC_THREADS = 32;            // one warp per CTA: the few decode warps of a call spread over all SMs
+constexpr uint64_t DEC_WARPS = 3072;       // decode warps a split call aims for (148 SMs x ~21)
 template <bool PK, bool CP>
 __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid_constant__ Params P, Item* plan) {
-    const uint64_t i = (uint64_t)blockIdx.x * DEC_THREADS + threadIdx.x;
+    if (threadIdx.x >= P.dec_lanes) return;
+    const uint64_t i = (uint64_t)blockIdx.x * P.dec_lanes + threadIdx.x;
     if (i >= P.total) return;
     Item* it = plan + i;
     if (!item_locate(P, i, it)) return;
@@ -1254,7 +1260,7 @@ template <bool PK, bool CP>
 static cudaError_t split_form(uint64_t total, uint64_t grid, size_t smem_e, cudaStream_t st, const Params& P, const Params& PE, Item* plan) {
     const cudaError_t e = smem_attr((const void*)pv_emit_kernel<PK>, 4 + (PK ? 1 : 0), smem_e);
     if (e != cudaSuccess) return e;
-    pv_decode_kernel<PK, CP><<<(unsigned)((total + DEC_THREADS - 1) / DEC_THREADS), DEC_THREADS, 0, st>>>(P, plan);
+    pv_decode_kernel<PK, CP><<<(unsigned)((total + P.dec_lanes - 1) / P.dec_lanes), DEC_THREADS, 0, st>>>(P, plan);
     pv_emit_kernel<PK><<<(unsigned)grid, CTA, smem_e, st>>>(PE, plan);
     return cudaGetLastError();
 }
@@ -1302,6 +1308,11 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     // the fused kernel while a call's items fit in about one wave of it (its warps then overlap their chains well);
     // the decode + emission pair beyond (32 chains per warp amortise the decode when there are many items)
     const bool fused = (flags & PV_WIN_FUSED) ? true : (flags & PV_WIN_SPLIT) ? false : P.total < SPLIT_MIN_ITEMS;
+    const uint32_t lanes = (flags >> PV_WIN_DEC_LANES_SHIFT) & 63u;
+    if (lanes > 32) { snprintf(g_cuda_err, sizeof g_cuda_err, "decode lanes per warp: 1 to 32"); return PV_EARG; }
+    // split form: items per decode warp so that a call runs about DEC_WARPS decode warps (~21 per SM): fewer chains per
+    // warp diverge less, and beyond that many warps the SMs' issue slots are full anyway (measured, 1.5 K-49 K items)
+    P.dec_lanes = lanes ? lanes : (uint32_t)std::min<uint64_t>(32, std::max<uint64_t>(1, (P.total + DEC_WARPS - 1) / DEC_WARPS));
     const uint64_t need = plan_bytes(P.total) + grid * Q;
     if (!work || work_bytes < need || ((uintptr_t)work & 15)) {
         snprintf(g_cuda_err, sizeof g_cuda_err, "work buffer: %llu bytes needed, 16-byte aligned", (unsigned long long)need);

@@ -60,3 +60,17 @@ def test_sample_coords_refuses_bad_arguments_without_launching():
     assert call(4, mode=1) == _C.PV_EARG                        # strand output missing
     assert b"NULL" in lib.pv_kernels_last_error()
     assert call(0, ptrs=False) == _C.PV_OK
+
+
+def test_windows_refuses_bad_decode_lanes_without_launching():
+    """pv_windows_ex checks its flags before any CUDA call: PV_WIN_DEC_LANES above 32 is refused (PV_EARG)."""
+    from panvram_b200 import _C
+    lib = _C._lib
+    dev = _C.DevCohort()
+    for f in ("ref", "payload", "blocks", "asms", "tabs", "low"):
+        setattr(dev, f, 16)
+    dev.Q, dev.nasm, dev.tab_max = 4096, 1, 1024
+    P = ctypes.c_void_p(16)
+    rc = lib.pv_windows_ex(ctypes.byref(dev), P, P, 8, 100, None, 0, 1, _C.PV_WIN_SPLIT | _C.PV_WIN_DEC_LANES(33), P, P, None,
+                           P, 1 << 30, None)
+    assert rc == _C.PV_EARG and b"lanes" in lib.pv_kernels_last_error()

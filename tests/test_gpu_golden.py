@@ -25,7 +25,8 @@ def _hashes(x):
     return np.array([xxhash.xxh3_64_intdigest(r.tobytes()) for r in x], dtype=np.uint64)
 
 
-@pytest.mark.parametrize("flags", [2, 3, 4, 5], ids=["fused", "fused-block-path", "split", "split-block-path"])
+@pytest.mark.parametrize("flags", [2, 3, 4, 5, 4 | (1 << 8), 4 | (5 << 8)],
+                         ids=["fused", "fused-block-path", "split", "split-block-path", "split-1-lane", "split-5-lanes"])
 def test_golden_windows(golden, cohorts, flags):
     win = golden["windows"]
     for (di, W, tok, case), rows in golden_cases(win).items():
