@@ -186,7 +186,7 @@ size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W);
  * caller) receives the PV_STATUS_* bits of each window; the cohort's block cache is filled this way at open. */
 #define PV_WIN_BLOCK_PATH 1u
 /* The kernels a call runs: by default the one-kernel form (one warp per item decodes on one lane and emits) while the
- * call has fewer than 6,144 (window, block) items, else two launches (pv_decode_kernel: one item per lane, as many
+ * call has fewer than 4,608 (window, block) items (3,072 at Q = 16,384; items = n x (ceil(W / Q) + 1)), else two launches (pv_decode_kernel: one item per lane, as many
  * per warp as keep about 3,072 decode warps busy, at most 32; pv_emit_kernel: one item per warp). PV_WIN_FUSED /
  * PV_WIN_SPLIT force one form; the output is the same. */
 #define PV_WIN_FUSED 2u

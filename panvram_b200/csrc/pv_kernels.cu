@@ -3,7 +3,7 @@
 // Replaces the reference's three-kernel path (pv_queue_kernel -> pv_case_kernel -> pv_rc_tok_kernel,
 // pv_cuda.cu:38-147) with kernels that write every output byte once. Work item = (window, one block it touches).
 //
-// The fused form, pv_windows_kernel (calls of fewer than 6,144 items), one item per warp, WARPS warps per CTA:
+// The fused form, pv_windows_kernel (calls of few items: split_min_items), one item per warp, WARPS warps per CTA:
 //   * lane 0 stages into the warp's shared slot, with TMA bulk copies completing on one mbarrier (bounded wait:
 //     status 4), the assembly's compact decode table (pv_layout.h), the block's rANS stream and the reference span the
 //     block's start diagonal covers (for windows shorter than a block, only the span under the output range, the rest
@@ -1222,7 +1222,10 @@ static uint64_t grid_of(uint32_t Q, int64_t n, int64_t W, uint64_t* total, uint6
 }
 
 // scratch: the plan (one Item per item, the split pipeline's decode results), then a Q-byte general-path buffer per CTA
-constexpr uint64_t SPLIT_MIN_ITEMS = 6144;
+// the fused kernel below this many items (n x blocks per window), the split form from it: where they cross, measured
+// on B200 with W = 8,192 (q4k: equal at 4,608 items, fused 20 % faster at 3,072; q16k: fused 22 % faster at 2,048,
+// split 6 % faster at 4,096; a q16k item decodes a 4x longer stream, so the split form pays off sooner)
+static uint64_t split_min_items(uint32_t Q) { return Q >= 16384 ? 3072 : 4608; }
 static uint64_t plan_bytes(uint64_t total) { return (total * sizeof(Item) + 255) & ~255ull; }
 size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W) {
     if (n <= 0 || W <= 0) return 0;
@@ -1305,9 +1308,9 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     if ((uint64_t)n > (1ull << 62) / (((uint64_t)W + Q - 1) / Q + 1)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
     const uint64_t grid = grid_of(Q, n, W, &P.total, &P.bpw);
     if (grid >= (1ull << 31)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
-    // the fused kernel while a call's items fit in about one wave of it (its warps then overlap their chains well);
-    // the decode + emission pair beyond (32 chains per warp amortise the decode when there are many items)
-    const bool fused = (flags & PV_WIN_FUSED) ? true : (flags & PV_WIN_SPLIT) ? false : P.total < SPLIT_MIN_ITEMS;
+    // the fused kernel for calls of few items (each warp's one chain then overlaps the others' well); the decode +
+    // emission pair beyond, where several chains per decode warp amortise the decode
+    const bool fused = (flags & PV_WIN_FUSED) ? true : (flags & PV_WIN_SPLIT) ? false : P.total < split_min_items(Q);
     const uint32_t lanes = (flags >> PV_WIN_DEC_LANES_SHIFT) & 63u;
     if (lanes > 32) { snprintf(g_cuda_err, sizeof g_cuda_err, "decode lanes per warp: 1 to 32"); return PV_EARG; }
     // split form: items per decode warp so that a call runs about DEC_WARPS decode warps (~21 per SM): fewer chains per
