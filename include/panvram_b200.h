@@ -293,6 +293,9 @@ int pv_xxh3_64_long_host(const void* data, uint64_t len, uint64_t* out_hash);
 
 /* at most how many kernel launches one pv_windows call with these sizes makes (0 for an empty call) */
 int pv_windows_launches(int64_t n, int64_t W);
+/* the form a pv_windows_ex call with these sizes and flags takes: *launches 1 (pv_windows_kernel) or 2
+ * (pv_decode_kernel + pv_emit_kernel; *dec_lanes items per decode warp), 0 for an empty call */
+int pv_windows_form(uint32_t Q, int64_t n, int64_t W, uint32_t flags, int* launches, uint32_t* dec_lanes);
 /* message of the calling thread's last pv_windows / pv_windows_ex argument or launch failure */
 const char* pv_kernels_last_error(void);
 

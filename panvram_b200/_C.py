@@ -92,6 +92,7 @@ for _name, _res, _args in (
         ("pv_windows_ids", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, ctypes.POINTER(ctypes.c_int64), _P, _P, _P, _SZ, _P]),
         ("pv_sample_coords", _I32, [_P, _P, _P, _P, _P, _I64, _P, _P, ctypes.c_float, _I32, _I64, _P, _P, _P, _P, _P, _P]),
         ("pv_windows_launches", _I32, [_I64, _I64]),
+        ("pv_windows_form", _I32, [_U32, _I64, _I64, _U32, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(_U32)]),
         ("pv_core_device_check_work_bytes", _SZ, [_P, _I64]),
         ("pv_core_fasta_xxh3_device", _I32, [_P, _I64, _P, _U64, _U64, _P, _SZ, _P, ctypes.POINTER(_U64)]),
         ("pv_core_fasta_write_device", _I32, [_P, _I64, _P, _U64, _P, _U64, _P, _SZ, _P, ctypes.POINTER(_U64)]),
@@ -395,3 +396,12 @@ def sample_coords(cum, valid, ctg, u, r, p, rc_mode, asm, start, rc=None, coords
 
 def launches_per_call(n, W):
     return int(_lib.pv_windows_launches(int(n), int(W)))
+
+
+def windows_form(Q, n, W, flags=0):
+    """(kernel launches, decode items per warp) of a window call with these sizes: (1, 0) the fused kernel, (2, k) the
+    split form with k items per decode warp, (0, 0) an empty call."""
+    L, k = ctypes.c_int(), _U32()
+    if _lib.pv_windows_form(int(Q), int(n), int(W), int(flags), ctypes.byref(L), ctypes.byref(k)):
+        raise ValueError((_lib.pv_kernels_last_error() or b"").decode())
+    return L.value, k.value

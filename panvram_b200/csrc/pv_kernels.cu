@@ -1226,6 +1226,14 @@ static uint64_t grid_of(uint32_t Q, int64_t n, int64_t W, uint64_t* total, uint6
 // on B200 with W = 8,192 (q4k: equal at 4,608 items, fused 20 % faster at 3,072; q16k: fused 22 % faster at 2,048,
 // split 6 % faster at 4,096; a q16k item decodes a 4x longer stream, so the split form pays off sooner)
 static uint64_t split_min_items(uint32_t Q) { return Q >= 16384 ? 3072 : 4608; }
+// the form a call of `total` items takes (true: fused) and, for the split form, its items per decode warp: enough that
+// the call runs about DEC_WARPS decode warps (~21 per SM; fewer chains per warp diverge less, and beyond that many
+// warps the SMs' issue slots are full anyway; measured, 1.5 K-49 K items), at most 32
+static bool form_of(uint32_t Q, uint64_t total, uint32_t flags, uint32_t* lanes) {
+    const uint32_t k = (flags >> PV_WIN_DEC_LANES_SHIFT) & 63u;
+    *lanes = k ? k : (uint32_t)std::min<uint64_t>(32, std::max<uint64_t>(1, (total + DEC_WARPS - 1) / DEC_WARPS));
+    return (flags & PV_WIN_FUSED) ? true : (flags & PV_WIN_SPLIT) ? false : total < split_min_items(Q);
+}
 static uint64_t plan_bytes(uint64_t total) { return (total * sizeof(Item) + 255) & ~255ull; }
 size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W) {
     if (n <= 0 || W <= 0) return 0;
@@ -1310,12 +1318,8 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     if (grid >= (1ull << 31)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
     // the fused kernel for calls of few items (each warp's one chain then overlaps the others' well); the decode +
     // emission pair beyond, where several chains per decode warp amortise the decode
-    const bool fused = (flags & PV_WIN_FUSED) ? true : (flags & PV_WIN_SPLIT) ? false : P.total < split_min_items(Q);
-    const uint32_t lanes = (flags >> PV_WIN_DEC_LANES_SHIFT) & 63u;
-    if (lanes > 32) { snprintf(g_cuda_err, sizeof g_cuda_err, "decode lanes per warp: 1 to 32"); return PV_EARG; }
-    // split form: items per decode warp so that a call runs about DEC_WARPS decode warps (~21 per SM): fewer chains per
-    // warp diverge less, and beyond that many warps the SMs' issue slots are full anyway (measured, 1.5 K-49 K items)
-    P.dec_lanes = lanes ? lanes : (uint32_t)std::min<uint64_t>(32, std::max<uint64_t>(1, (P.total + DEC_WARPS - 1) / DEC_WARPS));
+    if (((flags >> PV_WIN_DEC_LANES_SHIFT) & 63u) > 32) { snprintf(g_cuda_err, sizeof g_cuda_err, "decode lanes per warp: 1 to 32"); return PV_EARG; }
+    const bool fused = form_of(Q, P.total, flags, &P.dec_lanes);
     const uint64_t need = plan_bytes(P.total) + grid * Q;
     if (!work || work_bytes < need || ((uintptr_t)work & 15)) {
         snprintf(g_cuda_err, sizeof g_cuda_err, "work buffer: %llu bytes needed, 16-byte aligned", (unsigned long long)need);
@@ -1348,6 +1352,21 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
 }
 
 extern "C" {
+
+int pv_windows_form(uint32_t Q, int64_t n, int64_t W, uint32_t flags, int* launches, uint32_t* dec_lanes) {
+    *launches = 0; *dec_lanes = 0;
+    if (!(Q == 1024 || Q == 2048 || Q == 4096 || Q == 16384) || n < 0 || W < 0 || ((flags >> PV_WIN_DEC_LANES_SHIFT) & 63u) > 32) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_windows_form: arguments");
+        return PV_EARG;
+    }
+    if (n == 0 || W == 0) return PV_OK;
+    const uint64_t total = (uint64_t)n * (((uint64_t)W + Q - 1) / Q + 1);
+    uint32_t lanes;
+    const bool fused = form_of(Q, total, flags, &lanes);
+    *launches = fused ? 1 : 2;
+    *dec_lanes = fused ? 0 : lanes;
+    return PV_OK;
+}
 
 int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,
                   int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, uint8_t* wstatus, void* work,

@@ -74,3 +74,21 @@ def test_windows_refuses_bad_decode_lanes_without_launching():
     rc = lib.pv_windows_ex(ctypes.byref(dev), P, P, 8, 100, None, 0, 1, _C.PV_WIN_SPLIT | _C.PV_WIN_DEC_LANES(33), P, P, None,
                            P, 1 << 30, None)
     assert rc == _C.PV_EARG and b"lanes" in lib.pv_kernels_last_error()
+
+
+def test_windows_form_rule():
+    """pv_windows_form reports the launches a call takes without a GPU: the fused kernel for few items, the split form
+    beyond (4,608 items; 3,072 at Q = 16,384), with about 3,072 decode warps (at most 32 items per warp); flags pin it."""
+    from panvram_b200 import _C
+    assert _C.windows_form(4096, 1024, 8192) == (1, 0)              # config 1: 3,072 items
+    assert _C.windows_form(4096, 1536, 8192) == (2, 2)              # 4,608 items
+    assert _C.windows_form(16384, 1024, 8192) == (1, 0)             # 2,048 items
+    assert _C.windows_form(16384, 4096, 8192) == (2, 3)             # config 2: 8,192 items
+    assert _C.windows_form(4096, 131072, 512) == (2, 32)
+    assert _C.windows_form(4096, 1024, 8192, _C.PV_WIN_SPLIT) == (2, 1)
+    assert _C.windows_form(16384, 4096, 8192, _C.PV_WIN_FUSED) == (1, 0)
+    assert _C.windows_form(4096, 9999, 8192, _C.PV_WIN_SPLIT | _C.PV_WIN_DEC_LANES(7)) == (2, 7)
+    assert _C.windows_form(4096, 0, 8192) == (0, 0)
+    import pytest
+    with pytest.raises(ValueError):
+        _C.windows_form(3000, 10, 10)
