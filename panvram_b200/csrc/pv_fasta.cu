@@ -5,8 +5,9 @@
 //
 // Work per launch is HBM-bound byte work: each 1024-byte XXH3 block of the FASTA is one warp's (32 bytes a lane, so a
 // lane pair holds one 64-byte stripe); the warp's partial sums meet by shuffles. The FASTA's bytes are produced on the
-// fly from the record table: a lane seeks its first byte (a binary search over the records, one division into lines)
-// and then steps byte by byte through header, bases and line ends.
+// fly from the record table (a binary search over the records, one division into lines): inside a record's full lines
+// the warp reads the bases coalesced and regroups them through shared memory; at headers, record ends and short lines
+// each lane steps byte by byte through header, bases and line ends.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -116,15 +117,54 @@ __device__ __forceinline__ void lane_keys(const uint64_t* kw, int lane, uint64_t
     for (int j = 0; j < 4; j++) key[j] = kw[(lane >> 1) + 4 * (lane & 1) + j];    // secret word s + i
 }
 
+// One warp, the 1024 FASTA bytes [B, B + 1024) (B + 1024 <= fasta_len): lane l gets bytes [B + 32 l, B + 32 l + 32)
+// as 4 little-endian words. When the block lies inside full lines of one record's bases (the common case: records are
+// long, lines at least 32 wide) the warp steps through it coalesced - byte B + 32 j + l by lane l at step j, a line
+// end crossed at most once per step - and regroups the bytes through shared memory; otherwise each lane seeks and
+// steps on its own.
+__device__ __forceinline__ void fa_block1k(const pv_fasta_view& V, uint64_t B, uint8_t* stage, int lane, uint64_t w[4]) {
+    uint32_t lo = 0, hi = (uint32_t)V.nrec;              // the record holding B (warp-uniform)
+    while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (__ldg(&V.recs[mid].fasta_off) <= B) lo = mid; else hi = mid;
+    }
+    const pv_fasta_rec* R = V.recs + lo;
+    const uint64_t len = __ldg(&R->len), lw = __ldg(&R->line_width);
+    const uint64_t seq = __ldg(&R->fasta_off) + __ldg(&R->hdr_len) + 2;
+    const uint64_t last = lw && len ? seq + ((len + lw - 1) / lw - 1) * (lw + 1) : 0;   // where the last (maybe short) line starts
+    if (lw >= 32 && B >= seq && B + BLOCK <= last) {
+        const uint64_t q = B + lane - seq, line = q / (lw + 1);
+        uint32_t col = (uint32_t)(q - line * (lw + 1));
+        const uint32_t L = (uint32_t)lw;
+        const uint8_t* x = V.bases + __ldg(&R->boff) + line * lw + col;
+#pragma unroll 8
+        for (int j = 0; j < 32; j++) {
+            stage[32 * j + lane] = col == L ? (uint8_t)'\n' : __ldg(x);
+            const bool wrap = col + 32 > L;
+            col = wrap ? col + 32 - (L + 1) : col + 32;
+            x += wrap ? 31 : 32;
+        }
+        __syncwarp();
+        const ulonglong2 a = *(const ulonglong2*)(stage + 32 * lane), c = *(const ulonglong2*)(stage + 32 * lane + 16);
+        w[0] = a.x; w[1] = a.y; w[2] = c.x; w[3] = c.y;
+        __syncwarp();
+    } else {
+        fa_read32(V, B + 32 * lane, w);
+    }
+}
+
+constexpr int FA_WARPS = 8;      // warps per CTA of the FASTA kernels (256 threads), each with a 1 KB staging row
+
 __global__ void __launch_bounds__(256) pv_fasta_xxh3_kernel(const __grid_constant__ pv_fasta_view V, uint64_t blk0,
                                                             uint64_t nblk, uint64_t* contrib) {
-    const int lane = threadIdx.x & 31;
+    __shared__ __align__(16) uint8_t stage[FA_WARPS][BLOCK];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint64_t key[4];
     lane_keys(V.keys, lane, key);
-    const uint64_t nw = (uint64_t)gridDim.x * (blockDim.x >> 5);
-    for (uint64_t k = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); k < nblk; k += nw) {
+    const uint64_t nw = (uint64_t)gridDim.x * FA_WARPS;
+    for (uint64_t k = (uint64_t)blockIdx.x * FA_WARPS + warp; k < nblk; k += nw) {
         uint64_t w[4], p[4];
-        fa_read32(V, (blk0 + k) * BLOCK + 32 * lane, w);
+        fa_block1k(V, (blk0 + k) * BLOCK, stage[warp], lane, w);
         block_sums(w, key, true, p);
         if (lane < 2) {
             ulonglong2* o = (ulonglong2*)(contrib + 8 * k + 4 * lane);
@@ -134,21 +174,28 @@ __global__ void __launch_bounds__(256) pv_fasta_xxh3_kernel(const __grid_constan
     }
 }
 
+// FASTA bytes [p0, p1) into out: one warp per 1024 bytes (the last, partial kilobyte byte by byte)
 __global__ void __launch_bounds__(256) pv_fasta_bytes_kernel(const __grid_constant__ pv_fasta_view V, uint64_t p0, uint64_t p1,
                                                              uint8_t* out) {
-    const uint64_t nt = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t * 32 < p1 - p0; t += nt) {
-        const uint64_t p = p0 + 32 * t;
-        if (p + 32 <= p1) {
+    __shared__ __align__(16) uint8_t stage[FA_WARPS][BLOCK];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t nw = (uint64_t)gridDim.x * FA_WARPS, nk = (p1 - p0 + BLOCK - 1) / BLOCK;
+    for (uint64_t k = (uint64_t)blockIdx.x * FA_WARPS + warp; k < nk; k += nw) {
+        const uint64_t B = p0 + k * BLOCK;
+        if (B + BLOCK <= p1) {
             uint64_t w[4];
-            fa_read32(V, p, w);
-            ulonglong2* o = (ulonglong2*)(out + 32 * t);
+            fa_block1k(V, B, stage[warp], lane, w);
+            ulonglong2* o = (ulonglong2*)(out + k * BLOCK + 32 * lane);
             o[0] = make_ulonglong2(w[0], w[1]);
             o[1] = make_ulonglong2(w[2], w[3]);
         } else {
-            FaPos f;
-            fa_seek(V, f, p);
-            for (uint64_t q = p; q < p1; q++) out[q - p0] = (uint8_t)fa_next(V, f);
+            const uint64_t q0 = B + 32 * lane;
+            if (q0 < p1) {
+                FaPos f;
+                fa_seek(V, f, q0);
+                const uint64_t q1 = q0 + 32 < p1 ? q0 + 32 : p1;
+                for (uint64_t q = q0; q < q1; q++) out[q - p0] = (uint8_t)fa_next(V, f);
+            }
         }
     }
 }
@@ -355,7 +402,7 @@ int pv_fasta_bytes(const pv_fasta_view* v, uint64_t p0, uint64_t p1, uint8_t* ou
     if (!v || !out || ((uintptr_t)out & 15) || p0 > p1 || p1 > v->fasta_len) return fail(PV_EARG, "pv_fasta_bytes: arguments");
     if (p0 == p1) return PV_OK;
     if (v->nrec == 0 || v->nrec >= (1ull << 32)) return fail(PV_EARG, "pv_fasta_bytes: records");
-    pv_fasta_bytes_kernel<<<grid_for(((p1 - p0 + 31) / 32 + 31) / 32), 256, 0, (cudaStream_t)stream>>>(*v, p0, p1, out);
+    pv_fasta_bytes_kernel<<<grid_for((p1 - p0 + BLOCK - 1) / BLOCK), 256, 0, (cudaStream_t)stream>>>(*v, p0, p1, out);
     return launched("pv_fasta_bytes_kernel");
 }
 
