@@ -26,6 +26,7 @@
 #include <stdio.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "pv_layout.h"
 
@@ -946,14 +947,18 @@ __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
 }
 
 // the CTA decodes a heavy item into its shared block buffer, ops in order, then emits it. Out of line: it is rare, and
-// its code (a second decoder and an emission) would otherwise share the instruction cache with the common path.
-template <bool PK>
+// its code (a second decoder and an emission) would otherwise share the instruction cache with the common path. The
+// assembly's table: staged in the slot (fused kernel), or read through L1 (GT: the emission kernel, whose slots leave
+// the table out so that more of them fit)
+template <bool PK, bool GT>
 __device__ __noinline__ void heavy_item(const Params& P, uint8_t* slot, uint8_t* buf, Op* hops) {
     __shared__ int h_res, h_nops;
     __shared__ Dec<GlobalStream> h_dec;
     const Item* it = slot_item(slot);
     const pv_dev_cohort& C = P.C;
-    const SmemTab T{smem_addr(slot_tab(P, slot))};
+    using Tab = typename std::conditional<GT, GlobalTab, SmemTab>::type;
+    Tab T;
+    if constexpr (GT) T.b = C.tabs + it->tab_off; else T.b = smem_addr(slot_tab(P, slot));
     const RefView R = slot_ref<PK>(P, slot);
     if (threadIdx.x == 0) {
         const uint8_t* src = C.payload + it->poff;
@@ -1029,7 +1034,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constan
     uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
     for (int t = 0; t < WARPS; t++) {
         uint8_t* sl = (uint8_t*)smem_raw + (size_t)t * P.slot_bytes;
-        if (slot_item(sl)->state == ST_HEAVY) heavy_item<PK>(P, sl, buf, hops);
+        if (slot_item(sl)->state == ST_HEAVY) heavy_item<PK, false>(P, sl, buf, hops);
     }
 }
 
@@ -1124,15 +1129,13 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
     const int st0 = it->state;
     if (st0 == ST_OK || st0 == ST_HEAVY) {
         const pv_dev_cohort& C = P.C;
-        const bool heavy = st0 == ST_HEAVY;
         if (lane == 0) {
             // the span the emission reads: the start diagonal under the item's output range only (the decode has
             // finished; anything off it comes from global memory), so the slot holds min(W, Q) bases, not Q
             item_span(P, it, true, P.span_cap);
             const uint32_t span_tma = PK ? 0u : it->span_len;
             mbar_init(bar);
-            mbar_expect(bar, (heavy ? it->tab_bytes : 0u) + span_tma);
-            if (heavy) bulk_g2s(smem_addr(slot_tab(P, slot)), C.tabs + it->tab_off, it->tab_bytes, bar);
+            mbar_expect(bar, span_tma);
             if (span_tma) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + it->span_lo, span_tma, bar);
         }
         __syncwarp();
@@ -1156,7 +1159,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
     uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
     for (int t = 0; t < WARPS; t++) {
         uint8_t* sl = (uint8_t*)smem_raw + (size_t)t * P.slot_bytes;
-        if (slot_item(sl)->state == ST_HEAVY) heavy_item<PK>(P, sl, buf, hops);
+        if (slot_item(sl)->state == ST_HEAVY) heavy_item<PK, true>(P, sl, buf, hops);
     }
 }
 
@@ -1336,11 +1339,13 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     P.span_cap = (uint32_t)(((uint64_t)(P.narrow ? W : Q) + 2 * SPAN_MARGIN + 64 + 15) & ~15ull);
     P.slot_bytes = (uint32_t)sizeof(Item) + P.tab_area + P.pay_cap + P.span_cap;
     const size_t smem = (size_t)WARPS * P.slot_bytes;
-    // the emission kernel's slot: no stream, and a span of the output range's diagonal only (min(W, Q) + margins)
+    // the emission kernel's slot: no stream, no table (its general path reads it through L1), and a span of the output
+    // range's diagonal only (min(W, Q) + margins)
     Params PE = P;
     PE.pay_cap = 0;
+    PE.tab_area = 0;
     PE.span_cap = P.span_cap;
-    PE.slot_bytes = (uint32_t)sizeof(Item) + PE.tab_area + PE.span_cap;
+    PE.slot_bytes = (uint32_t)sizeof(Item) + PE.span_cap;
     const size_t smem_e = (size_t)WARPS * PE.slot_bytes;
     const int form = (cohort->packed ? 1 : 0) | (cohort->compact ? 2 : 0);
     const cudaError_t le = fused ? launch_fused(form, grid, smem, (cudaStream_t)stream, P)
