@@ -251,9 +251,9 @@ typedef struct pv_fasta_view {
     uint64_t nrec, nbases, fasta_len;
     uint64_t keys[40];
 } pv_fasta_view;
-/* contrib[8 k + j] (device uint64 [8 nblk], 16-byte aligned) = word j of the sum of XXH3's accumulate steps over the
- * FASTA's 1024-byte block blk0 + k, from zero accumulators: the data-parallel half of XXH3's long-input loop. Blocks
- * must lie wholly inside the FASTA. Asynchronous on `stream`. */
+/* contrib[j nblk + k] (device uint64 [8 nblk], 16-byte aligned) = word j of the sum of XXH3's accumulate steps over the
+ * FASTA's 1024-byte block blk0 + k, from zero accumulators: the data-parallel half of XXH3's long-input loop, lane-major
+ * (each accumulator's sums contiguous). Blocks must lie wholly inside the FASTA. Asynchronous on `stream`. */
 int pv_fasta_xxh3_blocks(const pv_fasta_view* view, uint64_t blk0, uint64_t nblk, uint64_t* contrib, void* stream);
 /* out[0 : p1 - p0] (device, 16-byte aligned) = FASTA bytes [p0, p1), p1 <= fasta_len. Asynchronous on `stream`. */
 int pv_fasta_bytes(const pv_fasta_view* view, uint64_t p0, uint64_t p1, uint8_t* out, void* stream);

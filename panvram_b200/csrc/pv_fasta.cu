@@ -12,6 +12,8 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <atomic>
+#include <thread>
 #include <vector>
 
 #include "panvram_b200.h"
@@ -166,10 +168,10 @@ __global__ void __launch_bounds__(256) pv_fasta_xxh3_kernel(const __grid_constan
         uint64_t w[4], p[4];
         fa_block1k(V, (blk0 + k) * BLOCK, stage[warp], lane, w);
         block_sums(w, key, true, p);
-        if (lane < 2) {
-            ulonglong2* o = (ulonglong2*)(contrib + 8 * k + 4 * lane);
-            o[0] = make_ulonglong2(p[0], p[1]);
-            o[1] = make_ulonglong2(p[2], p[3]);
+        if (lane < 4) {                          // lane-major: accumulator j's sums are contrib[j * nblk ...]
+            const int j0 = 4 * (lane & 1) + 2 * (lane >> 1);
+            contrib[(uint64_t)j0 * nblk + k] = p[2 * (lane >> 1)];
+            contrib[(uint64_t)(j0 + 1) * nblk + k] = p[2 * (lane >> 1) + 1];
         }
     }
 }
@@ -297,13 +299,24 @@ const Keys& xxh3_keys() {
 void keys40(const Keys& k, uint64_t out[40]) {
     memcpy(out, k.w, 24 * 8); memcpy(out + 24, k.last, 8 * 8); memcpy(out + 32, k.merge, 8 * 8);
 }
-// the serial chain over n block sums: acc = scramble(acc + sum) per block
+// the serial chain over n block sums: acc = scramble(acc + sum) per block (sums block-major, 8 per block)
 void scan_blocks(uint64_t acc[8], const uint64_t* sums, uint64_t n, const Keys& k) {
     uint64_t a[8];
     for (int i = 0; i < 8; i++) a[i] = acc[i];
     for (uint64_t b = 0; b < n; b++)
         for (int i = 0; i < 8; i++) a[i] = scramble(a[i] + sums[8 * b + i], k.w[16 + i]);
     for (int i = 0; i < 8; i++) acc[i] = a[i];
+}
+// the same for accumulators j0 .. j0 + 3 over lane-major sums (accumulator j's n sums at sums + j * n)
+void scan_lanes4(uint64_t acc[8], const uint64_t* sums, uint64_t n, int j0, const Keys& k) {
+    uint64_t a0 = acc[j0], a1 = acc[j0 + 1], a2 = acc[j0 + 2], a3 = acc[j0 + 3];
+    const uint64_t k0 = k.w[16 + j0], k1 = k.w[17 + j0], k2 = k.w[18 + j0], k3 = k.w[19 + j0];
+    const uint64_t *s0 = sums + (uint64_t)j0 * n, *s1 = s0 + n, *s2 = s1 + n, *s3 = s2 + n;
+    for (uint64_t b = 0; b < n; b++) {
+        a0 = scramble(a0 + s0[b], k0); a1 = scramble(a1 + s1[b], k1);
+        a2 = scramble(a2 + s2[b], k2); a3 = scramble(a3 + s3[b], k3);
+    }
+    acc[j0] = a0; acc[j0 + 1] = a1; acc[j0 + 2] = a2; acc[j0 + 3] = a3;
 }
 // after the full blocks: the partial block's stripes, the last stripe, the merge. tail = input bytes [t0, len).
 uint64_t finish(uint64_t acc[8], const uint8_t* tail, uint64_t t0, uint64_t len, const Keys& k) {
@@ -450,8 +463,9 @@ int pv_core_fasta_xxh3_device(const pv_core* c, int64_t i, const uint8_t* bases,
         *out_hash = XXH3_64bits(b, len);
         return PV_OK;
     }
-    // block sums on the device a chunk at a time, copied back into two pinned buffers; the host runs the scramble
-    // chain over chunk j - 1 while the device works on chunk j
+    // block sums on the device a chunk at a time, copied back into two pinned buffers; while the device works on chunk
+    // j, the host runs the scramble chain over chunk j - 1: accumulators 0-3 on this thread, 4-7 on a helper (the chain
+    // is bound by reading the sums and by each step's latency, so two threads take about half the time)
     const uint64_t nfull = (len - 1) / BLOCK, nch = (nfull + CH - 1) / CH;
     uint64_t acc[8];
     for (int j = 0; j < 8; j++) acc[j] = acc_init(j);
@@ -460,19 +474,42 @@ int pv_core_fasta_xxh3_device(const pv_core* c, int64_t i, const uint8_t* bases,
         PV_TRY(cuda_ok(cudaMallocHost(&pp.p, 2 * CH * 64), "pinned block sums"));
         for (auto& e : pp.ev) PV_TRY(cuda_ok(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event"));
     }
-    for (uint64_t j = 0; j <= nch; j++) {
-        if (j < nch) {
-            const uint64_t b0 = j * CH, nb = nfull - b0 < CH ? nfull - b0 : CH;
-            PV_TRY(pv_fasta_xxh3_blocks(&v, b0, nb, s.sums[j & 1], stream));
-            PV_TRY(cuda_ok(cudaMemcpyAsync(pp.p + (j & 1) * CH * 8, s.sums[j & 1], nb * 64, cudaMemcpyDeviceToHost, st), "block sums"));
-            PV_TRY(cuda_ok(cudaEventRecord(pp.ev[j & 1], st), "event"));
+    auto blocks_in = [&](uint64_t j) { const uint64_t b0 = j * CH; return nfull - b0 < CH ? nfull - b0 : CH; };
+    std::atomic<int64_t> issued{-1};               // the last chunk whose sums are on their way to the host
+    std::atomic<int64_t> helper_done{-1};          // the last chunk the helper has scanned
+    std::atomic<bool> stop{false};
+    std::atomic<int> helper_err{0};
+    std::thread helper([&] {
+        for (uint64_t j = 0; j < nch; j++) {
+            while ((int64_t)issued.load() < (int64_t)j && !stop.load()) std::this_thread::yield();
+            if (stop.load()) return;
+            if (cudaEventSynchronize(pp.ev[j & 1]) != cudaSuccess) { helper_err = 1; return; }
+            scan_lanes4(acc, pp.p + (j & 1) * CH * 8, blocks_in(j), 4, k);
+            helper_done = (int64_t)j;
         }
-        if (j > 0) {
-            const uint64_t b0 = (j - 1) * CH, nb = nfull - b0 < CH ? nfull - b0 : CH;
-            PV_TRY(cuda_ok(cudaEventSynchronize(pp.ev[(j - 1) & 1]), "block sums"));
-            scan_blocks(acc, pp.p + ((j - 1) & 1) * CH * 8, nb, k);
+    });
+    int rc = PV_OK;
+    for (uint64_t j = 0; j <= nch && rc == PV_OK; j++) {
+        if (j < nch) {
+            // buffer j & 1 held chunk j - 2: both threads must be done with it
+            while (j >= 2 && helper_done.load() < (int64_t)j - 2 && !helper_err.load()) std::this_thread::yield();
+            if (helper_err.load()) { rc = fail(PV_ECUDA, "block sums: event"); break; }
+            const uint64_t nb = blocks_in(j);
+            rc = pv_fasta_xxh3_blocks(&v, j * CH, nb, s.sums[j & 1], stream);
+            if (rc == PV_OK)
+                rc = cuda_ok(cudaMemcpyAsync(pp.p + (j & 1) * CH * 8, s.sums[j & 1], nb * 64, cudaMemcpyDeviceToHost, st), "block sums");
+            if (rc == PV_OK) rc = cuda_ok(cudaEventRecord(pp.ev[j & 1], st), "event");
+            if (rc == PV_OK) issued = (int64_t)j;
+        }
+        if (j > 0 && rc == PV_OK) {
+            rc = cuda_ok(cudaEventSynchronize(pp.ev[(j - 1) & 1]), "block sums");
+            if (rc == PV_OK) scan_lanes4(acc, pp.p + ((j - 1) & 1) * CH * 8, blocks_in(j - 1), 0, k);
         }
     }
+    if (rc != PV_OK) stop = true;
+    helper.join();
+    if (rc != PV_OK) return rc;
+    if (helper_err.load()) return fail(PV_ECUDA, "block sums: event");
     const uint64_t t0 = tail_start(len);
     uint8_t tail[TAIL_CAP];
     PV_TRY(pv_fasta_bytes(&v, t0, len, s.tail, stream));
