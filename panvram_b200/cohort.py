@@ -28,6 +28,18 @@ def _arch_ok(device):
         raise RuntimeError(f"panvram_b200 is built for sm_100a (B200); {torch.cuda.get_device_name(device)} is sm_{cap[0]}{cap[1]}")
 
 
+def _strand_mode(reverse_complement):
+    """sample()'s reverse_complement -> (mode, p): 0 none, 1 all, 2 each window with probability p"""
+    if reverse_complement is True:
+        return 1, 0.0
+    if reverse_complement is False or reverse_complement is None or reverse_complement == 0:
+        return 0, 0.0
+    p = float(reverse_complement)
+    if not 0 < p <= 1:
+        raise ValueError("reverse_complement: False, True or a probability")
+    return 2, p
+
+
 class Cohort:
     """Open with Cohort.open(dir, device=...). Coordinates are 0-based; a contig is its FASTA header up to the first
     space or tab, or its index in the assembly; an assembly is its name (archive file name without .<dataset>.rr3) or
@@ -283,11 +295,13 @@ class Cohort:
                 raise RuntimeError(STATUS_TEXT.format(s))
         return out
 
-    def _draw(self, n, W, generator, reverse_complement, tokens, return_coords, status=None):
+    def _draw(self, n, W, generator, reverse_complement, tokens, return_coords, status=None, rng=None):
         """The sample() sequence without the host check: (windows, coords or None, status tensor). The draws are the
         reference's (torch.randint over all valid starts, then torch.rand for the strand, on the generator's device);
         the arithmetic from the draws to the decode's coordinates is one kernel (pv_sample_coords). status: None (a
-        fresh word, zeroed by that kernel) or an int32 device word the decode ORs into."""
+        fresh word, zeroed by that kernel) or an int32 device word the decode ORs into. rng (int64 [3] on the cohort's
+        device: a generator's seed and offset, 0): the same draws made inside that kernel from rng, which it advances
+        as the two torch calls advance the generator (pv_sample_draw_coords)."""
         if W <= 0 or n < 0:
             raise ValueError("W must be positive, n non-negative")
         if W not in self._valid:
@@ -299,17 +313,12 @@ class Cohort:
             raise ValueError(f"no contig of {W} bases or more")
         gdev = generator.device if generator is not None else self.device
         dev = self.device
-        u = torch.randint(0, total, (n,), generator=generator, device=gdev, dtype=torch.int64).to(dev)
-        r, p, mode = None, 0.0, 0
-        if reverse_complement is True:
-            mode = 1
-        elif reverse_complement is False or reverse_complement is None or reverse_complement == 0:
-            mode = 0
-        else:
-            p = float(reverse_complement)
-            if not 0 < p <= 1:
-                raise ValueError("reverse_complement: False, True or a probability")
-            r, mode = torch.rand(n, generator=generator, device=gdev).to(dev), 2
+        mode, p = _strand_mode(reverse_complement)
+        u = r = None
+        if rng is None:
+            u = torch.randint(0, total, (n,), generator=generator, device=gdev, dtype=torch.int64).to(dev)
+            if mode == 2:
+                r = torch.rand(n, generator=generator, device=gdev).to(dev)
         with torch.cuda.device(dev):
             asm = torch.empty(n, dtype=torch.int64, device=dev)
             start = torch.empty(n, dtype=torch.int64, device=dev)
@@ -318,7 +327,10 @@ class Cohort:
             fresh = status is None
             if fresh:
                 status = torch.empty(1, dtype=torch.int32, device=dev)
-            _C.sample_coords(cum, v, self._ctg, u, r, p, mode, asm, start, rc, coords, status if fresh else None)
+            if rng is None:
+                _C.sample_coords(cum, v, self._ctg, u, r, p, mode, asm, start, rc, coords, status if fresh else None)
+            else:
+                _C.sample_draw_coords(cum, v, self._ctg, total, rng, p, mode, n, asm, start, rc, coords, status if fresh else None)
             x, status = self._launch(asm, start, W, rc, tokens, True, status=status)
         return x, coords, status
 
@@ -429,14 +441,20 @@ class Cohort:
 
 
 class Sampler:
-    """A captured sample() call (Cohort.sampler). The graph registers the generator's state, so replays advance the
-    same Philox stream successive eager sample() calls would."""
+    """A captured sample() call (Cohort.sampler): call k returns what the k-th eager sample() call with the same
+    generator would (windows, coordinates, status), and advances the generator as that call would. The graph makes the
+    draws itself (pv_sample_draw_coords: torch's randint / rand kernels restated in the coordinate kernel, from a device
+    copy of the generator's seed and offset that the graph advances), so a replay is two launches and needs no
+    generator bookkeeping on the device; if the generator is used or reseeded between calls, the next call reloads its
+    state."""
 
     def __init__(self, cohort, n, W, generator, reverse_complement, tokens, return_coords):
         if generator is None or generator.device.type != "cuda":
             raise ValueError("sampler: a CUDA torch.Generator on the cohort's device")
         self.cohort, self.n, self.W, self.return_coords = cohort, n, W, return_coords
+        self.generator = generator
         dev = cohort.device
+        mode, _ = _strand_mode(reverse_complement)
         args = (n, W, generator, reverse_complement, tokens, return_coords)
         with torch.cuda.device(dev):
             side = torch.cuda.Stream(dev)
@@ -447,18 +465,35 @@ class Sampler:
             torch.cuda.current_stream(dev).wait_stream(side)
             torch.cuda.synchronize(dev)
             generator.set_state(state)                           # the warm-up draws are not part of the stream
+            props = torch.cuda.get_device_properties(dev)
+            _, _, self._inc = _C.torch_draw_geometry(n, cohort._valid[W][2], mode, props.multi_processor_count,
+                                                     getattr(props, "max_threads_per_multi_processor", 2048))
+            self._rng = torch.zeros(3, dtype=torch.int64, device=dev)
+            self._seed = self._offset = None
+            self._load_rng()
             self.graph = torch.cuda.CUDAGraph()
-            self.graph.register_generator_state(generator)
             self._acc = torch.zeros(1, dtype=torch.int32, device=dev)
             events, cohort.kernel_events = cohort.kernel_events, None
             try:
                 with torch.cuda.graph(self.graph):
-                    self.x, self.coords, _ = cohort._draw(*args, status=self._acc)
+                    self.x, self.coords, _ = cohort._draw(*args, status=self._acc, rng=self._rng)
             finally:
                 cohort.kernel_events = events
 
+    def _load_rng(self):
+        """The generator's seed and offset into the graph's device copy, when they are not what it holds already."""
+        seed, off = self.generator.initial_seed(), self.generator.get_offset()
+        if (seed, off) != (self._seed, self._offset):
+            w = torch.tensor([seed - (1 << 64) if seed >= 1 << 63 else seed, off, 0], dtype=torch.int64)
+            self._rng.copy_(w)
+            self._seed, self._offset = seed, off
+
     def __call__(self):
-        self.graph.replay()
+        with torch.cuda.device(self.cohort.device):
+            self._load_rng()
+            self.graph.replay()
+        self._offset += self._inc
+        self.generator.set_offset(self._offset)
         return (self.x, self.coords) if self.return_coords else self.x
 
     def status(self):

@@ -22,10 +22,12 @@
 // about 3,072 decode warps in flight; tables through L1) into a plan in the caller's scratch, then pv_emit_kernel
 // emits one item per warp as above.
 #include <cuda_runtime.h>
+#include <curand_kernel.h>
 #include <stdint.h>
 #include <stdio.h>
 
 #include <algorithm>
+#include <utility>
 #include <type_traits>
 
 #include "pv_layout.h"
@@ -753,6 +755,13 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 }
 constexpr uint32_t WAIT_SPINS = 1u << 22;   // bounded wait on a bulk copy (milliseconds); then status 4
 
+// Programmatic dependent launch: the window kernels are launched so that their CTAs may be scheduled while the kernel
+// before them on the stream is still running; each waits here, before it reads anything that kernel wrote, until it
+// has completed and its memory is visible (a no-op when launched without the attribute). The kernels whose successors
+// can start early say so as soon as they start.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- items
 constexpr int WARPS = 4;                     // one item per warp
 // A warp's shared slot: its Item, then its assembly's decode table (tab_area bytes: the cohort's largest table), then
@@ -1010,6 +1019,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constan
     __shared__ __align__(8) uint64_t bars[WARPS];
     __shared__ Op hops[HOPS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
     uint8_t* slot = (uint8_t*)smem_raw + (size_t)warp * P.slot_bytes;
     Item* it = slot_item(slot);
     const uint64_t item = (uint64_t)blockIdx.x * WARPS + warp;
@@ -1084,6 +1094,8 @@ constexpr int DEC_THREADS = 32;            // one warp per CTA: the few decode w
 constexpr uint64_t DEC_WARPS = 3072;       // decode warps a split call aims for (148 SMs x ~21)
 template <bool PK, bool CP>
 __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid_constant__ Params P, Item* plan) {
+    pdl_trigger();                                  // the emission kernel's CTAs may be placed now; they wait for this grid
+    pdl_wait();
     if (threadIdx.x >= P.dec_lanes) return;
     const uint64_t i = (uint64_t)blockIdx.x * P.dec_lanes + threadIdx.x;
     if (i >= P.total) return;
@@ -1114,6 +1126,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
     __shared__ __align__(8) uint64_t bars[WARPS];
     __shared__ Op hops[HOPS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
     uint8_t* slot = (uint8_t*)smem_raw + (size_t)warp * P.slot_bytes;
     Item* it = slot_item(slot);
     const uint64_t item = (uint64_t)blockIdx.x * WARPS + warp;
@@ -1168,6 +1181,18 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
 // starts -> contig k = searchsorted(cum, u, right=True), pos = u - (cum[k] - v[k]), assembly and base-stream start,
 // strand from the rand() draw. One warp per window: a 32-way search (each level one load per lane and a ballot), so
 // 3 dependent loads cover 32,768 contigs.
+// sample()'s draws made in the coordinate kernel, as torch's CUDA kernels make them for torch.randint(0, total, (n,)) and
+// torch.rand(n) (ATen/native/cuda/DistributionTemplates.h: a grid-stride loop of `threads` threads, thread t's Philox
+// state curand_init(seed, t, offset); each curand4 call gives `unroll` values, element li taking value
+// (li mod threads x unroll) / threads of call li / (threads x unroll); randint keeps 64 bits (two words) per value for
+// a range of 2^28 or more and reduces them mod the range; rand maps curand_uniform's (0, 1] to [0, 1) by sending 1 to
+// 0). rng (device) holds the generator's seed and offset; the launch's last CTA advances the offset by what torch's two
+// calls would, so a captured graph replays the generator's stream call after call.
+struct TorchDraws {
+    pv_philox* rng;             // NULL: the draws come from u / r
+    uint64_t total, threads, inc_int, inc_all;
+    int64_t* u_out; float* r_out;   // the draws themselves (for tests), or NULL
+};
 struct CoordParams {
     const int64_t *cum, *v, *casm, *cboff, *clocal, *u;
     const float* r;
@@ -1177,33 +1202,84 @@ struct CoordParams {
     int64_t *asm_out, *start_out, *coords;
     uint8_t* rc_out;
     int32_t* status;
+    TorchDraws D;
 };
 constexpr int COORD_WARPS = 8;
 
+__device__ __noinline__ int64_t torch_randint(uint64_t seed, uint64_t off, uint64_t threads, uint64_t total, uint64_t li) {
+    const bool wide = total >= (1ull << 28);
+    const uint64_t per = threads * (wide ? 2 : 4), pass = li / per, rem = li - pass * per, ii = rem / threads;
+    curandStatePhilox4_32_10_t st;
+    curand_init(seed, rem - ii * threads, off, &st);
+    uint4 v = curand4(&st);
+    for (uint64_t k = 0; k < pass; k++) v = curand4(&st);
+    const uint64_t val = wide ? (ii == 0 ? ((uint64_t)v.x << 32 | v.y) : ((uint64_t)v.z << 32 | v.w))
+                              : (uint64_t)(ii == 0 ? v.x : ii == 1 ? v.y : ii == 2 ? v.z : v.w);
+    return (int64_t)(val % total);
+}
+__device__ __noinline__ float torch_rand(uint64_t seed, uint64_t off, uint64_t threads, uint64_t li) {
+    const uint64_t per = threads * 4, pass = li / per, rem = li - pass * per, ii = rem / threads;
+    curandStatePhilox4_32_10_t st;
+    curand_init(seed, rem - ii * threads, off, &st);
+    float4 f = curand_uniform4(&st);
+    for (uint64_t k = 0; k < pass; k++) f = curand_uniform4(&st);
+    const float x = ii == 0 ? f.x : ii == 1 ? f.y : ii == 2 ? f.z : f.w;
+    return x == 1.0f ? 0.0f : x;
+}
+
 __global__ void __launch_bounds__(COORD_WARPS * 32) pv_sample_coords_kernel(const CoordParams P) {
+    pdl_trigger();                                  // the window kernel's CTAs may be placed now; they wait for this grid
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t w = (int64_t)blockIdx.x * COORD_WARPS + (threadIdx.x >> 5);
     if (w == 0 && lane == 0 && P.status) *P.status = 0;
-    if (w >= P.n) return;
-    const int64_t u = P.u[w];
-    int64_t lo = 0, hi = P.nctg;                        // the answer (first k with cum[k] > u) lies in [lo, hi)
-    while (hi - lo > 1) {
-        const int64_t step = (hi - lo + 31) / 32;
-        const int64_t idx = lo + (int64_t)(lane + 1) * step - 1;   // lane 31's probe is at or past hi - 1
-        const bool above = idx >= hi - 1 || __ldg(P.cum + idx) > u;
-        const int f = __ffs(__ballot_sync(0xffffffffu, above)) - 1;
-        lo += (int64_t)f * step;
-        hi = min(hi, lo + step);
+    if (w < P.n) {                                      // (warp-uniform)
+        int64_t u = 0;
+        float r = 0.0f;
+        if (P.D.rng) {
+            if (lane == 0) {
+                const uint64_t seed = __ldcg(&P.D.rng->seed), off = __ldcg(&P.D.rng->offset);
+                u = torch_randint(seed, off, P.D.threads, P.D.total, (uint64_t)w);
+                if (P.rc_mode == 2) r = torch_rand(seed, off + P.D.inc_int, P.D.threads, (uint64_t)w);
+                if (P.D.u_out) P.D.u_out[w] = u;
+                if (P.D.r_out && P.rc_mode == 2) P.D.r_out[w] = r;
+            }
+            u = __shfl_sync(0xffffffffu, u, 0);
+        } else {
+            u = P.u[w];
+            if (P.rc_mode == 2 && lane == 0) r = P.r[w];
+        }
+        int64_t lo = 0, hi = P.nctg;                    // the answer (first k with cum[k] > u) lies in [lo, hi)
+        while (hi - lo > 1) {
+            const int64_t step = (hi - lo + 31) / 32;
+            const int64_t idx = lo + (int64_t)(lane + 1) * step - 1;   // lane 31's probe is at or past hi - 1
+            const bool above = idx >= hi - 1 || __ldg(P.cum + idx) > u;
+            const int f = __ffs(__ballot_sync(0xffffffffu, above)) - 1;
+            lo += (int64_t)f * step;
+            hi = min(hi, lo + step);
+        }
+        if (lane == 0) {
+            const int64_t k = lo, pos = u - (__ldg(P.cum + k) - __ldg(P.v + k)), a = __ldg(P.casm + k);
+            const uint8_t s = P.rc_mode == 1 ? 1 : P.rc_mode == 2 ? (uint8_t)(r < P.p) : 0;
+            P.asm_out[w] = a;
+            P.start_out[w] = __ldg(P.cboff + k) + pos;
+            if (P.rc_out) P.rc_out[w] = s;
+            if (P.coords) {
+                int64_t* c = P.coords + 4 * w;
+                c[0] = a; c[1] = __ldg(P.clocal + k); c[2] = pos; c[3] = s;
+            }
+        }
     }
-    if (lane != 0) return;
-    const int64_t k = lo, pos = u - (__ldg(P.cum + k) - __ldg(P.v + k)), a = __ldg(P.casm + k);
-    const uint8_t s = P.rc_mode == 1 ? 1 : P.rc_mode == 2 ? (uint8_t)(P.r[w] < P.p) : 0;
-    P.asm_out[w] = a;
-    P.start_out[w] = __ldg(P.cboff + k) + pos;
-    if (P.rc_out) P.rc_out[w] = s;
-    if (P.coords) {
-        int64_t* c = P.coords + 4 * w;
-        c[0] = a; c[1] = __ldg(P.clocal + k); c[2] = pos; c[3] = s;
+    if (P.D.rng) {                                      // every CTA has read the offset: the last one advances it
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            if (atomicAdd(&P.D.rng->arrived, 1u) == gridDim.x - 1) {
+                P.D.rng->offset += P.D.inc_all;
+                P.D.rng->arrived = 0;
+                __threadfence();
+            }
+        }
     }
 }
 
@@ -1252,6 +1328,18 @@ int pv_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int6
 
 }  // extern "C"
 
+// a launch with programmatic stream serialisation allowed (the kernel waits in pdl_wait for the one before it)
+template <typename... K, typename... A>
+static cudaError_t launch_pdl(void (*k)(K...), unsigned grid, unsigned block, size_t smem, cudaStream_t st, A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid); cfg.blockDim = dim3(block); cfg.dynamicSmemBytes = smem; cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at; cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
+}
+
 // kernel launches per resident form (packed reference / compact block table), each with its dynamic shared memory
 // attribute set once per device and size
 static cudaError_t smem_attr(const void* fn, int slot, size_t smem) {
@@ -1267,16 +1355,16 @@ template <bool PK, bool CP>
 static cudaError_t fused_form(uint64_t grid, size_t smem, cudaStream_t st, const Params& P) {
     const cudaError_t e = smem_attr((const void*)pv_windows_kernel<PK, CP>, (PK ? 1 : 0) | (CP ? 2 : 0), smem);
     if (e != cudaSuccess) return e;
-    pv_windows_kernel<PK, CP><<<(unsigned)grid, CTA, smem, st>>>(P);
-    return cudaGetLastError();
+    return launch_pdl(pv_windows_kernel<PK, CP>, (unsigned)grid, CTA, smem, st, P);
 }
 template <bool PK, bool CP>
 static cudaError_t split_form(uint64_t total, uint64_t grid, size_t smem_e, cudaStream_t st, const Params& P, const Params& PE, Item* plan) {
     const cudaError_t e = smem_attr((const void*)pv_emit_kernel<PK>, 4 + (PK ? 1 : 0), smem_e);
     if (e != cudaSuccess) return e;
-    pv_decode_kernel<PK, CP><<<(unsigned)((total + P.dec_lanes - 1) / P.dec_lanes), DEC_THREADS, 0, st>>>(P, plan);
-    pv_emit_kernel<PK><<<(unsigned)grid, CTA, smem_e, st>>>(PE, plan);
-    return cudaGetLastError();
+    const cudaError_t d = launch_pdl(pv_decode_kernel<PK, CP>, (unsigned)((total + P.dec_lanes - 1) / P.dec_lanes), DEC_THREADS, 0, st,
+                                     P, plan);
+    if (d != cudaSuccess) return d;
+    return launch_pdl(pv_emit_kernel<PK>, (unsigned)grid, CTA, smem_e, st, PE, (const Item*)plan);
 }
 static cudaError_t launch_fused(int form, uint64_t grid, size_t smem, cudaStream_t st, const Params& P) {
     switch (form) {
@@ -1400,11 +1488,55 @@ int pv_sample_coords(const int64_t* cum, const int64_t* valid, const int64_t* ct
         snprintf(g_cuda_err, sizeof g_cuda_err, "pv_sample_coords: a required pointer is NULL");
         return PV_EARG;
     }
-    CoordParams P{cum, valid, ctg_asm, ctg_boff, ctg_local, u, r, nctg, n, p, rc_mode, asm_index, start, coords, rc, status};
+    CoordParams P{cum, valid, ctg_asm, ctg_boff, ctg_local, u, r, nctg, n, p, rc_mode, asm_index, start, coords, rc, status, TorchDraws{}};
     const int64_t grid = n > 0 ? (n + COORD_WARPS - 1) / COORD_WARPS : 1;
-    pv_sample_coords_kernel<<<(unsigned)grid, COORD_WARPS * 32, 0, (cudaStream_t)stream>>>(P);
+    const cudaError_t le = launch_pdl(pv_sample_coords_kernel, (unsigned)grid, COORD_WARPS * 32, 0, (cudaStream_t)stream, P);
+    if (le != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(le)); return PV_ECUDA; }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
+    return PV_OK;
+}
+
+int pv_torch_draw_geometry(int64_t n, uint64_t total, int rc_mode, int sm_count, int threads_per_sm, uint64_t* threads,
+                           uint64_t* inc_int, uint64_t* inc_all) {
+    *threads = *inc_int = *inc_all = 0;
+    if (n < 0 || n >= (1ll << 31) || total == 0 || rc_mode < 0 || rc_mode > 2 || sm_count <= 0 || threads_per_sm < 256) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_torch_draw_geometry: arguments");
+        return PV_EARG;
+    }
+    if (n == 0) return PV_OK;                           // torch draws nothing and leaves the offset
+    const uint64_t grid = std::min<uint64_t>((uint64_t)sm_count * (uint64_t)(threads_per_sm / 256), ((uint64_t)n + 255) / 256);
+    *threads = 256 * grid;
+    const uint64_t un = total >= (1ull << 28) ? 2 : 4;
+    *inc_int = (((uint64_t)n - 1) / (*threads * un) + 1) * 4;
+    *inc_all = *inc_int + (rc_mode == 2 ? (((uint64_t)n - 1) / (*threads * 4) + 1) * 4 : 0);
+    return PV_OK;
+}
+
+int pv_sample_draw_coords(const int64_t* cum, const int64_t* valid, const int64_t* ctg_asm, const int64_t* ctg_boff,
+                          const int64_t* ctg_local, int64_t nctg, uint64_t total, pv_philox* rng, float p, int rc_mode, int64_t n,
+                          int64_t* asm_index, int64_t* start, uint8_t* rc, int64_t* coords, int32_t* status, int64_t* u_out,
+                          float* r_out, void* stream) {
+    if (n < 0 || n >= (1ll << 31) || nctg <= 0 || rc_mode < 0 || rc_mode > 2 || total == 0 || !rng) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_sample_draw_coords: n, contig count, rc_mode, total or rng");
+        return PV_EARG;
+    }
+    if (n > 0 && (!cum || !valid || !ctg_asm || !ctg_boff || !asm_index || !start || (rc_mode != 0 && !rc) || (coords && !ctg_local))) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_sample_draw_coords: a required pointer is NULL");
+        return PV_EARG;
+    }
+    int dev = 0, sms = 0, tps = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&tps, cudaDevAttrMaxThreadsPerMultiProcessor, dev) != cudaSuccess) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_sample_draw_coords: device attributes");
+        return PV_ECUDA;
+    }
+    TorchDraws D{rng, total, 0, 0, 0, u_out, r_out};
+    if (pv_torch_draw_geometry(n, total, rc_mode, sms, tps, &D.threads, &D.inc_int, &D.inc_all) != PV_OK) return PV_EARG;
+    CoordParams P{cum, valid, ctg_asm, ctg_boff, ctg_local, nullptr, nullptr, nctg, n, p, rc_mode, asm_index, start, coords, rc, status, D};
+    const int64_t grid = n > 0 ? (n + COORD_WARPS - 1) / COORD_WARPS : 1;
+    const cudaError_t le = launch_pdl(pv_sample_coords_kernel, (unsigned)grid, COORD_WARPS * 32, 0, (cudaStream_t)stream, P);
+    if (le != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(le)); return PV_ECUDA; }
     return PV_OK;
 }
 

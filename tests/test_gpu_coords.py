@@ -82,3 +82,34 @@ def test_coords_kernel_many_contigs(cuda):
         assert torch.equal(rc.to(torch.int64), strand)
         assert torch.equal(coords, torch.stack([ctg["ctg_asm"][k], ctg["ctg_local"][k], pos, strand], 1)), nctg
         assert bool((v[k] > 0).all()) and bool((pos >= 0).all()) and bool((pos < v[k]).all())
+
+
+@pytest.mark.parametrize("total", [1, 1000, (1 << 28) - 1, 1 << 28, 198_000_000_007])
+def test_in_kernel_draws_equal_torch(cohorts, total, cuda):
+    """pv_sample_draw_coords makes the draws torch.randint(0, total, (n,)) and torch.rand(n) make on a generator in the
+    same state, bit for bit, for both of randint's paths (range below / from 2^28), for n from 1 to beyond one pass of
+    torch's grid-stride loop (more than 2 x 303,104 elements on a 148-SM B200), after the generator has been used; and
+    it advances its copy of the offset exactly as those calls advance the generator."""
+    from panvram_b200 import _C
+    c = cohorts["q4k"]
+    cum = torch.tensor([total], dtype=torch.int64, device=cuda)            # one contig holding every start
+    ctg = {"ctg_asm": torch.zeros(1, dtype=torch.int64, device=cuda), "ctg_boff": torch.zeros(1, dtype=torch.int64, device=cuda),
+           "ctg_local": torch.zeros(1, dtype=torch.int64, device=cuda)}
+    for n in (1, 3, 256, 1023, 4096, 303_105, 700_001, 1_300_000):
+        g = torch.Generator(device=cuda).manual_seed(1000 + n)
+        torch.rand(17, generator=g, device=cuda)                              # a used generator: offset > 0
+        seed, off = g.initial_seed(), g.get_offset()
+        rng = torch.tensor([seed - (1 << 64) if seed >= 1 << 63 else seed, off, 0], dtype=torch.int64, device=cuda)
+        want_u = torch.randint(0, total, (n,), generator=g, device=cuda, dtype=torch.int64)
+        want_r = torch.rand(n, generator=g, device=cuda)
+        asm = torch.empty(n, dtype=torch.int64, device=cuda)
+        start = torch.empty(n, dtype=torch.int64, device=cuda)
+        rc = torch.empty(n, dtype=torch.uint8, device=cuda)
+        u = torch.empty(n, dtype=torch.int64, device=cuda)
+        r = torch.empty(n, dtype=torch.float32, device=cuda)
+        _C.sample_draw_coords(cum, cum, ctg, total, rng, 0.5, 2, n, asm, start, rc, u_out=u, r_out=r)
+        torch.cuda.synchronize(cuda)
+        assert torch.equal(u, want_u), (total, n)
+        assert torch.equal(r.view(torch.int32), want_r.view(torch.int32)), (total, n)
+        assert torch.equal(start, want_u) and torch.equal(rc, (want_r < 0.5).to(torch.uint8)), (total, n)
+        assert int(rng[1].item()) == g.get_offset() and int(rng[2].item()) == 0, (total, n)

@@ -112,20 +112,25 @@ def test_synth_cohort_parity(tmp_path_factory, oracle, cuda, Q):
 
 
 def test_sampler_graph_equals_sample(cfg0, cuda):
-    """Cohort.sampler (sample() captured as one CUDA graph) gives, call after call, exactly what eager sample() gives
-    with an identically seeded generator - windows, coordinates and status."""
+    """Cohort.sampler (sample() captured as one CUDA graph, its draws made in the coordinate kernel) gives, call after
+    call, exactly what eager sample() gives with an identically seeded generator - windows, coordinates and status -
+    and leaves the generator where eager calls leave it, also across a reseed between calls."""
     c, _, _ = cfg0
     for rcp, tok, coords in ((False, False, False), (0.5, True, True), (True, False, True)):
         g1 = torch.Generator(device=cuda).manual_seed(11)
         g2 = torch.Generator(device=cuda).manual_seed(11)
         s = c.sampler(256, 3000, g1, reverse_complement=rcp, tokens=tok, return_coords=coords)
-        for _ in range(4):
+        for k in range(6):
+            if k == 3:                                   # reseeded, then used elsewhere: the sampler follows
+                g1.manual_seed(77); g2.manual_seed(77)
+                torch.rand(5, generator=g1, device=cuda); torch.rand(5, generator=g2, device=cuda)
             got = s()
             want = c.sample(256, 3000, generator=g2, reverse_complement=rcp, tokens=tok, return_coords=coords)
             if coords:
                 assert torch.equal(got[0], want[0]) and torch.equal(got[1], want[1])
             else:
                 assert torch.equal(got, want)
+            assert g1.get_offset() == g2.get_offset()   # the generator advanced as the eager call advanced its twin
         assert s.status() == 0
 
 
