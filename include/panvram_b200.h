@@ -310,6 +310,22 @@ int pv_core_check_block_hashes_device(const pv_core* c, int64_t asm_index, const
  * device path splits (host only; it checks that restatement against the xxHash library) */
 int pv_xxh3_64_long_host(const void* data, uint64_t len, uint64_t* out_hash);
 
+/* Window coordinates that the caller holds in pinned host memory (asm_host, start_host int64 [n]; rc_host uint8 [n]
+ * or NULL; cudaHostAlloc'd), gathered into device arrays by a kernel that reads them through their mapped addresses,
+ * ordered on `stream` like a copy. Cohort.windows uses it for pinned host inputs in place of the reference's
+ * host-to-device copies (cohort.py:139-141, `.to(device)`): a copy engine busy with other transfers (the previous
+ * batch's windows going to the host) does not delay it. The host arrays must stay unchanged until the stream has
+ * passed this point. */
+int pv_coords_from_host(const int64_t* asm_host, const int64_t* start_host, const uint8_t* rc_host, int64_t n, int64_t* asm_index,
+                        int64_t* start, uint8_t* rc, void* stream);
+
+/* The int32 status word read back for Cohort.windows / sample(check=True) (cohort.py:153-156 reads it with
+ * status.item()): one thread stores it, after the work queued before it on `stream`, into host_word, which must be
+ * pinned host memory (cudaHostAlloc, mapped into the device's address space); the caller then waits for the stream
+ * and reads host_word. Unlike a device-to-host copy, this never waits behind other copies in flight (for example the
+ * previous batch's windows being copied to the host on another stream). */
+int pv_status_to_host(const int32_t* status, int32_t* host_word, void* stream);
+
 /* at most how many kernel launches one pv_windows call with these sizes makes (0 for an empty call) */
 int pv_windows_launches(int64_t n, int64_t W);
 /* the form a pv_windows_ex call with these sizes and flags takes: *launches 1 (pv_windows_kernel) or 2

@@ -92,6 +92,8 @@ for _name, _res, _args in (
         ("pv_windows_ids", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, ctypes.POINTER(ctypes.c_int64), _P, _P, _P, _SZ, _P]),
         ("pv_sample_coords", _I32, [_P, _P, _P, _P, _P, _I64, _P, _P, ctypes.c_float, _I32, _I64, _P, _P, _P, _P, _P, _P]),
         ("pv_windows_launches", _I32, [_I64, _I64]),
+        ("pv_status_to_host", _I32, [_P, _P, _P]),
+        ("pv_coords_from_host", _I32, [_P, _P, _P, _I64, _P, _P, _P, _P]),
         ("pv_windows_form", _I32, [_U32, _I64, _I64, _U32, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(_U32)]),
         ("pv_core_device_check_work_bytes", _SZ, [_P, _I64]),
         ("pv_core_fasta_xxh3_device", _I32, [_P, _I64, _P, _U64, _U64, _P, _SZ, _P, ctypes.POINTER(_U64)]),
@@ -418,6 +420,35 @@ def torch_draw_geometry(n, total, rc_mode, sm_count, threads_per_sm):
                                    ctypes.byref(b)):
         raise ValueError((_lib.pv_kernels_last_error() or b"").decode())
     return t.value, a.value, b.value
+
+
+def coords_from_host(asm, start, rc, device):
+    """Pinned host coordinates (int64 asm / start, uint8 rc or None) -> device tensors, gathered by a kernel through the
+    host arrays' mapped addresses (pv_coords_from_host) on the current stream; None if an array is not pinned."""
+    n = int(asm.numel())
+    a = torch.empty(n, dtype=torch.int64, device=device)
+    s = torch.empty(n, dtype=torch.int64, device=device)
+    r = torch.empty(n, dtype=torch.uint8, device=device) if rc is not None else None
+    code = _lib.pv_coords_from_host(asm.data_ptr(), start.data_ptr(), rc.data_ptr() if rc is not None else None, n, a.data_ptr(),
+                                    s.data_ptr(), r.data_ptr() if r is not None else None,
+                                    torch.cuda.current_stream(device).cuda_stream)
+    if code == PV_EARG:
+        return None
+    if code:
+        raise RuntimeError("panvram_b200 coordinates from host: " + (_lib.pv_kernels_last_error() or b"").decode())
+    return a, s, r
+
+
+def read_status(status):
+    """The int32 status word (a CUDA tensor) after the work queued before this call on the current stream, as an int:
+    stored by one device thread into a pinned host word (pv_status_to_host), then the stream waited for - so the read
+    never queues behind other device-to-host copies, as status.item() would."""
+    h = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    stream = torch.cuda.current_stream(status.device)
+    if _lib.pv_status_to_host(status.data_ptr(), h.data_ptr(), stream.cuda_stream):
+        raise RuntimeError("panvram_b200 status read: " + (_lib.pv_kernels_last_error() or b"").decode())
+    stream.synchronize()
+    return int(h[0])
 
 
 def launches_per_call(n, W):

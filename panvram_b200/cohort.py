@@ -28,6 +28,25 @@ def _arch_ok(device):
         raise RuntimeError(f"panvram_b200 is built for sm_100a (B200); {torch.cuda.get_device_name(device)} is sm_{cap[0]}{cap[1]}")
 
 
+def _pinned_coords(asm, start, rc, dev):
+    """Coordinates given as contiguous pinned host tensors (int64, and bool / uint8 strands) -> device tensors gathered
+    by one kernel through their mapped addresses (no copy engine: a device-to-host copy in flight, such as the previous
+    batch's windows, does not delay them); None for any other input."""
+    ts = (asm, start) + ((rc,) if rc is not None else ())
+    if not all(isinstance(t, torch.Tensor) and t.device.type == "cpu" and t.is_contiguous() for t in ts):
+        return None
+    if asm.dtype != torch.int64 or start.dtype != torch.int64 or asm.numel() != start.numel():
+        return None
+    if rc is not None:
+        if rc.dtype == torch.bool:
+            rc = rc.view(torch.uint8)
+        if rc.dtype != torch.uint8 or rc.numel() != asm.numel():
+            return None
+    if not all(t.is_pinned() for t in ts):
+        return None
+    return _C.coords_from_host(asm, start, rc, dev)
+
+
 def _strand_mode(reverse_complement):
     """sample()'s reverse_complement -> (mode, p): 0 none, 1 all, 2 each window with probability p"""
     if reverse_complement is True:
@@ -258,14 +277,18 @@ class Cohort:
         copied without a wait of their own."""
         dev = self.device
         with torch.cuda.device(dev):
-            asm = torch.as_tensor(asm).to(dev, torch.int64, non_blocking=synced).contiguous()
-            start = torch.as_tensor(start).to(dev, torch.int64, non_blocking=synced).contiguous()
-            rc = None
-            if reverse_complement is not None:
-                rc = torch.as_tensor(reverse_complement)
-                if rc.dtype == torch.bool:
-                    rc = rc.view(torch.uint8)                 # same bytes (0 / 1), no conversion kernel
-                rc = rc.to(dev, torch.uint8, non_blocking=synced).contiguous()
+            g = _pinned_coords(asm, start, reverse_complement, dev) if synced else None
+            if g is not None:
+                asm, start, rc = g
+            else:
+                asm = torch.as_tensor(asm).to(dev, torch.int64, non_blocking=synced).contiguous()
+                start = torch.as_tensor(start).to(dev, torch.int64, non_blocking=synced).contiguous()
+                rc = None
+                if reverse_complement is not None:
+                    rc = torch.as_tensor(reverse_complement)
+                    if rc.dtype == torch.bool:
+                        rc = rc.view(torch.uint8)                 # same bytes (0 / 1), no conversion kernel
+                    rc = rc.to(dev, torch.uint8, non_blocking=synced).contiguous()
             flags |= self.launch_flags
             if self.kernel_events is None:
                 return _C.windows_cuda(self._devc, asm, start, W, rc, tokens, apply_case, out=out, status=status, flags=flags, ids=ids)
@@ -290,7 +313,8 @@ class Cohort:
             raise ValueError("token_ids: five ids, for A C G T and anything else")
         out, status = self._launch(asm, start, int(W), reverse_complement, tokens or ids is not None, True, synced=bool(check), ids=ids)
         if check:
-            s = int(status.item())
+            with torch.cuda.device(self.device):
+                s = _C.read_status(status)
             if s:
                 raise RuntimeError(STATUS_TEXT.format(s))
         return out
@@ -342,7 +366,8 @@ class Cohort:
         reverse-complemented 0/1)."""
         x, coords, status = self._draw(int(n), int(W), generator, reverse_complement, tokens, return_coords)
         if check:
-            s = int(status.item())
+            with torch.cuda.device(self.device):
+                s = _C.read_status(status)
             if s:
                 raise RuntimeError(STATUS_TEXT.format(s))
         return (x, coords) if return_coords else x

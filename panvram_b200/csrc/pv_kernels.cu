@@ -1283,6 +1283,22 @@ __global__ void __launch_bounds__(COORD_WARPS * 32) pv_sample_coords_kernel(cons
     }
 }
 
+// window coordinates read from pinned host memory through its mapped address (pv_coords_from_host)
+__global__ void __launch_bounds__(256) pv_coords_from_host_kernel(const int64_t* a, const int64_t* s, const uint8_t* r, int64_t n,
+                                                                  int64_t* ad, int64_t* sd, uint8_t* rd) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        ad[i] = a[i];
+        sd[i] = s[i];
+        if (r) rd[i] = r[i];
+    }
+}
+// the status word stored into pinned host memory by one thread (pv_status_to_host): no copy engine involved
+__global__ void pv_status_to_host_kernel(const int32_t* s, int32_t* h) {
+    *(volatile int32_t*)h = *(const volatile int32_t*)s;
+    __threadfence_system();
+}
+
 }  // namespace
 
 namespace pvb { thread_local char g_cuda_err[256]; }   // pv_kernels_last_error (also set by pv_fasta.cu's launchers)
@@ -1293,6 +1309,42 @@ extern "C" {
 const char* pv_kernels_last_error(void) { return g_cuda_err; }
 
 int pv_windows_launches(int64_t n, int64_t W) { return (n > 0 && W > 0) ? 2 : 0; }   // (at most: 1 when fused)
+
+int pv_coords_from_host(const int64_t* asm_host, const int64_t* start_host, const uint8_t* rc_host, int64_t n, int64_t* asm_index,
+                        int64_t* start, uint8_t* rc, void* stream) {
+    if (n < 0 || (n > 0 && (!asm_host || !start_host || !asm_index || !start || (rc_host && !rc)))) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_coords_from_host: arguments");
+        return PV_EARG;
+    }
+    if (n == 0) return PV_OK;
+    const int64_t *a = nullptr, *s = nullptr;
+    const uint8_t* r = nullptr;
+    if (cudaHostGetDevicePointer((void**)&a, (void*)asm_host, 0) != cudaSuccess || !a ||
+        cudaHostGetDevicePointer((void**)&s, (void*)start_host, 0) != cudaSuccess || !s ||
+        (rc_host && (cudaHostGetDevicePointer((void**)&r, (void*)rc_host, 0) != cudaSuccess || !r))) {
+        cudaGetLastError();
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_coords_from_host: the host arrays must be pinned (cudaHostAlloc) memory");
+        return PV_EARG;
+    }
+    const int64_t grid = std::min<int64_t>((n + 255) / 256, 148 * 4);
+    pv_coords_from_host_kernel<<<(unsigned)grid, 256, 0, (cudaStream_t)stream>>>(a, s, r, n, asm_index, start, rc);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
+    return PV_OK;
+}
+
+int pv_status_to_host(const int32_t* status, int32_t* host_word, void* stream) {
+    int32_t* d = nullptr;
+    if (!status || !host_word || cudaHostGetDevicePointer((void**)&d, host_word, 0) != cudaSuccess || !d) {
+        cudaGetLastError();
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_status_to_host: the host word must be pinned (cudaHostAlloc) memory");
+        return PV_EARG;
+    }
+    pv_status_to_host_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(status, d);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
+    return PV_OK;
+}
 
 static uint64_t grid_of(uint32_t Q, int64_t n, int64_t W, uint64_t* total, uint64_t* bpw) {
     *bpw = ((uint64_t)W + Q - 1) / Q + 1;

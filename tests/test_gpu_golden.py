@@ -148,3 +148,20 @@ def test_corrupt_payload_parity(golden, oracle, tmp_path, cuda):
                 else:
                     assert st == 0 and np.array_equal(x[0].cpu().numpy(), want), (k, blk, flags)
     assert caught > 0
+
+
+def test_pinned_host_coordinates(golden, cohorts, cuda):
+    """Coordinates in pinned host memory (gathered by a kernel through their mapped addresses, pv_coords_from_host)
+    give exactly what the same coordinates on the device give, with and without strands, bool or uint8."""
+    c = cohorts["q4k"]
+    rng = np.random.default_rng(4)
+    nb = [c.info(i)["bases"] for i in range(len(NAMES))]
+    for n, W in ((1, 50), (777, 3000), (4096, 257)):
+        a = rng.integers(0, len(NAMES), n)
+        s = np.array([rng.integers(0, nb[k] - W + 1) for k in a])
+        rcb = rng.random(n) < 0.5
+        ah, sh = torch.from_numpy(a.astype(np.int64)).pin_memory(), torch.from_numpy(s.astype(np.int64)).pin_memory()
+        for rc in (None, torch.from_numpy(rcb).pin_memory(), torch.from_numpy(rcb.astype(np.uint8)).pin_memory()):
+            want = c.windows(ah.to(cuda), sh.to(cuda), W, None if rc is None else rc.to(cuda), tokens=True)
+            got = c.windows(ah, sh, W, rc, tokens=True)
+            assert torch.equal(got, want), (n, W, rc is None)
