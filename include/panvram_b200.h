@@ -223,15 +223,16 @@ int pv_sample_coords(const int64_t* cum, const int64_t* valid, const int64_t* ct
  * state (the same Philox states, element-to-thread mapping and transforms as torch's kernels for this device), then
  * the arithmetic of pv_sample_coords. rng (device): the generator's seed and Philox offset; the launch advances the
  * offset by what those two torch calls would (pv_torch_draw_geometry's inc_all), so replaying it call after call
- * follows the generator's stream. u_out / r_out (device, or NULL): the draws. All pointers device except as noted. */
+ * follows the generator's stream. With rng NULL the state is seed / offset (by value) and the caller advances its
+ * generator by inc_all itself. u_out / r_out (device, or NULL): the draws. All pointers device except as noted. */
 typedef struct pv_philox {
     uint64_t seed, offset;
     uint32_t arrived, pad;      /* launch bookkeeping: zero between launches */
 } pv_philox;
 int pv_sample_draw_coords(const int64_t* cum, const int64_t* valid, const int64_t* ctg_asm, const int64_t* ctg_boff,
-                          const int64_t* ctg_local, int64_t nctg, uint64_t total, pv_philox* rng, float p, int rc_mode, int64_t n,
-                          int64_t* asm_index, int64_t* start, uint8_t* rc, int64_t* coords, int32_t* status, int64_t* u_out,
-                          float* r_out, void* stream);
+                          const int64_t* ctg_local, int64_t nctg, uint64_t total, pv_philox* rng, uint64_t seed, uint64_t offset,
+                          float p, int rc_mode, int64_t n, int64_t* asm_index, int64_t* start, uint8_t* rc, int64_t* coords,
+                          int32_t* status, int64_t* u_out, float* r_out, void* stream);
 /* torch's launch for those draws on a device of sm_count SMs and threads_per_sm threads per SM (host, no GPU needed):
  * the grid's threads and the Philox offset the randint call consumes (inc_int) and both calls consume (inc_all) */
 int pv_torch_draw_geometry(int64_t n, uint64_t total, int rc_mode, int sm_count, int threads_per_sm, uint64_t* threads,

@@ -101,7 +101,8 @@ for _name, _res, _args in (
         ("pv_core_check_block_hashes_device", _I32, [_P, _I64, _P, _U64, _P, _SZ, _P, ctypes.POINTER(_I64)]),
         ("pv_apply_case_device", _I32, [ctypes.POINTER(DevCohort), _I64, _U64, _P, _U64, _P]),
         ("pv_xxh3_64_long_host", _I32, [_P, _U64, ctypes.POINTER(_U64)]),
-        ("pv_sample_draw_coords", _I32, [_P, _P, _P, _P, _P, _I64, _U64, _P, ctypes.c_float, _I32, _I64, _P, _P, _P, _P, _P, _P, _P, _P]),
+        ("pv_sample_draw_coords", _I32, [_P, _P, _P, _P, _P, _I64, _U64, _P, _U64, _U64, ctypes.c_float, _I32, _I64, _P, _P, _P, _P, _P, _P,
+                                         _P, _P]),
         ("pv_torch_draw_geometry", _I32, [_I64, _U64, _I32, _I32, _I32, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)])):
     _f = getattr(_lib, _name)
     _f.restype, _f.argtypes = _res, _args
@@ -399,16 +400,17 @@ def sample_coords(cum, valid, ctg, u, r, p, rc_mode, asm, start, rc=None, coords
 
 
 def sample_draw_coords(cum, valid, ctg, total, rng, p, rc_mode, n, asm, start, rc=None, coords=None, status=None, u_out=None,
-                       r_out=None):
+                       r_out=None, seed=0, offset=0):
     """sample_coords with the draws made in the same launch exactly as torch.randint(0, total, (n,)) and (rc_mode 2)
     torch.rand(n) would make them on a CUDA generator whose seed and Philox offset are in rng (int64 [3] on the device:
-    seed, offset, 0); the launch advances rng's offset as those calls advance the generator's. u_out / r_out: the
-    draws, when given. Asynchronous on torch's current stream of asm's device."""
+    seed, offset, 0; the launch advances rng's offset as those calls advance the generator's) or, with rng None, are
+    seed and offset (the caller advances its generator). u_out / r_out: the draws, when given. Asynchronous on torch's
+    current stream of asm's device."""
     ptr = lambda t: t.data_ptr() if t is not None else None
     code = _lib.pv_sample_draw_coords(cum.data_ptr(), valid.data_ptr(), ctg["ctg_asm"].data_ptr(), ctg["ctg_boff"].data_ptr(),
-                                      ctg["ctg_local"].data_ptr(), int(cum.numel()), int(total), rng.data_ptr(), float(p), int(rc_mode),
-                                      int(n), asm.data_ptr(), start.data_ptr(), ptr(rc), ptr(coords), ptr(status), ptr(u_out), ptr(r_out),
-                                      torch.cuda.current_stream(asm.device).cuda_stream)
+                                      ctg["ctg_local"].data_ptr(), int(cum.numel()), int(total), ptr(rng), int(seed) & ((1 << 64) - 1),
+                                      int(offset), float(p), int(rc_mode), int(n), asm.data_ptr(), start.data_ptr(), ptr(rc), ptr(coords),
+                                      ptr(status), ptr(u_out), ptr(r_out), torch.cuda.current_stream(asm.device).cuda_stream)
     if code:
         raise RuntimeError("panvram_b200 sample draws: " + (_lib.pv_kernels_last_error() or b"").decode())
 

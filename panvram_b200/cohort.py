@@ -91,6 +91,7 @@ class Cohort:
                                   groups=ptr("groups") if compact else None, btab=ptr("btab") if compact else None,
                                   bexc=ptr("bexc") if compact else None, packed=int(packed), compact=int(compact))
         self._valid = {}
+        self._incs = {}
         self._info = [core.info(i) for i in range(core.n)]
         # a list to collect (start, end) CUDA events around each window-kernel launch (measurement); None = off
         self.kernel_events = None
@@ -321,8 +322,10 @@ class Cohort:
 
     def _draw(self, n, W, generator, reverse_complement, tokens, return_coords, status=None, rng=None):
         """The sample() sequence without the host check: (windows, coords or None, status tensor). The draws are the
-        reference's (torch.randint over all valid starts, then torch.rand for the strand, on the generator's device);
-        the arithmetic from the draws to the decode's coordinates is one kernel (pv_sample_coords). status: None (a
+        reference's (torch.randint over all valid starts, then torch.rand for the strand, on the generator's device):
+        for a CUDA generator on the cohort's device, outside stream capture, made in the coordinate kernel exactly as
+        those torch calls make them (pv_sample_draw_coords; the generator then advanced as they advance it), else by
+        the torch calls; the arithmetic from the draws to the decode's coordinates is one kernel (pv_sample_coords). status: None (a
         fresh word, zeroed by that kernel) or an int32 device word the decode ORs into. rng (int64 [3] on the cohort's
         device: a generator's seed and offset, 0): the same draws made inside that kernel from rng, which it advances
         as the two torch calls advance the generator (pv_sample_draw_coords)."""
@@ -339,7 +342,12 @@ class Cohort:
         dev = self.device
         mode, p = _strand_mode(reverse_complement)
         u = r = None
-        if rng is None:
+        gen = None
+        if rng is None and gdev.type == "cuda" and (gdev.index or 0) == (dev.index or 0) and not torch.cuda.is_current_stream_capturing():
+            # outside stream capture the draws are made in the coordinate kernel, from the generator's seed and offset,
+            # exactly as torch.randint / torch.rand would make them; the generator is then advanced as they would
+            gen = generator if generator is not None else torch.cuda.default_generators[dev.index or 0]
+        elif rng is None:
             u = torch.randint(0, total, (n,), generator=generator, device=gdev, dtype=torch.int64).to(dev)
             if mode == 2:
                 r = torch.rand(n, generator=generator, device=gdev).to(dev)
@@ -351,12 +359,26 @@ class Cohort:
             fresh = status is None
             if fresh:
                 status = torch.empty(1, dtype=torch.int32, device=dev)
-            if rng is None:
+            if gen is not None:
+                seed, off = gen.initial_seed(), gen.get_offset()
+                _C.sample_draw_coords(cum, v, self._ctg, total, None, p, mode, n, asm, start, rc, coords, status if fresh else None,
+                                      seed=seed, offset=off)
+                gen.set_offset(off + self._draw_increment(n, total, mode))
+            elif rng is None:
                 _C.sample_coords(cum, v, self._ctg, u, r, p, mode, asm, start, rc, coords, status if fresh else None)
             else:
                 _C.sample_draw_coords(cum, v, self._ctg, total, rng, p, mode, n, asm, start, rc, coords, status if fresh else None)
             x, status = self._launch(asm, start, W, rc, tokens, True, status=status)
         return x, coords, status
+
+    def _draw_increment(self, n, total, mode):
+        """the Philox offset torch's randint (and, mode 2, rand) for sample() consume on this device"""
+        key = (n, total, mode)
+        if key not in self._incs:
+            pr = torch.cuda.get_device_properties(self.device)
+            self._incs[key] = _C.torch_draw_geometry(n, total, mode, pr.multi_processor_count,
+                                                     getattr(pr, "max_threads_per_multi_processor", 2048))[2]
+        return self._incs[key]
 
     def sample(self, n, W, generator=None, reverse_complement=False, tokens=False, return_coords=False, check=True):
         """n windows of W bases, uniform over every (assembly, contig, start) with start + W <= contig length (a

@@ -1189,9 +1189,11 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
 // 0). rng (device) holds the generator's seed and offset; the launch's last CTA advances the offset by what torch's two
 // calls would, so a captured graph replays the generator's stream call after call.
 struct TorchDraws {
-    pv_philox* rng;             // NULL: the draws come from u / r
+    pv_philox* rng;             // the generator state on the device (advanced by the launch), or NULL
     uint64_t total, threads, inc_int, inc_all;
     int64_t* u_out; float* r_out;   // the draws themselves (for tests), or NULL
+    uint64_t seed, offset;      // the generator state as arguments (rng NULL, draw 1)
+    int draw;                   // make the draws (else they come from u / r)
 };
 struct CoordParams {
     const int64_t *cum, *v, *casm, *cboff, *clocal, *u;
@@ -1236,9 +1238,9 @@ __global__ void __launch_bounds__(COORD_WARPS * 32) pv_sample_coords_kernel(cons
     if (w < P.n) {                                      // (warp-uniform)
         int64_t u = 0;
         float r = 0.0f;
-        if (P.D.rng) {
+        if (P.D.draw) {
             if (lane == 0) {
-                const uint64_t seed = __ldcg(&P.D.rng->seed), off = __ldcg(&P.D.rng->offset);
+                const uint64_t seed = P.D.rng ? __ldcg(&P.D.rng->seed) : P.D.seed, off = P.D.rng ? __ldcg(&P.D.rng->offset) : P.D.offset;
                 u = torch_randint(seed, off, P.D.threads, P.D.total, (uint64_t)w);
                 if (P.rc_mode == 2) r = torch_rand(seed, off + P.D.inc_int, P.D.threads, (uint64_t)w);
                 if (P.D.u_out) P.D.u_out[w] = u;
@@ -1541,6 +1543,7 @@ int pv_sample_coords(const int64_t* cum, const int64_t* valid, const int64_t* ct
         return PV_EARG;
     }
     CoordParams P{cum, valid, ctg_asm, ctg_boff, ctg_local, u, r, nctg, n, p, rc_mode, asm_index, start, coords, rc, status, TorchDraws{}};
+    P.D.draw = 0;
     const int64_t grid = n > 0 ? (n + COORD_WARPS - 1) / COORD_WARPS : 1;
     const cudaError_t le = launch_pdl(pv_sample_coords_kernel, (unsigned)grid, COORD_WARPS * 32, 0, (cudaStream_t)stream, P);
     if (le != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(le)); return PV_ECUDA; }
@@ -1566,10 +1569,10 @@ int pv_torch_draw_geometry(int64_t n, uint64_t total, int rc_mode, int sm_count,
 }
 
 int pv_sample_draw_coords(const int64_t* cum, const int64_t* valid, const int64_t* ctg_asm, const int64_t* ctg_boff,
-                          const int64_t* ctg_local, int64_t nctg, uint64_t total, pv_philox* rng, float p, int rc_mode, int64_t n,
-                          int64_t* asm_index, int64_t* start, uint8_t* rc, int64_t* coords, int32_t* status, int64_t* u_out,
-                          float* r_out, void* stream) {
-    if (n < 0 || n >= (1ll << 31) || nctg <= 0 || rc_mode < 0 || rc_mode > 2 || total == 0 || !rng) {
+                          const int64_t* ctg_local, int64_t nctg, uint64_t total, pv_philox* rng, uint64_t seed, uint64_t offset,
+                          float p, int rc_mode, int64_t n, int64_t* asm_index, int64_t* start, uint8_t* rc, int64_t* coords,
+                          int32_t* status, int64_t* u_out, float* r_out, void* stream) {
+    if (n < 0 || n >= (1ll << 31) || nctg <= 0 || rc_mode < 0 || rc_mode > 2 || total == 0) {
         snprintf(g_cuda_err, sizeof g_cuda_err, "pv_sample_draw_coords: n, contig count, rc_mode, total or rng");
         return PV_EARG;
     }
@@ -1583,7 +1586,7 @@ int pv_sample_draw_coords(const int64_t* cum, const int64_t* valid, const int64_
         snprintf(g_cuda_err, sizeof g_cuda_err, "pv_sample_draw_coords: device attributes");
         return PV_ECUDA;
     }
-    TorchDraws D{rng, total, 0, 0, 0, u_out, r_out};
+    TorchDraws D{rng, total, 0, 0, 0, u_out, r_out, seed, offset, 1};
     if (pv_torch_draw_geometry(n, total, rc_mode, sms, tps, &D.threads, &D.inc_int, &D.inc_all) != PV_OK) return PV_EARG;
     CoordParams P{cum, valid, ctg_asm, ctg_boff, ctg_local, nullptr, nullptr, nctg, n, p, rc_mode, asm_index, start, coords, rc, status, D};
     const int64_t grid = n > 0 ? (n + COORD_WARPS - 1) / COORD_WARPS : 1;

@@ -49,6 +49,36 @@ def test_sample_coords_equal_reference_arithmetic(cohorts, ds, cuda):
         assert x.shape == (n, W)
 
 
+def test_sample_default_generator_and_user_capture(cohorts, cuda):
+    """Eager sample() makes its draws in the coordinate kernel from the generator's state: with the default CUDA
+    generator too (the same coordinates as the reference's torch calls, the generator left where they leave it). Inside
+    a CUDA graph a caller captures, sample() keeps torch's own draw calls, so each replay draws anew as torch's
+    graph-safe generator does: replays equal successive eager calls."""
+    c = cohorts["q4k"]
+    torch.cuda.manual_seed(123)
+    _, co = c.sample(300, 1000, reverse_complement=0.5, return_coords=True)
+    st = torch.cuda.get_rng_state(cuda)
+    torch.cuda.manual_seed(123)
+    want = _reference_coords(c._ctg, 1000, 300, None, 0.5, cuda)
+    assert torch.equal(co, want) and torch.equal(st, torch.cuda.get_rng_state(cuda))
+    g = torch.Generator(device=cuda).manual_seed(9)
+    e = torch.Generator(device=cuda).manual_seed(9)
+    side = torch.cuda.Stream(cuda)
+    side.wait_stream(torch.cuda.current_stream(cuda))
+    with torch.cuda.stream(side):
+        c.sample(64, 3000, generator=torch.Generator(device=cuda).manual_seed(1), check=False)      # warm-up off the graph
+    torch.cuda.current_stream(cuda).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    graph.register_generator_state(g)
+    with torch.cuda.graph(graph):
+        x, co = c.sample(64, 3000, generator=g, reverse_complement=0.5, return_coords=True, check=False)
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize(cuda)
+        wx, wco = c.sample(64, 3000, generator=e, reverse_complement=0.5, return_coords=True)
+        assert torch.equal(co, wco) and torch.equal(x, wx)
+
+
 def test_coords_kernel_many_contigs(cuda):
     """The 32-way search at several levels: 40,000 contigs (about a fifth shorter than W, so runs of equal prefix
     sums), draws including both ends of the range, against torch.searchsorted(right=True)."""
