@@ -92,3 +92,18 @@ def test_windows_form_rule():
     import pytest
     with pytest.raises(ValueError):
         _C.windows_form(3000, 10, 10)
+
+
+def test_torch_draw_geometry_without_gpu():
+    """pv_torch_draw_geometry restates torch's launch for sample()'s draws (256-thread blocks, at most SMs x 8 of them;
+    each thread's curand4 call gives 2 values for randint ranges of 2^28 or more, else 4, and 4 for rand; the Philox
+    offset advances 4 per call a thread makes): known cases on a 148-SM, 2,048-thread-per-SM device."""
+    from panvram_b200 import _C
+    import pytest
+    assert _C.torch_draw_geometry(1024, 198_000_000_000, 2, 148, 2048) == (1024, 4, 8)
+    assert _C.torch_draw_geometry(1024, 1000, 0, 148, 2048) == (1024, 4, 4)
+    assert _C.torch_draw_geometry(700_000, 1 << 40, 2, 148, 2048) == (303_104, 8, 12)        # randint: 2 passes
+    assert _C.torch_draw_geometry(1_300_000, 1000, 2, 148, 2048) == (303_104, 8, 16)         # both: 2 passes
+    assert _C.torch_draw_geometry(0, 5, 2, 148, 2048) == (0, 0, 0)                           # no draws, no advance
+    with pytest.raises(ValueError):
+        _C.torch_draw_geometry(10, 0, 0, 148, 2048)
