@@ -1,6 +1,6 @@
 """Regenerate the golden fixtures of tests/golden/ from the reference checkout (run where the reference is present):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <the reference checkout>]
 
 What it writes, all produced by the reference itself:
   data/{synthA,synthB}.{q1k,q4k,q16k}.rr3  the reference's own test archives (its tests/data), unchanged bytes
