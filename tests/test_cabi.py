@@ -107,3 +107,22 @@ def test_torch_draw_geometry_without_gpu():
     assert _C.torch_draw_geometry(0, 5, 2, 148, 2048) == (0, 0, 0)                           # no draws, no advance
     with pytest.raises(ValueError):
         _C.torch_draw_geometry(10, 0, 0, 148, 2048)
+
+
+def test_new_entry_points_refuse_bad_arguments_without_launching():
+    """The host-coordinate gather and the status read accept only pinned host memory, and the in-kernel draws check
+    their sizes, all before any launch: ordinary (pageable) host memory, a zero range or a negative count are refused
+    with PV_EARG and a message."""
+    import numpy as np
+    from panvram_b200 import _C
+    lib = _C._lib
+    a = np.zeros(8, dtype=np.int64)
+    s = np.zeros(8, dtype=np.int64)
+    P = ctypes.c_void_p(16)
+    assert lib.pv_coords_from_host(a.ctypes.data, s.ctypes.data, None, 8, P, P, None, None) == _C.PV_EARG
+    assert b"pinned" in lib.pv_kernels_last_error()
+    assert lib.pv_coords_from_host(None, None, None, 0, None, None, None, None) == _C.PV_OK          # nothing to do
+    w = np.zeros(1, dtype=np.int32)
+    assert lib.pv_status_to_host(P, w.ctypes.data, None) == _C.PV_EARG
+    for n, total in ((-1, 10), (4, 0)):
+        assert lib.pv_sample_draw_coords(P, P, P, P, P, 1, total, None, 0, 0, 0.5, 2, n, P, P, P, None, None, None, None, None) == _C.PV_EARG
