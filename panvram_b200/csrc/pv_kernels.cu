@@ -11,9 +11,10 @@
 //     reports status 1 exactly as the reference does) with the decoder state in registers, keeping only the ops and
 //     literal bytes that land inside the window. Each block's serial rANS chain runs in its own warp, so the chains'
 //     latencies overlap across warps.
-//   * the warp then writes the item's output range op by op in 16-byte vector stores (reference copies realigned with
-//     funnel shifts, reverse-complement copies byte-reversed, literals from the item's array), then lower-case runs,
-//     reverse complement and the token map (or the fused token-id map) in registers.
+//   * the warp then writes the item's output range in 16-byte vector stores, chunks inside one op first (lane i
+//     every 32nd chunk; reference copies realigned with funnel shifts, reverse-complement copies byte-reversed,
+//     literals from the item's array), then the chunks around op boundaries, one lane each; lower-case runs, reverse
+//     complement and the token map (or the fused token-id map) are applied in registers before each store.
 //   * blocks in the cohort's block cache (decoded once at open) are copied from it like a reference span.
 //   * items needing the general path (a self copy inside the window, or more ops / literals than a slot holds) are
 //     decoded again by the whole CTA into a Q-byte block buffer in the caller's scratch, ops executed in order, then
@@ -21,6 +22,10 @@
 // The split form (larger calls): pv_decode_kernel decodes one item per lane (up to 32 chains per warp, as many as keep
 // about 3,072 decode warps in flight; tables through L1) into a plan in the caller's scratch, then pv_emit_kernel
 // emits one item per warp as above.
+// Also here: pv_sample_coords_kernel, sample()'s coordinate arithmetic and (pv_sample_draw_coords) the draws torch's
+// randint / rand would make, restated on curand's Philox states; small kernels that move window coordinates from and
+// the status word to pinned host memory without a copy engine. The window kernels are launched with programmatic
+// dependent launch and wait for their predecessor in griddepcontrol.wait.
 #include <cuda_runtime.h>
 #include <curand_kernel.h>
 #include <stdint.h>
