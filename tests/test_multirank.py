@@ -59,3 +59,23 @@ def test_two_cpu_ranks(tmp_path):
     assert rate0 == rate1 == 2 * 1024 * 10 / 1.5
     # the global batch: every rank's rows, in rank order, on every rank
     assert g0 == g1 == ([1, 1, 1, 2, 2, 2], [0, 4, 8, 100, 104, 108])
+
+
+def test_bench_parity_helpers():
+    """bench.py's parity record: coordinates (assembly, contig index, start in the contig, strand) -> base-stream starts
+    through the contig table, and mismatching rows counted against the CPU decoder's output."""
+    import numpy as np
+    import bench
+    ctg = {"ctg_asm": np.array([0, 0, 1, 1, 1], np.int64), "ctg_boff": np.array([0, 100, 0, 50, 90], np.int64)}
+    co = np.array([[0, 1, 7, 1], [1, 2, 3, 0], [1, 0, 0, 1]], np.int64)
+    a, s, r = bench.coords_to_stream(ctg, co)
+    assert a.tolist() == [0, 1, 1] and s.tolist() == [107, 93, 0] and r.tolist() == [1, 0, 1]
+
+    def fn(asm, start, W, rc, tokens, verify=False):
+        assert verify
+        return np.stack([np.full(W, x % 256, np.uint8) for x in start])
+    good = fn(a, s, 4, r, False, True)
+    bad = good.copy()
+    bad[1, 2] ^= 1
+    par = bench.parity_check(fn, "reference", [(good, a, s, r), (bad, a, s, r)], 4, False)
+    assert par["windows"] == 6 and par["mismatches"] == 1 and par["first_mismatch"] == {"asm": 1, "start": 93}
