@@ -66,6 +66,24 @@ typedef struct pv_blk_group {
     uint32_t cache_base;   /* cache slot of the first of them; the next ones follow in block order */
 } pv_blk_group;
 
+/* Decoder checkpoint (32 bytes): the refrel3 decoder's whole state at an event boundary inside a block (the top of the
+ * event loop of refrel3.h:119-159), so that a decode can start there instead of at the block's start. The checkpoint
+ * index of a cohort holds, per block, Q / S of them (S = 1 << pv_dev_cohort.ckpt_shift, the stride): checkpoint j is
+ * the state at the last event boundary at or before block offset j S (checkpoint 0 is the block's start). Built on
+ * the device at open by pv_index_build, which decodes every block once and so also validates it: a block that fails
+ * to decode has PV_CKPT_BAD in all its checkpoints, and a window touching it reports PV_STATUS_DECODE as the
+ * reference's decode of that block would. The diagonal cache entries are stored as c + PV_CKPT_BIAS in 39 bits. */
+typedef struct pv_ckpt {
+    uint32_t xs;          /* rANS state (24 bits) | previous kind + 1 << 24 (3 bits) | diagonal count - 1 << 27 (2 bits) */
+    uint32_t p;           /* stream bytes consumed (from the block stream's first byte) */
+    uint32_t clo[4];      /* diagonal k (most recent first): bits 0..31 of c + PV_CKPT_BIAS */
+    uint8_t chi[4];       /* bits 32..38 of c + PV_CKPT_BIAS | strand << 7 */
+    uint16_t o;           /* block offset of the event boundary */
+    uint16_t flags;       /* PV_CKPT_BAD */
+} pv_ckpt;
+#define PV_CKPT_BIAS (1ll << 20)
+#define PV_CKPT_BAD 1u
+
 /* The pooled cohort as the window kernel reads it (device addresses). Built on the host by pv_core_pools() and
  * uploaded by the caller; it replaces the reference's pooled tensors P, pay_base, off, st, tab, blk_base, nbases,
  * low_s, low_l, low_base, low_cnt, ref (pv_core.cpp:65-90) that windows_cuda takes (pv_cuda.cu:153-162). */
@@ -92,6 +110,11 @@ typedef struct pv_dev_cohort {
     const uint32_t* btab;        /* per pooled block: length | code << 16 */
     const int64_t* bexc;         /* exception states, in block order */
     uint32_t packed, compact;
+    /* checkpoint index (pv_index_build), or NULL: then every window item decodes its block from the block's start to
+     * its end, validating it as it goes */
+    const pv_ckpt* ckpt;         /* [pooled blocks << (log2 Q - ckpt_shift)] */
+    uint32_t ckpt_shift;         /* log2 of the stride S (8 <= ckpt_shift <= log2 Q) */
+    uint32_t pad2;
 } pv_dev_cohort;
 
 /* Block table word 0 of a block served from pv_dev_cohort.cache: cache slot | PV_BLOCK_CACHED << 40 (the payload
@@ -254,6 +277,16 @@ int pv_torch_draw_geometry(int64_t n, uint64_t total, int rc_mode, int sm_count,
 int pv_windows_noalloc(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
                        const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* stream);
 
+/* ---- device: the checkpoint index (no counterpart in the reference, whose decoder always starts at a block's start) */
+
+/* bytes of the checkpoint index of a cohort of nblocks pooled blocks at stride 1 << ckpt_shift (0 when the stride is
+ * not a power of two between 256 and Q) */
+size_t pv_index_bytes(uint32_t Q, uint64_t nblocks, uint32_t ckpt_shift);
+/* Decode every block of the cohort once on the device (blocks served from the block cache are skipped) and write its
+ * checkpoints into out (pv_index_bytes bytes, 16-byte aligned, device). cohort->ckpt is ignored. *nbad (device uint64,
+ * zeroed by the caller, or NULL) counts the blocks that failed. Asynchronous on `stream`. */
+int pv_index_build(const pv_dev_cohort* cohort, uint64_t nblocks, uint32_t ckpt_shift, pv_ckpt* out, uint64_t* nbad, void* stream);
+
 /* ---- device: the whole-assembly checks (Cohort.check_full / fasta, panvram/cohort.py:224-234, whose FASTA rebuild
  * and XXH3 run on the host in the reference, pv_core.cpp:138-176) ---- */
 
@@ -330,8 +363,9 @@ int pv_status_to_host(const int32_t* status, int32_t* host_word, void* stream);
 /* at most how many kernel launches one pv_windows call with these sizes makes (0 for an empty call) */
 int pv_windows_launches(int64_t n, int64_t W);
 /* the form a pv_windows_ex call with these sizes and flags takes: *launches 1 (pv_windows_kernel) or 2
- * (pv_decode_kernel + pv_emit_kernel; *dec_lanes items per decode warp), 0 for an empty call */
-int pv_windows_form(uint32_t Q, int64_t n, int64_t W, uint32_t flags, int* launches, uint32_t* dec_lanes);
+ * (pv_decode_kernel + pv_emit_kernel; *dec_lanes items per decode warp), 0 for an empty call. cell: the cohort's item
+ * cell, its checkpoint stride (1 << ckpt_shift) when it has an index, else its block size Q. */
+int pv_windows_form(uint32_t cell, int64_t n, int64_t W, uint32_t flags, int* launches, uint32_t* dec_lanes);
 /* message of the calling thread's last pv_windows / pv_windows_ex argument or launch failure */
 const char* pv_kernels_last_error(void);
 

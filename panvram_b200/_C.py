@@ -37,7 +37,8 @@ class DevCohort(ctypes.Structure):
                 ("Q", ctypes.c_uint32), ("pad", ctypes.c_uint32),
                 ("pref", ctypes.c_void_p), ("pruns", ctypes.c_void_p), ("pidx", ctypes.c_void_p), ("pnruns", ctypes.c_uint64),
                 ("groups", ctypes.c_void_p), ("btab", ctypes.c_void_p), ("bexc", ctypes.c_void_p),
-                ("packed", ctypes.c_uint32), ("compact", ctypes.c_uint32)]
+                ("packed", ctypes.c_uint32), ("compact", ctypes.c_uint32),
+                ("ckpt", ctypes.c_void_p), ("ckpt_shift", ctypes.c_uint32), ("pad2", ctypes.c_uint32)]
 
 
 class HostPools(ctypes.Structure):
@@ -103,7 +104,9 @@ for _name, _res, _args in (
         ("pv_xxh3_64_long_host", _I32, [_P, _U64, ctypes.POINTER(_U64)]),
         ("pv_sample_draw_coords", _I32, [_P, _P, _P, _P, _P, _I64, _U64, _P, _U64, _U64, ctypes.c_float, _I32, _I64, _P, _P, _P, _P, _P, _P,
                                          _P, _P]),
-        ("pv_torch_draw_geometry", _I32, [_I64, _U64, _I32, _I32, _I32, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)])):
+        ("pv_torch_draw_geometry", _I32, [_I64, _U64, _I32, _I32, _I32, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)]),
+        ("pv_index_bytes", _SZ, [_U32, _U64, _U32]),
+        ("pv_index_build", _I32, [ctypes.POINTER(DevCohort), _U64, _U32, _P, _P, _P])):
     _f = getattr(_lib, _name)
     _f.restype, _f.argtypes = _res, _args
 
@@ -441,6 +444,26 @@ def coords_from_host(asm, start, rc, device):
     return a, s, r
 
 
+PV_CKPT_BAD = 1
+
+
+def index_build(dev, nblocks, ckpt_shift, device):
+    """The cohort's checkpoint index on `device` (pv_index_build: every block decoded once on the device; blocks in the
+    block cache skipped) -> (uint8 tensor of pv_ckpt records, number of blocks that failed to decode). Waits for it."""
+    nbytes = int(_lib.pv_index_bytes(int(dev.Q), int(nblocks), int(ckpt_shift)))
+    if not nbytes:
+        raise ValueError(f"checkpoint stride 2^{ckpt_shift}: a power of two from 256 to the block size {dev.Q}")
+    out = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    nbad = torch.zeros(1, dtype=torch.int64, device=device)
+    with torch.cuda.device(device):
+        code = _lib.pv_index_build(ctypes.byref(dev), int(nblocks), int(ckpt_shift), out.data_ptr(), nbad.data_ptr(),
+                                   torch.cuda.current_stream(device).cuda_stream)
+        if code:
+            raise RuntimeError("panvram_b200 index: " + (_lib.pv_kernels_last_error() or b"").decode())
+        torch.cuda.current_stream(device).synchronize()
+    return out, int(nbad.item())
+
+
 def read_status(status):
     """The int32 status word (a CUDA tensor) after the work queued before this call on the current stream, as an int:
     stored by one device thread into a pinned host word (pv_status_to_host), then the stream waited for - so the read
@@ -457,10 +480,11 @@ def launches_per_call(n, W):
     return int(_lib.pv_windows_launches(int(n), int(W)))
 
 
-def windows_form(Q, n, W, flags=0):
+def windows_form(cell, n, W, flags=0):
     """(kernel launches, decode items per warp) of a window call with these sizes: (1, 0) the fused kernel, (2, k) the
-    split form with k items per decode warp, (0, 0) an empty call."""
+    split form with k items per decode warp, (0, 0) an empty call. cell: the cohort's checkpoint stride when it has an
+    index (Cohort.item_cell), else its block size."""
     L, k = ctypes.c_int(), _U32()
-    if _lib.pv_windows_form(int(Q), int(n), int(W), int(flags), ctypes.byref(L), ctypes.byref(k)):
+    if _lib.pv_windows_form(int(cell), int(n), int(W), int(flags), ctypes.byref(L), ctypes.byref(k)):
         raise ValueError((_lib.pv_kernels_last_error() or b"").decode())
     return L.value, k.value

@@ -64,7 +64,9 @@ class Cohort:
     space or tab, or its index in the assembly; an assembly is its name (archive file name without .<dataset>.rr3) or
     its index."""
 
-    def __init__(self, core, names, device, block_cache=True):
+    CHECKPOINT_STRIDE = 2048
+
+    def __init__(self, core, names, device, block_cache=True, checkpoint_stride=None):
         self._core, self.names, self.device = core, list(names), torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("panvram_b200 decodes on the GPU only: open the cohort with device='cuda' or 'cuda:N'")
@@ -102,6 +104,32 @@ class Cohort:
         self.launch_flags = 0
         if block_cache:
             self._build_block_cache(pools)
+        self._index, self.checkpoint_stride, self.bad_blocks = None, 0, 0
+        stride = self.CHECKPOINT_STRIDE if checkpoint_stride is None else int(checkpoint_stride)
+        if stride:
+            self._build_index(min(stride, core.Q))
+
+    def _build_index(self, stride):
+        """The checkpoint index (pv_index_build): every block not in the block cache decoded once on the device, its
+        decoder state kept at the last event boundary at or before each multiple of `stride` in the block. Window items
+        then cover one stride each: each decodes from its checkpoint to the end of its range only, so a window's serial
+        chains are about a stride long instead of a block, and the blocks outside the window's span are not decoded.
+        Decoding every block here also validates it: a block that fails is marked, and windows touching it report
+        status 1 exactly as when they decoded it in full."""
+        if stride & (stride - 1) or not 256 <= stride <= self._core.Q:
+            raise ValueError(f"checkpoint_stride: a power of two from 256 to the block size ({self._core.Q}), or 0")
+        shift = stride.bit_length() - 1
+        asms = self._dev["asms"].cpu().numpy().view(np.uint64).reshape(-1, 8)
+        nblocks = int(asms[:, 2].sum())
+        self._index, self.bad_blocks = _C.index_build(self._devc, nblocks, shift, self.device)
+        self._devc.ckpt, self._devc.ckpt_shift = self._index.data_ptr(), shift
+        self.checkpoint_stride = stride
+
+    @property
+    def item_cell(self):
+        """The bases one work item of the window kernels covers: the checkpoint stride, or the block size without an
+        index."""
+        return self.checkpoint_stride or self._core.Q
 
     CACHE_BYTES = 4 << 30
 
@@ -175,7 +203,7 @@ class Cohort:
 
     @classmethod
     def open(cls, path, device="cuda", dataset="q4k", reference=None, threads=0, assemblies=None,
-             packed_reference=False, compact_blocks=False, block_cache=True):
+             packed_reference=False, compact_blocks=False, block_cache=True, checkpoint_stride=None):
         """Open the cohort directory `path`: every `*.<dataset>.rr3` in it (sorted by name; `assemblies` = a list of
         names to take only those) and the reference they were encoded against - `reference` if given, else
         `path/reference.fa`, else the file named in the archives' header in `path`. Every archive is checked before
@@ -183,7 +211,11 @@ class Cohort:
         device: "cuda" or "cuda:N". block_cache: decode the long (literal-heavy) blocks once at open and serve them
         from HBM (same output; see _build_block_cache). Opt-in compact resident forms (same archives, same output):
         packed_reference - the reference in 2 bits per base plus its runs of other bytes instead of a byte per base;
-        compact_blocks - the block table as 32-byte records per 32 blocks plus 4 bytes per block instead of 16."""
+        compact_blocks - the block table as 32-byte records per 32 blocks plus 4 bytes per block instead of 16.
+        checkpoint_stride: the decoder checkpoint index built on the device at open (see _build_index): a checkpoint
+        every this many bases of each block (a power of two from 256 to the block size; None: 2048, capped at the block
+        size; 0: no index - every window item then decodes its whole block). Same output either way; 32 bytes per
+        checkpoint of device memory."""
         if dataset is not None and not re.fullmatch(r"q\d+k", dataset):
             raise ValueError(f"dataset: {DATASETS} (or another q<N>k suffix), or None for every *.rr3")
         pat = f"*.{dataset}.rr3" if dataset else "*.rr3"
@@ -215,7 +247,7 @@ class Cohort:
         if device.index is None:
             device = torch.device("cuda", torch.cuda.current_device())
         core = _C.Core(os.fspath(reference), [os.fspath(f) for f in files], int(threads), bool(packed_reference), bool(compact_blocks))
-        return cls(core, names, device, block_cache=block_cache)
+        return cls(core, names, device, block_cache=block_cache, checkpoint_stride=checkpoint_stride)
 
     # ------------------------------------------------------------------ description
     def __len__(self):
@@ -243,12 +275,13 @@ class Cohort:
         """Bytes of the cohort on its device (reference included), by component. Keys follow the reference's where
         the component is the same (P payload, tab model tables, ref reference); blocks is the block table (the
         reference's off + st), low the lower-case runs (low_s + low_l), asm the per-assembly records, cache the decoded
-        long blocks."""
+        long blocks, index the decoder checkpoints."""
         d = self._dev
         nb = lambda *ks: sum(d[k].numel() * d[k].element_size() for k in ks if k in d)
         r = {"P": nb("payload"), "blocks": nb("blocks", "groups", "btab", "bexc"), "tab": nb("tabs"), "low": nb("low"),
              "ref": nb("ref_padded", "pref", "pruns", "pidx"), "asm": nb("asms"),
-             "cache": self._cache.numel() if self._cache is not None else 0}
+             "cache": self._cache.numel() if self._cache is not None else 0,
+             "index": self._index.numel() if self._index is not None else 0}
         r["total"] = sum(r.values())
         return r
 

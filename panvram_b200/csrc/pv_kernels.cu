@@ -74,6 +74,10 @@ struct __align__(16) Item {
     uint32_t run_first, run_cnt;
     uint32_t tab_bytes, span_len;   // span_len: bytes of the reference staged in the slot (from position span_lo)
     int64_t span_lo;
+    uint64_t ck;            // its decode's starting checkpoint in the cohort's index, or NO_CK (the block's start)
+    int64_t cst;            // the current diagonal c << 1 | dir where the decode starts (the spans follow it)
+    uint32_t co;            // the block offset where the decode starts
+    uint32_t jc, wx0, wx1;  // its cell of the block; the window's bytes in the block [wx0, wx1)
     Op ops[OPS_CAP];
     uint8_t lits[LIT_CAP];
     int32_t runs[2 * RUN_CAP];   // window-relative [start, end), clipped to the item's range
@@ -92,7 +96,9 @@ struct Params {
     int64_t* out64;                // token-id output (pv_windows_ids): int64 [n, W]; then `out` is unused
     int64_t ids[5];                // the ids of tokens 0..4
     uint32_t dec_lanes;            // split form: items per decode warp (one per lane, lanes 0 .. dec_lanes - 1)
+    uint32_t cshift;               // log2 of an item's cell: the checkpoint stride, or the block size without an index
 };
+constexpr uint64_t NO_CK = ~0ull;
 
 // status bits into the call's word and, when asked, into the window's byte (4-byte aligned, padded array)
 __device__ __forceinline__ void report(const Params& P, uint64_t w, int bits) {
@@ -310,13 +316,30 @@ __device__ __forceinline__ void dec_init(Dec<S>& d, const S& src, int64_t st) {
     d.st.skip(3);
 }
 
-// The event loop of refrel3.h:114-160. Sinks: more() is asked before each event (false pauses, resumable),
-// lit()/op() returning false abort the decode (the caller takes another path). Returns DEC_*.
+// The decoder at a checkpoint of the cohort's index (include/panvram_b200.h pv_ckpt): st reads the block's stream from
+// its first byte; the checkpoint says how far it had been consumed.
+__device__ __forceinline__ uint64_t ck_diag(uint32_t lo, uint32_t hi) { return (((uint64_t)(hi & 0x7Fu) << 32) | lo) - (uint64_t)PV_CKPT_BIAS; }
+template <class S>
+__device__ __forceinline__ void dec_init_ck(Dec<S>& d, const S& src, const pv_ckpt* ck) {
+    const uint4 a = __ldg((const uint4*)ck), b = __ldg((const uint4*)ck + 1);
+    d.st = src; d.st.skip(a.y); d.bad = 0;
+    d.x = a.x & 0xFFFFFFu; d.pk = (a.x >> 24) & 7u; d.nc = (int)((a.x >> 27) & 3u) + 1;
+    d.o = b.w & 0xFFFFu; d.li = 0;
+    d.c0 = ck_diag(a.z, b.z); d.c1 = ck_diag(a.w, b.z >> 8); d.c2 = ck_diag(b.x, b.z >> 16); d.c3 = ck_diag(b.y, b.z >> 24);
+    d.d0 = (b.z >> 7) & 1u; d.d1 = (b.z >> 15) & 1u; d.d2 = (b.z >> 23) & 1u; d.d3 = b.z >> 31;
+}
+
+// The event loop of refrel3.h:114-160, from the decoder's state (a block's start or a checkpoint) until the output
+// reaches `stop` (blen: the whole block, with the end-of-stream checks of refrel3.h:157; less: an item's range of a
+// block the cohort's index has validated, so the decode ends with the event that reaches `stop`). Sinks: at(d) sees
+// the state at each event boundary, more() is asked before each event (false pauses, resumable), lit()/op()
+// returning false abort the decode (the caller takes another path). Returns DEC_*.
 template <class S, class Sink, class Tb>
-__device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefView& R, uint32_t blen, Sink& sk) {
+__device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefView& R, uint32_t blen, uint32_t stop, Sink& sk) {
     const uint64_t ref_n = R.n;
     if (d.bad) return DEC_ERR;
-    while (d.o < blen) {
+    while (d.o < stop) {
+        sk.at(d);
         if (!sk.more()) return DEC_PAUSE;
         const uint32_t kc = kclass(d.pk);
         const uint32_t ll = dval_big(d, T, (int)kc);                         // LL x previous kind class
@@ -336,7 +359,7 @@ __device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefVi
             if (!sk.op(0, d.li, d.o, ll)) return DEC_ABORT;
             d.li += ll; d.o += ll;
         }
-        if (d.o == blen) break;
+        if (d.o >= stop) break;
         const uint32_t kind = dsym_small(d, T, C_KIND + (int)(llc(ll) * 4 + kc));
         if (kind > K_FLIP) return DEC_ERR;
         // the kind's arguments, in stream order: at most one small symbol (REP: cache index - 1, ABS: strand, FLIP: cache
@@ -381,6 +404,7 @@ __device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefVi
         if (!sk.op(okind, osrc, d.o, L)) return DEC_ABORT;
         d.o += L; d.pk = kind + 1;
     }
+    if (d.o < blen) return DEC_DONE;                 // stopped inside a validated block
     if (d.bad || d.x != RANS_L || d.st.left() != 0) return DEC_ERR;
     return DEC_DONE;
 }
@@ -388,6 +412,7 @@ __device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefVi
 // keeps the ops and literals that fall inside [ox0, ox1) of the block
 struct WindowSink {
     Op* ops; uint8_t* lits; uint32_t ox0, ox1, nops, nlits;
+    template <class D> __device__ __forceinline__ void at(const D&) const {}
     __device__ bool more() const { return true; }
     __device__ bool lit(uint32_t o, uint8_t b) {
         if (o < ox0 || o >= ox1) return true;
@@ -407,6 +432,7 @@ struct WindowSink {
 // heavy path: literals straight into the block buffer, copies (up to ox1) into a chunk of HOPS ops
 struct BlockSink {
     uint8_t* buf; Op* ops; uint32_t nops, ox1;
+    template <class D> __device__ __forceinline__ void at(const D&) const {}
     __device__ bool more() const { return nops + 1 < (uint32_t)HOPS; }
     __device__ bool lit(uint32_t o, uint8_t b) { buf[o] = b; return true; }
     __device__ bool op(uint32_t kind, uint64_t src, uint32_t dst, uint32_t len) {
@@ -785,7 +811,9 @@ __device__ __forceinline__ RefView slot_ref(const Params& P, uint8_t* slot) {
                    PK ? P.C.pref : nullptr, P.C.pruns, P.C.pidx};
 }
 
-// lane 0: the item's window and block; the ranges, its lower-case runs; false when there is nothing to decode
+// lane 0: the item's window, block and cell (items of a window are the cells [jS, (j+1)S) of the cohort's checkpoint
+// stride S it touches, S = Q without an index, so then one item per block), its nominal output range (cell and window
+// intersected); false when there is nothing to decode
 __device__ bool item_locate(const Params& P, uint64_t item, Item* it) {
     it->state = ST_IDLE;
     if (item >= P.total) return false;
@@ -795,8 +823,10 @@ __device__ bool item_locate(const Params& P, uint64_t item, Item* it) {
     if (a < 0 || a >= C.nasm) { if (j == 0) report(P, w, PV_STATUS_WINDOW); return false; }
     const pv_asm_rec& R = C.asms[a];
     if (s < 0 || (uint64_t)s + P.W > R.nbases) { if (j == 0) report(P, w, PV_STATUS_WINDOW); return false; }
-    const uint64_t Q = C.Q, b0 = (uint64_t)s >> P.qshift, b1 = ((uint64_t)s + P.W - 1) >> P.qshift, b = b0 + j;
-    if (b > b1) return false;
+    const uint32_t cs = P.cshift;
+    const uint64_t Q = C.Q, g0 = (uint64_t)s >> cs, g1 = ((uint64_t)s + P.W - 1) >> cs, g = g0 + j;
+    if (g > g1) return false;
+    const uint64_t b = g >> (P.qshift - cs);
     const uint64_t bst = b * Q, blen = R.nbases - bst < Q ? R.nbases - bst : Q;
     const uint64_t x0 = (uint64_t)s > bst ? (uint64_t)s : bst, x1 = (uint64_t)s + P.W < bst + blen ? (uint64_t)s + P.W : bst + blen;
     it->w = (int64_t)w; it->s = (uint64_t)s; it->bst = bst; it->gblk = R.blk_base + b; it->a = (int32_t)a;
@@ -804,24 +834,63 @@ __device__ bool item_locate(const Params& P, uint64_t item, Item* it) {
     it->gm = (uint32_t)(R.nb - (b & ~31ull) < 32 ? R.nb - (b & ~31ull) : 32);
     it->staged = 0;
     it->tab_off = R.tab_off; it->tab_bytes = (uint32_t)R.tab_bytes; it->span_lo = 0; it->span_len = 0;
-    it->ox0 = (uint32_t)(x0 - bst); it->ox1 = (uint32_t)(x1 - bst); it->blen = (uint32_t)blen;
+    it->jc = (uint32_t)(g - (b << (P.qshift - cs)));
+    it->wx0 = (uint32_t)(x0 - bst); it->wx1 = (uint32_t)(x1 - bst); it->blen = (uint32_t)blen;
+    const uint32_t cx0 = it->jc << cs, cx1 = cx0 + (1u << cs);
+    it->ox0 = it->wx0 > cx0 ? it->wx0 : cx0; it->ox1 = it->wx1 < cx1 ? it->wx1 : cx1;
+    it->ck = NO_CK; it->co = 0;
     it->run_first = 0; it->run_cnt = 0; it->nops = 0; it->nlits = 0;
-    if (P.apply_case && !P.tokens && R.low_cnt) {                      // runs overlapping [x0, x1)
-        const uint64_t* low = C.low + 2 * R.low_base;
-        uint64_t lo = 0, hi = R.low_cnt;
-        while (lo < hi) { const uint64_t m = (lo + hi) >> 1; if (__ldg(low + 2 * m + 1) <= x0) lo = m + 1; else hi = m; }
-        uint64_t e = lo;
-        while (e < R.low_cnt && __ldg(low + 2 * e) < x1) e++;
-        it->run_first = (uint32_t)(R.low_base + lo); it->run_cnt = (uint32_t)(e - lo);
-        if (e - lo <= (uint64_t)RUN_CAP)
-            for (uint64_t r = lo; r < e; r++) {
-                const uint64_t rs = __ldg(low + 2 * r), re = __ldg(low + 2 * r + 1);
-                it->runs[2 * (r - lo)] = (int32_t)((rs > x0 ? rs : x0) - (uint64_t)s);
-                it->runs[2 * (r - lo) + 1] = (int32_t)((re < x1 ? re : x1) - (uint64_t)s);
-            }
-    }
     it->state = ST_LOCATED;
     return true;
+}
+
+// lane 0, for a located item of a cohort with a checkpoint index: its decode starts at its cell's checkpoint j (the
+// last event boundary at or before the cell's start), and its output range is what the decode from there produces up
+// to the next cell's checkpoint - or, for the window's last cell of the block, up to the window's end - intersected
+// with the window: [max(wx0, o_j), j last ? wx1 : o_j+1). So the items of a window tile it exactly, each event is
+// decoded once (but the one reaching the window's end), and a long event spanning several cells belongs to one item.
+// A block the index found corrupt reports status 1 (ST_ERR); an empty range leaves the item idle.
+__device__ void item_ckpt(const Params& P, Item* it) {
+    const pv_dev_cohort& C = P.C;
+    const uint32_t ncs = P.qshift - P.cshift;
+    const uint64_t k = (it->gblk << ncs) + it->jc;
+    const pv_ckpt* ck = C.ckpt + k;
+    const uint32_t ow = __ldg((const uint32_t*)ck + 7);            // o | flags << 16
+    if (ow >> 16) { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); return; }
+    const uint32_t o0 = ow & 0xFFFFu;
+    const bool last = it->jc == ((it->wx1 - 1) >> P.cshift);
+    uint32_t o1 = it->wx1;
+    if (!last) {
+        const uint32_t on = it->jc + 1 < (1u << ncs) ? (__ldg((const uint32_t*)(ck + 1) + 7) & 0xFFFFu) : it->blen;
+        o1 = on < o1 ? on : o1;
+    }
+    it->ox0 = it->wx0 > o0 ? it->wx0 : o0;
+    it->ox1 = o1;
+    if (it->ox0 >= it->ox1) { it->state = ST_IDLE; return; }
+    it->ck = k; it->co = o0;
+    const uint4 b = __ldg((const uint4*)ck + 1);
+    const uint32_t lo = __ldg((const uint32_t*)ck + 2);
+    it->cst = (int64_t)(ck_diag(lo, b.z) << 1) | (int64_t)((b.z >> 7) & 1u);
+}
+
+// lane 0: the lower-case runs overlapping the item's output range (window-relative, clipped to it)
+__device__ void item_runs(const Params& P, Item* it) {
+    const pv_dev_cohort& C = P.C;
+    const pv_asm_rec& R = C.asms[it->a];
+    if (!(P.apply_case && !P.tokens && R.low_cnt)) return;
+    const uint64_t x0 = it->bst + it->ox0, x1 = it->bst + it->ox1, s = it->s;
+    const uint64_t* low = C.low + 2 * R.low_base;
+    uint64_t lo = 0, hi = R.low_cnt;
+    while (lo < hi) { const uint64_t m = (lo + hi) >> 1; if (__ldg(low + 2 * m + 1) <= x0) lo = m + 1; else hi = m; }
+    uint64_t e = lo;
+    while (e < R.low_cnt && __ldg(low + 2 * e) < x1) e++;
+    it->run_first = (uint32_t)(R.low_base + lo); it->run_cnt = (uint32_t)(e - lo);
+    if (e - lo <= (uint64_t)RUN_CAP)
+        for (uint64_t r = lo; r < e; r++) {
+            const uint64_t rs = __ldg(low + 2 * r), re = __ldg(low + 2 * r + 1);
+            it->runs[2 * (r - lo)] = (int32_t)((rs > x0 ? rs : x0) - s);
+            it->runs[2 * (r - lo) + 1] = (int32_t)((re < x1 ? re : x1) - s);
+        }
 }
 
 // The block's stream (offset, length) and start state, into the Item; the state becomes ST_CACHED for a block served
@@ -836,7 +905,7 @@ __device__ void item_block(const Params& P, Item* it, int lane) {
     if (!CP) {
         if (lane != 0) return;
         const uint64_t loc = __ldg(C.blocks + 2 * it->gblk);
-        it->pst = (int64_t)__ldg(C.blocks + 2 * it->gblk + 1);
+        it->pst = it->cst = (int64_t)__ldg(C.blocks + 2 * it->gblk + 1);
         it->poff = loc_off(loc);
         it->plen = loc_len(loc);
         if (it->plen == (uint32_t)PV_BLOCK_CACHED) { it->state = ST_CACHED; it->cptr = C.cache + loc_off(loc) * C.Q; }
@@ -863,7 +932,7 @@ __device__ void item_block(const Params& P, Item* it, int lane) {
     if (lane != 0) return;
     const int64_t c = (base >> 1) + sum;
     const uint32_t dir = (int)j == b ? (uint32_t)(base & 1) : (uint32_t)(cj & 1);
-    it->poff = off; it->plen = lj; it->pst = (int64_t)((uint64_t)c << 1) | (int64_t)dir;
+    it->poff = off; it->plen = lj; it->pst = it->cst = (int64_t)((uint64_t)c << 1) | (int64_t)dir;
     const uint32_t cmask = __ldg(&G->cache_mask);
     if ((cmask >> j) & 1u) {
         it->state = ST_CACHED;
@@ -871,11 +940,13 @@ __device__ void item_block(const Params& P, Item* it, int lane) {
     }
 }
 
-// the reference span of an item, 16-byte aligned: its block's start diagonal over the whole block, or (out_only) under
-// the item's output range only, with a margin either way; empty when it would not fit `cap` bytes
+// the reference span of an item, 16-byte aligned: the diagonal current where its decode starts (the block's start
+// diagonal, or its checkpoint's) over the range its decode covers, or (out_only) under the item's output range only,
+// with a margin either way; empty when it would not fit `cap` bytes
 __device__ __forceinline__ void item_span(const Params& P, Item* it, bool out_only, uint64_t cap) {
-    const int64_t st = it->pst, c0 = st >> 1;
-    const int64_t o0 = out_only ? (int64_t)it->ox0 : 0, o1 = out_only ? (int64_t)it->ox1 : (int64_t)it->blen;
+    const int64_t st = it->cst, c0 = st >> 1;
+    const bool ck = it->ck != NO_CK;               // from a checkpoint the decode covers [co, ox1), else the whole block
+    const int64_t o0 = out_only ? (int64_t)it->ox0 : (int64_t)it->co, o1 = (out_only || ck) ? (int64_t)it->ox1 : (int64_t)it->blen;
     int64_t lo = (st & 1) ? c0 - o1 + 1 - SPAN_MARGIN : c0 + o0 - SPAN_MARGIN, hi = (st & 1) ? c0 - o0 + 1 + SPAN_MARGIN : c0 + o1 + SPAN_MARGIN;
     lo = lo < 0 ? 0 : lo; hi = hi > (int64_t)P.C.ref_n ? (int64_t)P.C.ref_n : hi;
     uint64_t ra = 0, re = 0;
@@ -884,14 +955,18 @@ __device__ __forceinline__ void item_span(const Params& P, Item* it, bool out_on
     it->span_lo = (int64_t)ra; it->span_len = (uint32_t)(re - ra);
 }
 
-// lane 0: the reference span the block's start diagonal covers over the whole block, with a margin (the literal
-// contexts and most copy sources read it from shared memory), then TMA bulk copies into the warp's slot of the
+// lane 0: the reference span the decode's starting diagonal covers over the range it decodes, with a margin (the
+// literal contexts and most copy sources read it from shared memory), then TMA bulk copies into the warp's slot of the
 // assembly's decode table, the block's stream when it fits and, for the byte reference, the span
 template <bool PK>
 __device__ void item_stage(const Params& P, uint8_t* slot, uint32_t bar) {
     Item* it = slot_item(slot);
     const pv_dev_cohort& C = P.C;
-    if (P.narrow) {
+    if (it->ck != NO_CK) {
+        // from a checkpoint: the decode covers [co, ox1), little more than the output range
+        item_span(P, it, false, P.span_cap);
+        if (!it->span_len) item_span(P, it, true, P.span_cap);
+    } else if (P.narrow) {
         // windows shorter than a block: the slot holds the diagonal under the output range only (what the emission
         // reads); the whole block's span is warmed in L2 for the literal contexts the decode reads off it
         item_span(P, it, false, ~0ull);
@@ -952,8 +1027,10 @@ __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
     WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
     const uint32_t sp = smem_addr(slot_pay(P, slot)) + (uint32_t)((uintptr_t)(P.C.payload + it->poff) & 15);
     Dec<SmemStream> d;
-    dec_init(d, SmemStream{sp, sp + it->plen}, it->pst);
-    const int r = decode_events(d, SmemTab{smem_addr(slot_tab(P, slot))}, slot_ref<PK>(P, slot), it->blen, sk);
+    uint32_t stop = it->blen;
+    if (it->ck != NO_CK) { dec_init_ck(d, SmemStream{sp, sp + it->plen}, P.C.ckpt + it->ck); stop = it->ox1; }
+    else dec_init(d, SmemStream{sp, sp + it->plen}, it->pst);
+    const int r = decode_events(d, SmemTab{smem_addr(slot_tab(P, slot))}, slot_ref<PK>(P, slot), it->blen, stop, sk);
     it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     if (r == DEC_DONE) it->state = ST_OK;
     else if (r == DEC_ABORT) it->state = ST_HEAVY;
@@ -983,7 +1060,7 @@ __device__ __noinline__ void heavy_item(const Params& P, uint8_t* slot, uint8_t*
         if (threadIdx.x == 0) {
             Dec<GlobalStream> d = h_dec;
             BlockSink sk{buf, hops, 0, it->ox1};
-            h_res = decode_events(d, T, R, it->blen, sk);
+            h_res = decode_events(d, T, R, it->blen, it->blen, sk);
             h_nops = (int)sk.nops;
             h_dec = d;
         }
@@ -1034,6 +1111,11 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constan
     if (it->state == ST_LOCATED) {
         item_block<CP>(P, it, lane);
         __syncwarp();
+        if (lane == 0) {
+            if (P.C.ckpt && it->state == ST_LOCATED) item_ckpt(P, it);
+            if (it->state == ST_LOCATED || it->state == ST_CACHED) item_runs(P, it);
+        }
+        __syncwarp();
         if (it->state == ST_LOCATED) {
             if (lane == 0) item_stage<PK>(P, slot, bar);
             __syncwarp();
@@ -1060,22 +1142,24 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constan
 // the warp, and the other 31 lanes no longer idle). The result, the Item (ops and literal bytes inside the window),
 // goes to the plan array in global memory. pv_emit_kernel: one item per WARP, as the fused kernel's emission.
 
-// the compact table walked by one lane (the reference's chain, pv_compact.h:40-46): offset and state of block j of its group
+// One lane's block lookup: pooled block gblk (block b of its assembly, whose first compact group is grp_base) -> its
+// stream's payload offset and length, its start state c << 1 | dir, and (cache) its row in the block cache, or NULL.
+// The compact table is walked as the reference's chain (pv_compact.h:40-46): offset and state of block j of its group.
+struct BlockRec { uint64_t poff; int64_t pst; uint32_t plen; const uint8_t* cache; };
 template <bool CP>
-__device__ void item_block_lane(const Params& P, Item* it) {
-    const pv_dev_cohort& C = P.C;
+__device__ __forceinline__ BlockRec block_rec(const pv_dev_cohort& C, uint64_t gblk, uint64_t grp_base, uint64_t b) {
+    BlockRec r{0, 0, 0, nullptr};
     if (!CP) {
-        const uint64_t loc = __ldg(C.blocks + 2 * it->gblk);
-        it->pst = (int64_t)__ldg(C.blocks + 2 * it->gblk + 1);
-        it->poff = loc_off(loc);
-        it->plen = loc_len(loc);
-        if (it->plen == (uint32_t)PV_BLOCK_CACHED) { it->state = ST_CACHED; it->cptr = C.cache + loc_off(loc) * C.Q; }
-        else if (it->plen == (uint32_t)PV_BLEN_BAD) { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
-        return;
+        const uint64_t loc = __ldg(C.blocks + 2 * gblk);
+        r.pst = (int64_t)__ldg(C.blocks + 2 * gblk + 1);
+        r.poff = loc_off(loc);
+        r.plen = loc_len(loc);
+        if (r.plen == (uint32_t)PV_BLOCK_CACHED) r.cache = C.cache + loc_off(loc) * C.Q;
+        return r;
     }
-    const uint32_t j = it->gj;
-    const pv_blk_group* G = C.groups + it->grp;
-    const uint32_t* bt = C.btab + (it->gblk - j);
+    const uint32_t j = (uint32_t)(b & 31);
+    const pv_blk_group* G = C.groups + grp_base + (b >> 5);
+    const uint32_t* bt = C.btab + (gblk - j);
     const uint32_t emask = __ldg(&G->exc_mask);
     uint64_t off = __ldg(&G->off);
     int64_t st = __ldg(&G->state);
@@ -1087,12 +1171,17 @@ __device__ void item_block_lane(const Params& P, Item* it) {
         const int64_t pc = st >> 1, pred = (st & 1) ? pc - (int64_t)C.Q : pc + (int64_t)C.Q;
         st = (int64_t)((uint64_t)(pred + (code >> 1)) << 1) | (int64_t)(code & 1);
     }
-    it->poff = off; it->pst = st; it->plen = __ldg(bt + j) & 0xFFFFu;
+    r.poff = off; r.pst = st; r.plen = __ldg(bt + j) & 0xFFFFu;
     const uint32_t cmask = __ldg(&G->cache_mask);
-    if ((cmask >> j) & 1u) {
-        it->state = ST_CACHED;
-        it->cptr = C.cache + (uint64_t)(__ldg(&G->cache_base) + __popc(cmask & ((1u << j) - 1u))) * C.Q;
-    }
+    if ((cmask >> j) & 1u) r.cache = C.cache + (uint64_t)(__ldg(&G->cache_base) + __popc(cmask & ((1u << j) - 1u))) * C.Q;
+    return r;
+}
+template <bool CP>
+__device__ void item_block_lane(const Params& P, Item* it) {
+    const BlockRec r = block_rec<CP>(P.C, it->gblk, P.C.asms[it->a].grp_base, it->bst >> P.qshift);
+    it->poff = r.poff; it->plen = r.plen; it->pst = it->cst = r.pst;
+    if (r.cache) { it->state = ST_CACHED; it->cptr = r.cache; }
+    else if (!CP && r.plen == (uint32_t)PV_BLEN_BAD) { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
 }
 
 constexpr int DEC_THREADS = 32;            // one warp per CTA: the few decode warps of a call spread over all SMs
@@ -1107,6 +1196,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
     Item* it = plan + i;
     if (!item_locate(P, i, it)) return;
     item_block_lane<CP>(P, it);
+    if (P.C.ckpt && it->state == ST_LOCATED) item_ckpt(P, it);
+    if (it->state == ST_LOCATED || it->state == ST_CACHED) item_runs(P, it);
     if (it->state != ST_LOCATED) return;
     item_span(P, it, false, ~0ull);              // (L2 only: any length)
     const pv_dev_cohort& C = P.C;
@@ -1116,9 +1207,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
     const uint8_t* src = C.payload + it->poff;
     WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
     Dec<GlobalStream> d;
-    dec_init(d, GlobalStream{src, src + it->plen}, it->pst);
+    uint32_t stop = it->blen;
+    if (it->ck != NO_CK) { dec_init_ck(d, GlobalStream{src, src + it->plen}, C.ckpt + it->ck); stop = it->ox1; }
+    else dec_init(d, GlobalStream{src, src + it->plen}, it->pst);
     const RefView R{C.ref, C.ref_n, 0, 0, 0, PK ? C.pref : nullptr, C.pruns, C.pidx};
-    const int r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, sk);
+    const int r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, stop, sk);
     it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     if (r == DEC_DONE) it->state = ST_OK;
     else if (r == DEC_ABORT) it->state = ST_HEAVY;
@@ -1178,6 +1271,62 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
     for (int t = 0; t < WARPS; t++) {
         uint8_t* sl = (uint8_t*)smem_raw + (size_t)t * P.slot_bytes;
         if (slot_item(sl)->state == ST_HEAVY) heavy_item<PK, true>(P, sl, buf, hops);
+    }
+}
+
+// ---------------------------------------------------------------- the checkpoint index (pv_index_build)
+// A block decoded once, from its start, by one lane; at every event boundary the sink sees the decoder's state and
+// writes it into the checkpoints whose offsets j S it is the last boundary at or before (pv_ckpt, packed the same way
+// dec_init_ck unpacks it).
+struct CkptSink {
+    uint4* out;                  // the block's checkpoints, two uint4 each
+    const uint8_t* base;         // the block stream's first byte
+    uint32_t cs, ncell, jn;      // stride shift, checkpoints per block, the next one to write
+    uint4 sa, sb;                // the last event boundary's state
+    __device__ __forceinline__ void put(uint32_t j) { out[2 * j] = sa; out[2 * j + 1] = sb; }
+    __device__ __forceinline__ void at(const Dec<GlobalStream>& d) {
+        while (jn < ncell && (jn << cs) < d.o) put(jn++);
+        const uint64_t c[4] = {d.c0 + (uint64_t)PV_CKPT_BIAS, d.c1 + (uint64_t)PV_CKPT_BIAS, d.c2 + (uint64_t)PV_CKPT_BIAS,
+                               d.c3 + (uint64_t)PV_CKPT_BIAS};
+        sa.x = d.x | (d.pk << 24) | ((uint32_t)(d.nc - 1) << 27);
+        sa.y = (uint32_t)(d.st.p - base);
+        sa.z = (uint32_t)c[0]; sa.w = (uint32_t)c[1]; sb.x = (uint32_t)c[2]; sb.y = (uint32_t)c[3];
+        sb.z = ((uint32_t)(c[0] >> 32) & 0x7Fu) | (d.d0 << 7) | ((((uint32_t)(c[1] >> 32) & 0x7Fu) | (d.d1 << 7)) << 8) |
+               ((((uint32_t)(c[2] >> 32) & 0x7Fu) | (d.d2 << 7)) << 16) | ((((uint32_t)(c[3] >> 32) & 0x7Fu) | (d.d3 << 7)) << 24);
+        sb.w = d.o;
+    }
+    __device__ bool more() const { return true; }
+    __device__ bool lit(uint32_t, uint8_t) { return true; }
+    __device__ bool op(uint32_t, uint64_t, uint32_t, uint32_t) { return true; }
+};
+
+template <bool PK, bool CP>
+__global__ void __launch_bounds__(128) pv_index_kernel(const pv_dev_cohort C, uint64_t nblk, uint32_t cs, uint32_t qs, uint4* out,
+                                                       unsigned long long* nbad) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblk) return;
+    int64_t lo = 0, hi = C.nasm;                    // the assembly: the last one whose first block is at or before i
+    while (hi - lo > 1) { const int64_t m = (lo + hi) >> 1; if (__ldg(&C.asms[m].blk_base) <= i) lo = m; else hi = m; }
+    const pv_asm_rec& R = C.asms[lo];
+    const uint64_t b = i - __ldg(&R.blk_base), nbases = __ldg(&R.nbases), bst = b << qs;
+    const uint32_t blen = (uint32_t)(nbases - bst < (1ull << qs) ? nbases - bst : (1ull << qs));
+    const uint32_t ncell = 1u << (qs - cs);
+    uint4* o = out + 2 * (i << (qs - cs));
+    const BlockRec r = block_rec<CP>(C, i, __ldg(&R.grp_base), b);
+    if (r.cache) return;                            // served from the block cache: never decoded by windows
+    int res = DEC_ERR;
+    if (CP || r.plen != (uint32_t)PV_BLEN_BAD) {
+        const uint8_t* src = C.payload + r.poff;
+        CkptSink sk{o, src, cs, ncell, 0, make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+        Dec<GlobalStream> d;
+        dec_init(d, GlobalStream{src, src + r.plen}, r.pst);
+        const RefView V{C.ref, C.ref_n, 0, 0, 0, PK ? C.pref : nullptr, C.pruns, C.pidx};
+        res = decode_events(d, GlobalTab{C.tabs + __ldg(&R.tab_off)}, V, blen, blen, sk);
+        if (res == DEC_DONE) while (sk.jn < ncell) sk.put(sk.jn++);   // the last boundary's state for the rest
+    }
+    if (res != DEC_DONE) {
+        for (uint32_t j = 0; j < ncell; j++) { o[2 * j] = make_uint4(0, 0, 0, 0); o[2 * j + 1] = make_uint4(0, 0, 0, PV_CKPT_BAD << 16); }
+        if (nbad) atomicAdd(nbad, 1ull);
     }
 }
 
@@ -1353,8 +1502,10 @@ int pv_status_to_host(const int32_t* status, int32_t* host_word, void* stream) {
     return PV_OK;
 }
 
-static uint64_t grid_of(uint32_t Q, int64_t n, int64_t W, uint64_t* total, uint64_t* bpw) {
-    *bpw = ((uint64_t)W + Q - 1) / Q + 1;
+// an item's cell: the checkpoint stride of a cohort with an index, else the block (items = (window, cell touched))
+static uint32_t cell_of(const pv_dev_cohort* c) { return c->ckpt ? 1u << c->ckpt_shift : c->Q; }
+static uint64_t grid_of(uint32_t cell, int64_t n, int64_t W, uint64_t* total, uint64_t* bpw) {
+    *bpw = ((uint64_t)W + cell - 1) / cell + 1;
     *total = (uint64_t)n * *bpw;
     return (*total + WARPS - 1) / WARPS;
 }
@@ -1363,20 +1514,20 @@ static uint64_t grid_of(uint32_t Q, int64_t n, int64_t W, uint64_t* total, uint6
 // the fused kernel below this many items (n x blocks per window), the split form from it: where they cross, measured
 // on B200 with W = 8,192 (q4k: equal at 4,608 items, fused 20 % faster at 3,072; q16k: fused 22 % faster at 2,048,
 // split 6 % faster at 4,096; a q16k item decodes a 4x longer stream, so the split form pays off sooner)
-static uint64_t split_min_items(uint32_t Q) { return Q >= 16384 ? 3072 : 4608; }
+static uint64_t split_min_items(uint32_t cell) { return cell >= 16384 ? 3072 : 4608; }
 // the form a call of `total` items takes (true: fused) and, for the split form, its items per decode warp: enough that
 // the call runs about DEC_WARPS decode warps (~21 per SM; fewer chains per warp diverge less, and beyond that many
 // warps the SMs' issue slots are full anyway; measured, 1.5 K-49 K items), at most 32
-static bool form_of(uint32_t Q, uint64_t total, uint32_t flags, uint32_t* lanes) {
+static bool form_of(uint32_t cell, uint64_t total, uint32_t flags, uint32_t* lanes) {
     const uint32_t k = (flags >> PV_WIN_DEC_LANES_SHIFT) & 63u;
     *lanes = k ? k : (uint32_t)std::min<uint64_t>(32, std::max<uint64_t>(1, (total + DEC_WARPS - 1) / DEC_WARPS));
-    return (flags & PV_WIN_FUSED) ? true : (flags & PV_WIN_SPLIT) ? false : total < split_min_items(Q);
+    return (flags & PV_WIN_FUSED) ? true : (flags & PV_WIN_SPLIT) ? false : total < split_min_items(cell);
 }
 static uint64_t plan_bytes(uint64_t total) { return (total * sizeof(Item) + 255) & ~255ull; }
 size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W) {
     if (n <= 0 || W <= 0) return 0;
     uint64_t total, bpw;
-    const uint64_t grid = grid_of(cohort->Q, n, W, &total, &bpw);
+    const uint64_t grid = grid_of(cell_of(cohort), n, W, &total, &bpw);
     return (size_t)(plan_bytes(total) + grid * cohort->Q);
 }
 
@@ -1457,19 +1608,26 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     if (W < 0 || W >= (1ll << 31)) { snprintf(g_cuda_err, sizeof g_cuda_err, "W"); return PV_EARG; }
     if (n < 0) { snprintf(g_cuda_err, sizeof g_cuda_err, "n"); return PV_EARG; }
     if (cohort->tab_max > PV_TAB_MAX_BYTES || cohort->tab_max % 16) { snprintf(g_cuda_err, sizeof g_cuda_err, "decode table size"); return PV_EARG; }
+    uint32_t qshift = 0;
+    while ((1u << qshift) < Q) qshift++;
+    if (cohort->ckpt && (cohort->ckpt_shift < 8 || cohort->ckpt_shift > qshift)) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "checkpoint stride: 256 to Q");
+        return PV_EARG;
+    }
     if (n == 0 || W == 0) return PV_OK;
+    const uint32_t cell = cell_of(cohort);
     Params P;
     P.C = *cohort; P.wasm = asm_index; P.wstart = start; P.rc = rc; P.out = out; P.status = status; P.wstatus = wstatus;
     P.out64 = out64;
     for (int k = 0; k < 5; k++) P.ids[k] = ids ? ids[k] : 0;
     P.n = (uint64_t)n; P.W = (uint64_t)W;
-    if ((uint64_t)n > (1ull << 62) / (((uint64_t)W + Q - 1) / Q + 1)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
-    const uint64_t grid = grid_of(Q, n, W, &P.total, &P.bpw);
+    if ((uint64_t)n > (1ull << 62) / (((uint64_t)W + cell - 1) / cell + 1)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
+    const uint64_t grid = grid_of(cell, n, W, &P.total, &P.bpw);
     if (grid >= (1ull << 31)) { snprintf(g_cuda_err, sizeof g_cuda_err, "too many blocks in one call"); return PV_EARG; }
     // the fused kernel for calls of few items (each warp's one chain then overlaps the others' well); the decode +
     // emission pair beyond, where several chains per decode warp amortise the decode
     if (((flags >> PV_WIN_DEC_LANES_SHIFT) & 63u) > 32) { snprintf(g_cuda_err, sizeof g_cuda_err, "decode lanes per warp: 1 to 32"); return PV_EARG; }
-    const bool fused = form_of(Q, P.total, flags, &P.dec_lanes);
+    const bool fused = form_of(cell, P.total, flags, &P.dec_lanes);
     const uint64_t need = plan_bytes(P.total) + grid * Q;
     if (!work || work_bytes < need || ((uintptr_t)work & 15)) {
         snprintf(g_cuda_err, sizeof g_cuda_err, "work buffer: %llu bytes needed, 16-byte aligned", (unsigned long long)need);
@@ -1478,12 +1636,16 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     Item* plan = (Item*)work;
     P.work = (uint8_t*)work + plan_bytes(P.total);
     P.tokens = tokens; P.apply_case = apply_case; P.force_block = (flags & PV_WIN_BLOCK_PATH) ? 1 : 0;
-    P.qshift = 0;
-    while ((1u << P.qshift) < Q) P.qshift++;
+    P.qshift = qshift;
+    P.cshift = cohort->ckpt ? cohort->ckpt_shift : qshift;
     P.tab_area = (uint32_t)((cohort->tab_max + 15) & ~15ull);
     P.pay_cap = ((Q / 32 + 32 < 160 ? 160 : Q / 32 + 32) + 15) & ~15u;
     P.narrow = W < (int64_t)Q;
-    P.span_cap = (uint32_t)(((uint64_t)(P.narrow ? W : Q) + 2 * SPAN_MARGIN + 64 + 15) & ~15ull);
+    // a slot's reference span: an item's range is at most min(W, Q) bases; from checkpoints it is about one stride,
+    // so the slot holds two strides (a longer item reads what does not fit from global memory)
+    uint64_t span = P.narrow ? (uint64_t)W : Q;
+    if (cohort->ckpt && span > 2ull * cell) span = 2ull * cell;
+    P.span_cap = (uint32_t)((span + 2 * SPAN_MARGIN + 64 + 15) & ~15ull);
     P.slot_bytes = (uint32_t)sizeof(Item) + P.tab_area + P.pay_cap + P.span_cap;
     const size_t smem = (size_t)WARPS * P.slot_bytes;
     // the emission kernel's slot: no stream, no table (its general path reads it through L1), and a span of the output
@@ -1505,16 +1667,16 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
 
 extern "C" {
 
-int pv_windows_form(uint32_t Q, int64_t n, int64_t W, uint32_t flags, int* launches, uint32_t* dec_lanes) {
+int pv_windows_form(uint32_t cell, int64_t n, int64_t W, uint32_t flags, int* launches, uint32_t* dec_lanes) {
     *launches = 0; *dec_lanes = 0;
-    if (!(Q == 1024 || Q == 2048 || Q == 4096 || Q == 16384) || n < 0 || W < 0 || ((flags >> PV_WIN_DEC_LANES_SHIFT) & 63u) > 32) {
+    if (cell < 256 || cell > 16384 || (cell & (cell - 1)) || n < 0 || W < 0 || ((flags >> PV_WIN_DEC_LANES_SHIFT) & 63u) > 32) {
         snprintf(g_cuda_err, sizeof g_cuda_err, "pv_windows_form: arguments");
         return PV_EARG;
     }
     if (n == 0 || W == 0) return PV_OK;
-    const uint64_t total = (uint64_t)n * (((uint64_t)W + Q - 1) / Q + 1);
+    const uint64_t total = (uint64_t)n * (((uint64_t)W + cell - 1) / cell + 1);
     uint32_t lanes;
-    const bool fused = form_of(Q, total, flags, &lanes);
+    const bool fused = form_of(cell, total, flags, &lanes);
     *launches = fused ? 1 : 2;
     *dec_lanes = fused ? 0 : lanes;
     return PV_OK;
@@ -1601,6 +1763,50 @@ int pv_sample_draw_coords(const int64_t* cum, const int64_t* valid, const int64_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- the checkpoint index: host side
+extern "C" size_t pv_index_bytes(uint32_t Q, uint64_t nblocks, uint32_t ckpt_shift) {
+    uint32_t qs = 0;
+    while ((1u << qs) < Q) qs++;
+    if ((1u << qs) != Q || ckpt_shift < 8 || ckpt_shift > qs || nblocks > (1ull << 40)) return 0;
+    return (size_t)(nblocks << (qs - ckpt_shift)) * sizeof(pv_ckpt);
+}
+
+extern "C" int pv_index_build(const pv_dev_cohort* cohort, uint64_t nblocks, uint32_t ckpt_shift, pv_ckpt* out, uint64_t* nbad,
+                              void* stream) {
+    static_assert(sizeof(pv_ckpt) == 32, "pv_ckpt is two 16-byte words");
+    const uint32_t Q = cohort ? cohort->Q : 0;
+    if (!cohort || !(Q == 1024 || Q == 2048 || Q == 4096 || Q == 16384) || !pv_index_bytes(Q, nblocks, ckpt_shift) || !out ||
+        ((uintptr_t)out & 15)) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_index_build: cohort, stride (256 to Q) or output (16-byte aligned)");
+        return PV_EARG;
+    }
+    if ((cohort->packed && (!cohort->pref || !cohort->pruns || !cohort->pidx)) || (cohort->compact && (!cohort->groups || !cohort->btab)) ||
+        (!cohort->packed && !cohort->ref) || (!cohort->compact && !cohort->blocks) || cohort->tab_max > PV_TAB_MAX_BYTES) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_index_build: the arrays of the cohort's resident form are missing");
+        return PV_EARG;
+    }
+    if (cohort->ref_n >= (1ull << 38)) {                // diagonals are stored in 39 bits
+        snprintf(g_cuda_err, sizeof g_cuda_err, "pv_index_build: reference longer than 2^38 bases");
+        return PV_EARG;
+    }
+    if (nblocks == 0) return PV_OK;
+    uint32_t qs = 0;
+    while ((1u << qs) < Q) qs++;
+    const unsigned grid = (unsigned)((nblocks + 127) / 128);
+    const cudaStream_t st = (cudaStream_t)stream;
+    unsigned long long* nb = (unsigned long long*)nbad;
+    const int form = (cohort->packed ? 1 : 0) | (cohort->compact ? 2 : 0);
+    switch (form) {
+    case 0: pv_index_kernel<false, false><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb); break;
+    case 1: pv_index_kernel<true, false><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb); break;
+    case 2: pv_index_kernel<false, true><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb); break;
+    default: pv_index_kernel<true, true><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb); break;
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
+    return PV_OK;
+}
 
 // ---------------------------------------------------------------- the no-allocation variant (pv_windows_noalloc)
 // Its scratch is this fixed array in device memory (PV_NOALLOC_SCRATCH_BYTES on every GPU that loads the library).

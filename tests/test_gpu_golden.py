@@ -14,10 +14,20 @@ from conftest import DATASETS, NAMES, golden_cases
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module")
-def cohorts(golden, cuda):
+# the cohorts with the default checkpoint index (stride 2048, capped at the block size), without one (every item
+# decodes its whole block), and with the smallest stride (many items per block, most starting mid-block)
+STRIDES = {"index": None, "no-index": 0, "stride-256": 256}
+
+
+@pytest.fixture(scope="module", params=list(STRIDES))
+def cohorts(golden, cuda, request):
     import panvram_b200 as P
-    return {ds: P.Cohort.open(golden["dirs"][ds], device=cuda, dataset=ds, reference=golden["ref"]) for ds in DATASETS}
+    cs = {ds: P.Cohort.open(golden["dirs"][ds], device=cuda, dataset=ds, reference=golden["ref"], checkpoint_stride=STRIDES[request.param])
+          for ds in DATASETS}
+    for c in cs.values():
+        want = 0 if STRIDES[request.param] == 0 else min(STRIDES[request.param] or 2048, c.block_size)
+        assert c.checkpoint_stride == want and c.bad_blocks == 0
+    return cs
 
 
 def _hashes(x):
@@ -116,9 +126,11 @@ def test_edge_cases(golden, cohorts, oracle_cohorts):
         c.fetch("nope", 0, 0, 1)
 
 
-def test_corrupt_payload_parity(golden, oracle, tmp_path, cuda):
+@pytest.mark.parametrize("stride", [None, 0, 256], ids=["index", "no-index", "stride-256"])
+def test_corrupt_payload_parity(golden, oracle, tmp_path, cuda, stride):
     """A payload byte flipped: per block, the GPU reports status 1 exactly where the reference decoder fails, and
-    otherwise returns exactly the reference decoder's bytes (valid-looking corruption included)."""
+    otherwise returns exactly the reference decoder's bytes (valid-looking corruption included). With a checkpoint
+    index the failing blocks are found when it is built at open; windows over any part of them report status 1."""
     import panvram_b200 as P
     raw = bytearray(open(os.path.join(golden["dirs"]["q4k"], "synthA.q4k.rr3"), "rb").read())
     ref = oracle.Reference(golden["ref"])
@@ -131,22 +143,27 @@ def test_corrupt_payload_parity(golden, oracle, tmp_path, cuda):
         d.mkdir()
         (d / "synthA.q4k.rr3").write_bytes(bytes(b))
         arc = oracle.Archive(str(d / "synthA.q4k.rr3"), ref)
-        c = P.Cohort.open(str(d), device=cuda, reference=golden["ref"])
+        c = P.Cohort.open(str(d), device=cuda, reference=golden["ref"], checkpoint_stride=stride)
         Q, n = c.block_size, arc.nbases
+        bad = 0
         for blk in range(arc.nblocks):
             s, W = blk * Q, min(Q, n - blk * Q)
             try:
                 want = arc.window(s, W, apply_case=False)
             except oracle.OracleError:
                 want = None
-            for flags in (2, 4):                            # the fused kernel, and the decode + emission pair
-                x, status = c._launch(torch.tensor([0]), torch.tensor([s]), W, None, False, False, flags=flags)
-                st = int(status.item())
-                if want is None:
-                    assert st == 1, (k, blk, flags)
-                    caught += 1
-                else:
-                    assert st == 0 and np.array_equal(x[0].cpu().numpy(), want), (k, blk, flags)
+            bad += want is None
+            # the whole block, and a window inside it that starts and ends mid-block
+            for ws, ww in ((s, W), (s + W // 3, max(1, W // 3))):
+                for flags in (2, 4):                        # the fused kernel, and the decode + emission pair
+                    x, status = c._launch(torch.tensor([0]), torch.tensor([ws]), ww, None, False, False, flags=flags)
+                    st = int(status.item())
+                    if want is None:
+                        assert st == 1, (k, blk, flags, ws, ww)
+                        caught += 1
+                    else:
+                        assert st == 0 and np.array_equal(x[0].cpu().numpy(), want[ws - s:ws - s + ww]), (k, blk, flags, ws, ww)
+        assert c.bad_blocks == (bad if c.checkpoint_stride else 0), k
     assert caught > 0
 
 

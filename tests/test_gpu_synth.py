@@ -87,12 +87,16 @@ def test_block_cache_same_output(tmp_path_factory, oracle, cuda, Q):
                 assert int(st.item()) == 0 and np.array_equal(x.cpu().numpy(), want), (Q, W, tok, co.cached_blocks)
 
 
-@pytest.mark.parametrize("Q", [1024, 2048, 4096, 16384])
-def test_synth_cohort_parity(tmp_path_factory, oracle, cuda, Q):
+@pytest.mark.parametrize("Q,stride", [(1024, None), (2048, None), (4096, None), (16384, None), (4096, 256), (16384, 512), (4096, 0),
+                                      (16384, 0)])
+def test_synth_cohort_parity(tmp_path_factory, oracle, cuda, Q, stride):
+    """Synthesizer cohorts against the oracle with the default checkpoint index, the smallest strides (long copies of
+    the structural variants span many cells, so many items own no event and one item a long one) and no index."""
     import panvram_b200 as P
     d = str(tmp_path_factory.mktemp(f"syn{Q}"))
     synth.make_cohort(d, "cfg1", Q=Q, nasm=4, scale=0.004)
-    c = P.Cohort.open(d, device=cuda, dataset=synth.dataset_of(Q))
+    c = P.Cohort.open(d, device=cuda, dataset=synth.dataset_of(Q), checkpoint_stride=stride)
+    assert c.checkpoint_stride == (min(2048, Q) if stride is None else stride) and c.bad_blocks == 0
     ref = oracle.Reference(os.path.join(d, "reference.fa"))
     arcs = [oracle.Archive(p, ref) for p in sorted(glob.glob(os.path.join(d, f"*.{synth.dataset_of(Q)}.rr3")))]
     g = torch.Generator(device=cuda).manual_seed(Q)
