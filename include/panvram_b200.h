@@ -214,6 +214,11 @@ size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W);
  * PV_WIN_SPLIT force one form; the output is the same. */
 #define PV_WIN_FUSED 2u
 #define PV_WIN_SPLIT 4u
+/* For testing the expired-wait path (status 4) without a fault: every kernel's bounded wait on its shared-memory bulk
+ * copies is made to expire - its barrier expects 16 bytes that no copy brings, and the wait's bound is short - so each
+ * item that stages copies reports PV_STATUS_WAIT and writes nothing; the kernel then completes the missing 16 bytes with
+ * one more copy and waits until every copy has landed before it returns. The context stays usable. */
+#define PV_WIN_TEST_WAIT 16u
 /* the split form's decode warps: PV_WIN_DEC_LANES(k) runs k items per warp (one per lane, k in 1..32) instead of
  * the size rule's choice; the output is the same */
 #define PV_WIN_DEC_LANES_SHIFT 8
@@ -265,14 +270,17 @@ int pv_torch_draw_geometry(int64_t n, uint64_t total, int rc_mode, int sm_count,
  * Some callers cannot call cudaMalloc or hand over a scratch buffer: a data-loading hook inside a training framework
  * whose caching allocator already owns the device memory (a direct cudaMalloc there can fail or fragment its pool),
  * or code that must not stall the device (cudaMalloc / cudaFree can synchronise it). This variant takes the same
- * inputs and outputs as pv_windows but keeps its scratch (the general path's block buffers) in a fixed array of
- * PV_NOALLOC_SCRATCH_BYTES that the library places in device memory; every GPU that loads the library holds that
- * array until the process exits. A call that would need more scratch than that returns PV_EARG (message in
- * pv_kernels_last_error()) without launching; split it into smaller calls. The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress, with that device current), so make that first call before any CUDA
- * stream capture. All calls share the one array: two calls that run on the GPU at the same time (different streams,
- * or devices sharing nothing else) must not overlap, or they race on it. Nothing in it needs to start at zero: every
- * byte of a block buffer is written before it is read. The call makes no cudaMalloc, cudaFree or other allocation. */
+ * inputs and outputs as pv_windows but keeps its scratch - the split form's plan (the decode results of every item)
+ * and the general path's block buffers - in a fixed array of PV_NOALLOC_SCRATCH_BYTES that the library places in
+ * device memory; every GPU that loads the library holds its own copy of that array until the process exits. A call
+ * that would need more scratch than that (pv_windows_work_bytes) returns PV_EARG (message in pv_kernels_last_error())
+ * without launching; split it into smaller calls. The first call on a device looks up that device's array address
+ * (cudaGetSymbolAddress, with the device current) and keeps it for later calls, so make that first call before any
+ * CUDA stream capture; the kept address assumes the device's primary context lives as long as the process (after a
+ * cudaDeviceReset, do not call this again). The calls on one device share its array: two calls on the same device
+ * that run on the GPU at the same time (on different streams) race on it and must not overlap; calls on different
+ * devices use different arrays and may. Nothing in it needs to start at zero: every byte of the plan and of a block
+ * buffer is written before it is read. The call makes no cudaMalloc, cudaFree or other allocation. */
 #define PV_NOALLOC_SCRATCH_BYTES (16u << 20)
 int pv_windows_noalloc(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
                        const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* stream);

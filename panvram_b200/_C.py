@@ -316,6 +316,7 @@ def sha256_file_bases(path):
 PV_WIN_BLOCK_PATH = 1
 PV_WIN_FUSED = 2          # force the one-kernel form
 PV_WIN_SPLIT = 4          # force the decode + emission pair
+PV_WIN_TEST_WAIT = 16     # make every kernel's bounded copy wait expire (status 4), for testing that path
 
 
 def PV_WIN_DEC_LANES(k):

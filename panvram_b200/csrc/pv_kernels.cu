@@ -32,6 +32,7 @@
 #include <stdio.h>
 
 #include <algorithm>
+#include <atomic>
 #include <utility>
 #include <type_traits>
 
@@ -78,6 +79,7 @@ struct __align__(16) Item {
     int64_t cst;            // the current diagonal c << 1 | dir where the decode starts (the spans follow it)
     uint32_t co;            // the block offset where the decode starts
     uint32_t jc, wx0, wx1;  // its cell of the block; the window's bytes in the block [wx0, wx1)
+    uint4 landing;          // 16 bytes a bulk copy may target (the expired-wait test's completing copy)
     Op ops[OPS_CAP];
     uint8_t lits[LIT_CAP];
     int32_t runs[2 * RUN_CAP];   // window-relative [start, end), clipped to the item's range
@@ -91,6 +93,7 @@ struct Params {
     uint64_t n, W, bpw, total;
     uint32_t slot_bytes, tab_area, pay_cap, span_cap;   // a warp's shared slot: Item | table | payload | reference span
     int tokens, apply_case, force_block;
+    int test_wait;                 // PV_WIN_TEST_WAIT: every slot's barrier expects 16 bytes more than its copies bring
     uint32_t qshift;               // log2 of the block size
     int narrow;                    // windows shorter than a block: stage only the span under the output range
     int64_t* out64;                // token-id output (pv_windows_ids): int64 [n, W]; then `out` is unused
@@ -785,6 +788,8 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                  :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
 constexpr uint32_t WAIT_SPINS = 1u << 22;   // bounded wait on a bulk copy (milliseconds); then status 4
+constexpr uint32_t TEST_WAIT_SPINS = 1u << 10;   // the same under PV_WIN_TEST_WAIT, so the test's wait expires soon
+constexpr uint32_t DRAIN_SPINS = 1u << 24;  // after an expired wait: the bound on waiting for the copies to land
 
 // Programmatic dependent launch: the window kernels are launched so that their CTAs may be scheduled while the kernel
 // before them on the stream is still running; each waits here, before it reads anything that kernel wrote, until it
@@ -982,7 +987,7 @@ __device__ void item_stage(const Params& P, uint8_t* slot, uint32_t bar) {
     it->staged = pe - pa <= (uintptr_t)P.pay_cap;
     const uint32_t span_tma = PK ? 0u : it->span_len;
     mbar_init(bar);
-    mbar_expect(bar, it->tab_bytes + (it->staged ? (uint32_t)(pe - pa) : 0u) + span_tma);
+    mbar_expect(bar, it->tab_bytes + (it->staged ? (uint32_t)(pe - pa) : 0u) + span_tma + (P.test_wait ? 16u : 0u));
     bulk_g2s(smem_addr(slot_tab(P, slot)), C.tabs + it->tab_off, it->tab_bytes, bar);
     if (it->staged) bulk_g2s(smem_addr(slot_pay(P, slot)), (const void*)pa, (uint32_t)(pe - pa), bar);
     if (span_tma) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + ra, span_tma, bar);
@@ -1010,19 +1015,27 @@ __device__ void stage_span_packed(const Params& P, uint8_t* slot, int lane) {
     }
 }
 
+// lane 0: wait, bounded, for the slot's bulk copies to complete on `bar` (phase 0). If the wait expires the window
+// reports status 4 (the reference's expired wait, pv_cuda.cu:26,78) and the item is dropped, and lane 0 then waits on,
+// bounded again, until the copies have landed: a CTA must not leave while a copy still targets its shared memory.
+// Under PV_WIN_TEST_WAIT the barrier expects 16 bytes that no copy brings, so the first wait expires for sure; a
+// 16-byte copy issued then completes them, and the second wait ends once every copy, that one included, has landed.
+__device__ bool slot_wait(const Params& P, Item* it, uint32_t bar) {
+    const uint32_t lim = P.test_wait ? TEST_WAIT_SPINS : WAIT_SPINS;
+    for (uint32_t k = 0; k < lim; k++)
+        if (mbar_try(bar, 0)) return true;
+    report(P, it->w, PV_STATUS_WAIT);
+    it->state = ST_ERR;
+    if (P.test_wait) bulk_g2s(smem_addr(&it->landing), P.C.tabs, 16, bar);
+    for (uint32_t k = 0; k < DRAIN_SPINS && !mbar_try(bar, 0); k++) {}
+    return false;
+}
+
 // lane 0 of the item's warp: wait (bounded) for the slot's copies, then decode the block keeping the window's ops
 template <bool PK>
 __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
     Item* it = slot_item(slot);
-    uint32_t spins = 0;
-    while (!mbar_try(bar, 0)) {
-        if (++spins == WAIT_SPINS) {                           // report, then wait (bounded) for the copies to land
-            report(P, it->w, PV_STATUS_WAIT);
-            it->state = ST_ERR;
-            for (uint32_t k = 0; k < WAIT_SPINS && !mbar_try(bar, 0); k++) {}
-            return;
-        }
-    }
+    if (!slot_wait(P, it, bar)) return;
     if (P.force_block || !it->staged) { it->state = ST_HEAVY; return; }   // (a stream longer than the slot: uncached long block)
     WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
     const uint32_t sp = smem_addr(slot_pay(P, slot)) + (uint32_t)((uintptr_t)(P.C.payload + it->poff) & 15);
@@ -1246,22 +1259,12 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
             item_span(P, it, true, P.span_cap);
             const uint32_t span_tma = PK ? 0u : it->span_len;
             mbar_init(bar);
-            mbar_expect(bar, span_tma);
+            mbar_expect(bar, span_tma + (P.test_wait ? 16u : 0u));
             if (span_tma) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + it->span_lo, span_tma, bar);
         }
         __syncwarp();
         if (PK) stage_span_packed(P, slot, lane);
-        if (lane == 0) {
-            uint32_t spins = 0;
-            while (!mbar_try(bar, 0)) {
-                if (++spins == WAIT_SPINS) {
-                    report(P, it->w, PV_STATUS_WAIT);
-                    it->state = ST_ERR;
-                    for (uint32_t k = 0; k < WAIT_SPINS && !mbar_try(bar, 0); k++) {}
-                    break;
-                }
-            }
-        }
+        if (lane == 0) slot_wait(P, it, bar);
     }
     __syncwarp();
     if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
@@ -1636,6 +1639,7 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     Item* plan = (Item*)work;
     P.work = (uint8_t*)work + plan_bytes(P.total);
     P.tokens = tokens; P.apply_case = apply_case; P.force_block = (flags & PV_WIN_BLOCK_PATH) ? 1 : 0;
+    P.test_wait = (flags & PV_WIN_TEST_WAIT) ? 1 : 0;
     P.qshift = qshift;
     P.cshift = cohort->ckpt ? cohort->ckpt_shift : qshift;
     P.tab_area = (uint32_t)((cohort->tab_max + 15) & ~15ull);
@@ -1814,7 +1818,7 @@ extern "C" int pv_index_build(const pv_dev_cohort* cohort, uint64_t nblocks, uin
 // cudaGetSymbolAddress and passed to the kernel like any other scratch pointer.
 namespace {
 static __device__ __align__(256) uint8_t g_noalloc_scratch[PV_NOALLOC_SCRATCH_BYTES];
-void* g_noalloc_addr[64] = {nullptr};
+std::atomic<void*> g_noalloc_addr[64];      // per device, filled by its first call (every thread would store the same)
 }  // namespace
 
 extern "C" int pv_windows_noalloc(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
@@ -1831,15 +1835,15 @@ extern "C" int pv_windows_noalloc(const pv_dev_cohort* cohort, const int64_t* as
         snprintf(g_cuda_err, sizeof g_cuda_err, "pv_windows_noalloc: current device: %s", e != cudaSuccess ? cudaGetErrorString(e) : "index >= 64");
         return PV_ECUDA;
     }
-    if (!g_noalloc_addr[dev]) {                              // set-up, once per device, with that device current
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p) {
+    void* addr = g_noalloc_addr[dev].load(std::memory_order_acquire);
+    if (!addr) {                                             // set-up, once per device, with that device current
+        e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+        if (e != cudaSuccess || !addr) {
             snprintf(g_cuda_err, sizeof g_cuda_err, "pv_windows_noalloc: scratch address: %s", cudaGetErrorString(e));
             return PV_ECUDA;
         }
-        g_noalloc_addr[dev] = p;
+        g_noalloc_addr[dev].store(addr, std::memory_order_release);
     }
-    return pv_windows_ex(cohort, asm_index, start, n, W, rc, tokens, apply_case, 0u, out, status, nullptr, g_noalloc_addr[dev],
+    return pv_windows_ex(cohort, asm_index, start, n, W, rc, tokens, apply_case, 0u, out, status, nullptr, addr,
                          (size_t)PV_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -1,8 +1,9 @@
 """pv_windows_noalloc: the window decode for callers that cannot allocate device memory (for example a data-loading
 hook inside a training framework whose allocator owns the GPU's memory). It keeps its scratch in a fixed array inside
-the library instead of a caller buffer. Here it is called through the C ABI, twice in a row on different windows, and
-each result (bytes and status) must equal the ordinary entry point's exactly - the path is integer work, so the
-tolerance is zero. This file sorts last so that a run stopping at its first failure has run every other test."""
+the library instead of a caller buffer. Here it is called through the C ABI three times in a row on different windows,
+and each result (bytes and status) must equal the ordinary entry point's exactly - the path is integer work, so the
+tolerance is zero. The third call is large enough for the two-kernel split form, whose plan also lives in the fixed
+array. This file sorts last so that a run stopping at its first failure has run every other test."""
 import ctypes
 import os
 
@@ -36,8 +37,11 @@ def test_noalloc_matches_windows_twice(golden, cuda):
     c = _cohort(golden, cuda)
     rng = np.random.default_rng(2026)
     nb = [c.info(i)["bases"] for i in range(len(NAMES))]
-    for call, (W, tokens) in enumerate(((3000, False), (777, True))):
-        n = 600
+    # two small calls (the one-kernel form), then one of 1,500 x 4 items (the split form, whose plan of every item's
+    # decode results also lives in the fixed array)
+    for call, (n, W, tokens) in enumerate(((600, 3000, False), (600, 777, True), (1500, 3000, False))):
+        if call == 2:
+            assert _C.windows_form(c.item_cell, n, W)[0] == 2 and lib.pv_windows_work_bytes(ctypes.byref(c._devc), n, W) <= 16 << 20
         a = rng.integers(0, len(NAMES), n)
         s = np.array([rng.integers(0, nb[k] - W + 1) for k in a])
         asm = torch.from_numpy(a.astype(np.int64)).to(cuda)
