@@ -235,6 +235,21 @@ int pv_windows_ids(const pv_dev_cohort* cohort, const int64_t* asm_index, const 
                    const uint8_t* rc, const int64_t* ids, int64_t* out, int32_t* status, void* work, size_t work_bytes,
                    void* stream);
 
+/* Work items of a pv_windows call with these sizes: (window, cell) pairs, the cell being the cohort's checkpoint stride
+ * (or its block without an index); n x (ceil(W / cell) + 1), some of them empty. */
+size_t pv_windows_items(const pv_dev_cohort* cohort, int64_t n, int64_t W);
+/* pv_windows_ex without a per-window status, and with a per-item trace (no counterpart in the reference, which has
+ * none; its logs time the decode ad hoc with clock64 / %globaltimer): trace (device uint64 [trace_records x 8],
+ * trace_records >= pv_windows_items, zeroed by the caller) receives for item i the %globaltimer time (ns) at which it
+ * reached each phase - word 0 start, 1 located (block, checkpoint, lower-case runs), 2 its decode starts (fused
+ * kernel: after its staged copies landed), 3 decoded, 4 taken by the emission kernel (split form), 5 its reference
+ * span staged there, 6 its bytes written - and in word 7: SM | item state << 8 | form << 12 (1 fused, 2 split) | decode
+ * from a checkpoint << 14 | ops << 16 | literal bytes << 32 | bases decoded << 48. A phase the item did not reach
+ * stays 0. Same output as pv_windows_ex; the timer reads add a little time. */
+int pv_windows_trace(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
+                     const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, void* work,
+                     size_t work_bytes, uint64_t* trace, size_t trace_records, void* stream);
+
 /* The coordinate arithmetic of Cohort.sample between its draws and its pv_windows call (panvram/cohort.py:177-189 and 193-194,
  * there six torch ops), as one launch. For window i: contig k = the first index with cum[k] > u[i] (searchsorted
  * right; u[i] in [0, cum[nctg-1]), cum the inclusive prefix sum of valid[], valid[k] = max(0, contig length - W + 1)),

@@ -106,6 +106,8 @@ for _name, _res, _args in (
                                          _P, _P]),
         ("pv_torch_draw_geometry", _I32, [_I64, _U64, _I32, _I32, _I32, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)]),
         ("pv_index_bytes", _SZ, [_U32, _U64, _U32]),
+        ("pv_windows_items", _SZ, [ctypes.POINTER(DevCohort), _I64, _I64]),
+        ("pv_windows_trace", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _U32, _P, _P, _P, _SZ, _P, _SZ, _P]),
         ("pv_index_build", _I32, [ctypes.POINTER(DevCohort), _U64, _U32, _P, _P, _P])):
     _f = getattr(_lib, _name)
     _f.restype, _f.argtypes = _res, _args
@@ -446,6 +448,62 @@ def coords_from_host(asm, start, rc, device):
 
 
 PV_CKPT_BAD = 1
+TRACE_PHASES = ("start", "located", "decode_start", "decoded", "emit_start", "staged", "emitted")
+
+
+def windows_trace(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, flags=0):
+    """windows_cuda with the per-item %globaltimer trace (pv_windows_trace) -> (out, status, trace): trace a numpy
+    uint64 [items, 8] array, read after the call (one sync)."""
+    n, W = int(wasm.numel()), int(W)
+    device = wasm.device
+    items = int(_lib.pv_windows_items(ctypes.byref(dev), n, W))
+    out = torch.empty((n, W), dtype=torch.uint8, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    trace = torch.zeros((max(1, items), 8), dtype=torch.int64, device=device)
+    work, need = work_buffer(dev, device, n, W)
+    code = _lib.pv_windows_trace(ctypes.byref(dev), wasm.data_ptr(), wstart.data_ptr(), n, W, rc.data_ptr() if rc is not None else None,
+                                 int(bool(tokens)), int(bool(apply_case)), int(flags), out.data_ptr(), status.data_ptr(),
+                                 work.data_ptr() if work is not None else None, need, trace.data_ptr(), items,
+                                 torch.cuda.current_stream(device).cuda_stream)
+    if code:
+        raise RuntimeError("panvram_b200 traced window launch: " + (_lib.pv_kernels_last_error() or b"").decode())
+    return out, status, trace[:items].cpu().numpy().view(np.uint64)
+
+
+def trace_summary(trace):
+    """Per-phase durations (ns) of the items that were decoded (state 1 = decoded and emitted): mean, median, p99 and
+    max of each phase, the items' span from the call's first start to their end, and the decode's bases and ops."""
+    t = trace.astype(np.int64)
+    info = trace[:, 7]
+    state = (info >> np.uint64(8)) & np.uint64(15)
+    form = (info >> np.uint64(12)) & np.uint64(3)
+    ok = (state == 1) & (t[:, 6] > 0)
+    r = {"items": int(len(t)), "decoded": int(ok.sum())}
+    if not ok.any():
+        return r
+    t, info, form = t[ok], info[ok], form[ok]
+    t0 = t[:, 0][t[:, 0] > 0].min()
+    split = form == 2
+
+    def stats(x):
+        x = np.asarray(x, dtype=np.float64)
+        return {"mean": float(x.mean()), "p50": float(np.median(x)), "p99": float(np.percentile(x, 99)), "max": float(x.max())}
+    r["locate_ns"] = stats(t[:, 1] - t[:, 0])
+    r["wait_ns"] = stats(t[:, 2] - t[:, 1])
+    r["decode_ns"] = stats(t[:, 3] - t[:, 2])
+    emit0 = np.where(split, t[:, 5], t[:, 3])
+    r["emit_ns"] = stats(t[:, 6] - emit0)
+    if split.any():
+        r["emit_queue_ns"] = stats((t[:, 4] - t[:, 3])[split])
+        r["emit_stage_ns"] = stats((t[:, 5] - t[:, 4])[split])
+    r["end_ns"] = stats(t[:, 6] - t0)
+    r["call_ns"] = float(t[:, 6].max() - t0)
+    r["bases_decoded"] = stats(info >> np.uint64(48))
+    r["ops"] = stats((info >> np.uint64(16)) & np.uint64(0xFFFF))
+    r["sms"] = int(len(np.unique(info & np.uint64(0xFF))))
+    return r
+
+
 
 
 def index_build(dev, nblocks, ckpt_shift, device):

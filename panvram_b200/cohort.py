@@ -353,6 +353,21 @@ class Cohort:
                 raise RuntimeError(STATUS_TEXT.format(s))
         return out
 
+    def trace_windows(self, asm, start, W, reverse_complement=None, tokens=False, flags=0):
+        """windows() with a per-item trace of the kernels (pv_windows_trace: %globaltimer at every phase of every work
+        item) -> (windows, status, summary dict of the phase times, the raw trace [items, 8]). For measurement; one
+        sync. flags: PV_WIN_* (e.g. _C.PV_WIN_FUSED / PV_WIN_SPLIT to trace one kernel form)."""
+        dev = self.device
+        with torch.cuda.device(dev):
+            asm = torch.as_tensor(asm).to(dev, torch.int64).contiguous()
+            start = torch.as_tensor(start).to(dev, torch.int64).contiguous()
+            rc = None
+            if reverse_complement is not None:
+                rc = torch.as_tensor(reverse_complement)
+                rc = (rc.view(torch.uint8) if rc.dtype == torch.bool else rc).to(dev, torch.uint8).contiguous()
+            x, status, tr = _C.windows_trace(self._devc, asm, start, int(W), rc, tokens, True, flags | self.launch_flags)
+        return x, int(status.item()), _C.trace_summary(tr), tr
+
     def _draw(self, n, W, generator, reverse_complement, tokens, return_coords, status=None, rng=None):
         """The sample() sequence without the host check: (windows, coords or None, status tensor). The draws are the
         reference's (torch.randint over all valid starts, then torch.rand for the strand, on the generator's device):

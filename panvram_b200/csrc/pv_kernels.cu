@@ -80,6 +80,7 @@ struct __align__(16) Item {
     uint32_t co;            // the block offset where the decode starts
     uint32_t jc, wx0, wx1;  // its cell of the block; the window's bytes in the block [wx0, wx1)
     uint4 landing;          // 16 bytes a bulk copy may target (the expired-wait test's completing copy)
+    uint64_t idx;           // its index in the call (the trace record it writes)
     Op ops[OPS_CAP];
     uint8_t lits[LIT_CAP];
     int32_t runs[2 * RUN_CAP];   // window-relative [start, end), clipped to the item's range
@@ -100,8 +101,26 @@ struct Params {
     int64_t ids[5];                // the ids of tokens 0..4
     uint32_t dec_lanes;            // split form: items per decode warp (one per lane, lanes 0 .. dec_lanes - 1)
     uint32_t cshift;               // log2 of an item's cell: the checkpoint stride, or the block size without an index
+    uint64_t* trace;               // pv_windows_trace: 8 words per item, or NULL
 };
 constexpr uint64_t NO_CK = ~0ull;
+
+// The trace (pv_windows_trace): per item, %globaltimer (ns) when it reaches each phase - 0 start, 1 located (block,
+// checkpoint, case runs), 2 its decode starts (the fused kernel: its slot's copies have landed), 3 decoded, 4 the
+// emission kernel takes it (split form), 5 its span is staged there, 6 emitted - and word 7: SM | state << 8 | form
+// << 12 (1 fused, 2 split) | from a checkpoint << 14 | ops << 16 | literals << 32 | decoded bases << 48.
+__device__ __forceinline__ uint64_t gtime() { uint64_t t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); return t; }
+__device__ __forceinline__ void trace_at(const Params& P, uint64_t item, int k) { if (P.trace) P.trace[item * 8 + k] = gtime(); }
+template <class It>
+__device__ __forceinline__ void trace_done(const Params& P, const It* it, int form) {
+    if (!P.trace) return;
+    uint32_t sm;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+    P.trace[it->idx * 8 + 6] = gtime();
+    const uint64_t dec = it->ox1 > it->co ? it->ox1 - it->co : 0;
+    P.trace[it->idx * 8 + 7] = (uint64_t)(sm & 0xFF) | ((uint64_t)(it->state & 15) << 8) | ((uint64_t)form << 12) |
+                               ((uint64_t)(it->ck != ~0ull) << 14) | ((uint64_t)it->nops << 16) | ((uint64_t)it->nlits << 32) | (dec << 48);
+}
 
 // status bits into the call's word and, when asked, into the window's byte (4-byte aligned, padded array)
 __device__ __forceinline__ void report(const Params& P, uint64_t w, int bits) {
@@ -822,6 +841,7 @@ __device__ __forceinline__ RefView slot_ref(const Params& P, uint8_t* slot) {
 __device__ bool item_locate(const Params& P, uint64_t item, Item* it) {
     it->state = ST_IDLE;
     if (item >= P.total) return false;
+    it->idx = item;
     const uint64_t w = item < 0xFFFFFFFFull ? (uint64_t)((uint32_t)item / (uint32_t)P.bpw) : item / P.bpw, j = item - w * P.bpw;
     const int64_t a = P.wasm[w], s = P.wstart[w];
     const pv_dev_cohort& C = P.C;
@@ -1036,6 +1056,7 @@ template <bool PK>
 __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
     Item* it = slot_item(slot);
     if (!slot_wait(P, it, bar)) return;
+    trace_at(P, it->idx, 2);
     if (P.force_block || !it->staged) { it->state = ST_HEAVY; return; }   // (a stream longer than the slot: uncached long block)
     WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
     const uint32_t sp = smem_addr(slot_pay(P, slot)) + (uint32_t)((uintptr_t)(P.C.payload + it->poff) & 15);
@@ -1044,6 +1065,7 @@ __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
     if (it->ck != NO_CK) { dec_init_ck(d, SmemStream{sp, sp + it->plen}, P.C.ckpt + it->ck); stop = it->ox1; }
     else dec_init(d, SmemStream{sp, sp + it->plen}, it->pst);
     const int r = decode_events(d, SmemTab{smem_addr(slot_tab(P, slot))}, slot_ref<PK>(P, slot), it->blen, stop, sk);
+    trace_at(P, it->idx, 3);
     it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     if (r == DEC_DONE) it->state = ST_OK;
     else if (r == DEC_ABORT) it->state = ST_HEAVY;
@@ -1119,7 +1141,10 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constan
     Item* it = slot_item(slot);
     const uint64_t item = (uint64_t)blockIdx.x * WARPS + warp;
     const uint32_t bar = smem_addr(&bars[warp]);
-    if (lane == 0) item_locate(P, item, it);
+    if (lane == 0) {
+        if (item < P.total) trace_at(P, item, 0);
+        item_locate(P, item, it);
+    }
     __syncwarp();
     if (it->state == ST_LOCATED) {
         item_block<CP>(P, it, lane);
@@ -1127,6 +1152,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constan
         if (lane == 0) {
             if (P.C.ckpt && it->state == ST_LOCATED) item_ckpt(P, it);
             if (it->state == ST_LOCATED || it->state == ST_CACHED) item_runs(P, it);
+            trace_at(P, it->idx, 1);
         }
         __syncwarp();
         if (it->state == ST_LOCATED) {
@@ -1140,11 +1166,16 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constan
     __syncwarp();
     if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
     else if (it->state == ST_CACHED) emit_cached(P, it, lane);
+    __syncwarp();
+    if (lane == 0 && item < P.total && it->state != ST_HEAVY) trace_done(P, it, 1);
     __syncthreads();
     uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
     for (int t = 0; t < WARPS; t++) {
         uint8_t* sl = (uint8_t*)smem_raw + (size_t)t * P.slot_bytes;
-        if (slot_item(sl)->state == ST_HEAVY) heavy_item<PK, false>(P, sl, buf, hops);
+        if (slot_item(sl)->state == ST_HEAVY) {
+            heavy_item<PK, false>(P, sl, buf, hops);
+            if (threadIdx.x == 0) trace_done(P, slot_item(sl), 1);
+        }
     }
 }
 
@@ -1207,10 +1238,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
     const uint64_t i = (uint64_t)blockIdx.x * P.dec_lanes + threadIdx.x;
     if (i >= P.total) return;
     Item* it = plan + i;
+    trace_at(P, i, 0);
     if (!item_locate(P, i, it)) return;
     item_block_lane<CP>(P, it);
     if (P.C.ckpt && it->state == ST_LOCATED) item_ckpt(P, it);
     if (it->state == ST_LOCATED || it->state == ST_CACHED) item_runs(P, it);
+    trace_at(P, i, 1);
     if (it->state != ST_LOCATED) return;
     item_span(P, it, false, ~0ull);              // (L2 only: any length)
     const pv_dev_cohort& C = P.C;
@@ -1224,7 +1257,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
     if (it->ck != NO_CK) { dec_init_ck(d, GlobalStream{src, src + it->plen}, C.ckpt + it->ck); stop = it->ox1; }
     else dec_init(d, GlobalStream{src, src + it->plen}, it->pst);
     const RefView R{C.ref, C.ref_n, 0, 0, 0, PK ? C.pref : nullptr, C.pruns, C.pidx};
+    trace_at(P, i, 2);
     const int r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, stop, sk);
+    trace_at(P, i, 3);
     it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     if (r == DEC_DONE) it->state = ST_OK;
     else if (r == DEC_ABORT) it->state = ST_HEAVY;
@@ -1243,6 +1278,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
     const uint64_t item = (uint64_t)blockIdx.x * WARPS + warp;
     const uint32_t bar = smem_addr(&bars[warp]);
     if (item < P.total) {
+        if (lane == 0) trace_at(P, item, 4);
         const uint4* src = (const uint4*)(plan + item);
         uint4* dst = (uint4*)it;
         for (uint32_t k = lane; k < sizeof(Item) / 16; k += 32) dst[k] = src[k];
@@ -1264,16 +1300,21 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
         }
         __syncwarp();
         if (PK) stage_span_packed(P, slot, lane);
-        if (lane == 0) slot_wait(P, it, bar);
+        if (lane == 0 && slot_wait(P, it, bar)) trace_at(P, item, 5);
     }
     __syncwarp();
     if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
     else if (it->state == ST_CACHED) emit_cached(P, it, lane);
+    __syncwarp();
+    if (lane == 0 && item < P.total && it->state != ST_HEAVY && it->state != ST_IDLE) trace_done(P, it, 2);
     __syncthreads();
     uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
     for (int t = 0; t < WARPS; t++) {
         uint8_t* sl = (uint8_t*)smem_raw + (size_t)t * P.slot_bytes;
-        if (slot_item(sl)->state == ST_HEAVY) heavy_item<PK, true>(P, sl, buf, hops);
+        if (slot_item(sl)->state == ST_HEAVY) {
+            heavy_item<PK, true>(P, sl, buf, hops);
+            if (threadIdx.x == 0) trace_done(P, slot_item(sl), 2);
+        }
     }
 }
 
@@ -1599,7 +1640,8 @@ static cudaError_t launch_split(int form, uint64_t total, uint64_t grid, size_t 
 
 static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
                           const uint8_t* rc, int tokens, int apply_case, uint32_t flags, uint8_t* out, int64_t* out64,
-                          const int64_t* ids, int32_t* status, uint8_t* wstatus, void* work, size_t work_bytes, void* stream) {
+                          const int64_t* ids, int32_t* status, uint8_t* wstatus, void* work, size_t work_bytes, void* stream,
+                          uint64_t* trace = nullptr, size_t trace_records = 0) {
     const uint32_t Q = cohort->Q;
     if ((cohort->packed && (!cohort->pref || !cohort->pruns || !cohort->pidx)) ||
         (cohort->compact && (!cohort->groups || !cohort->btab || !cohort->bexc)) || (!cohort->packed && !cohort->ref) ||
@@ -1636,6 +1678,11 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
         snprintf(g_cuda_err, sizeof g_cuda_err, "work buffer: %llu bytes needed, 16-byte aligned", (unsigned long long)need);
         return PV_EARG;
     }
+    if (trace && (trace_records < P.total || ((uintptr_t)trace & 7))) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "trace: %llu records of 8 words needed", (unsigned long long)P.total);
+        return PV_EARG;
+    }
+    P.trace = trace;
     Item* plan = (Item*)work;
     P.work = (uint8_t*)work + plan_bytes(P.total);
     P.tokens = tokens; P.apply_case = apply_case; P.force_block = (flags & PV_WIN_BLOCK_PATH) ? 1 : 0;
@@ -1691,6 +1738,21 @@ int pv_windows_ex(const pv_dev_cohort* cohort, const int64_t* asm_index, const i
                   size_t work_bytes, void* stream) {
     return launch_windows(cohort, asm_index, start, n, W, rc, tokens, apply_case, flags, out, nullptr, nullptr, status, wstatus,
                           work, work_bytes, stream);
+}
+
+size_t pv_windows_items(const pv_dev_cohort* cohort, int64_t n, int64_t W) {
+    if (!cohort || n <= 0 || W <= 0) return 0;
+    uint64_t total, bpw;
+    grid_of(cell_of(cohort), n, W, &total, &bpw);
+    return (size_t)total;
+}
+
+int pv_windows_trace(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,
+                     int tokens, int apply_case, uint32_t flags, uint8_t* out, int32_t* status, void* work, size_t work_bytes,
+                     uint64_t* trace, size_t trace_records, void* stream) {
+    if (!trace) { snprintf(g_cuda_err, sizeof g_cuda_err, "pv_windows_trace: the trace array"); return PV_EARG; }
+    return launch_windows(cohort, asm_index, start, n, W, rc, tokens, apply_case, flags, out, nullptr, nullptr, status, nullptr,
+                          work, work_bytes, stream, trace, trace_records);
 }
 
 int pv_windows_ids(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,

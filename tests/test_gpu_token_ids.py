@@ -42,3 +42,4 @@ def test_token_ids_equal_the_two_pass_map(cohort, cuda):
 def test_token_ids_refuses_a_wrong_count(cohort, cuda):
     with pytest.raises(ValueError):
         cohort.windows(torch.zeros(1, dtype=torch.int64), torch.zeros(1, dtype=torch.int64), 10, token_ids=(1, 2, 3))
+
