@@ -62,7 +62,9 @@ def build_encoder(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    # the reference checkout: $PANVRAM_REFERENCE, else a directory named "reference" beside this repository
+    ap.add_argument("--reference", default=os.environ.get("PANVRAM_REFERENCE") or
+                    os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference"))
     ap.add_argument("--cuda", action="store_true")
     ap.add_argument("-v", action="store_true")
     a = ap.parse_args()

@@ -104,7 +104,7 @@ class Cohort:
         self.launch_flags = 0
         if block_cache:
             self._build_block_cache(pools)
-        self._index, self.checkpoint_stride, self.bad_blocks = None, 0, 0
+        self._ckpt, self.checkpoint_stride, self.bad_blocks = None, 0, 0
         stride = self.CHECKPOINT_STRIDE if checkpoint_stride is None else int(checkpoint_stride)
         if stride:
             self._build_index(min(stride, core.Q))
@@ -121,8 +121,8 @@ class Cohort:
         shift = stride.bit_length() - 1
         asms = self._dev["asms"].cpu().numpy().view(np.uint64).reshape(-1, 8)
         nblocks = int(asms[:, 2].sum())
-        self._index, self.bad_blocks = _C.index_build(self._devc, nblocks, shift, self.device)
-        self._devc.ckpt, self._devc.ckpt_shift = self._index.data_ptr(), shift
+        self._ckpt, self.bad_blocks = _C.index_build(self._devc, nblocks, shift, self.device)
+        self._devc.ckpt, self._devc.ckpt_shift = self._ckpt.data_ptr(), shift
         self.checkpoint_stride = stride
 
     @property
@@ -281,7 +281,7 @@ class Cohort:
         r = {"P": nb("payload"), "blocks": nb("blocks", "groups", "btab", "bexc"), "tab": nb("tabs"), "low": nb("low"),
              "ref": nb("ref_padded", "pref", "pruns", "pidx"), "asm": nb("asms"),
              "cache": self._cache.numel() if self._cache is not None else 0,
-             "index": self._index.numel() if self._index is not None else 0}
+             "index": self._ckpt.numel() if self._ckpt is not None else 0}
         r["total"] = sum(r.values())
         return r
 

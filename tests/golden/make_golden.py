@@ -43,7 +43,9 @@ def mutations(raw):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    # the reference checkout: $PANVRAM_REFERENCE, else a directory named "reference" beside this repository
+    ap.add_argument("--reference", default=os.environ.get("PANVRAM_REFERENCE") or
+                    os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))), "reference"))
     a = ap.parse_args()
     sys.path.insert(0, os.path.join(a.reference, "tests"))
     import synth  # the reference's own deterministic generator
