@@ -132,7 +132,8 @@ def test_loader_fast_path(q16k, extra):
             assert np.array_equal(lb, want_text[:, 1:])
         else:
             assert np.array_equal(lb[:, :-1], want_text[:, 1:]) and (lb[:, -1] == 0).all()
-        assert (b["loss_mask"].cpu().numpy() == 1).all()        # no end-of-document id inside a document, no padding
+        lm = b["loss_mask"].cpu().numpy()                       # no end-of-document id inside a document; without the
+        assert (lm[:, :S - 1 + extra] == 1).all() and (lm[:, -1] == extra).all()   # extra token the last label is padding
         assert np.array_equal(b["position_ids"].cpu().numpy(), np.broadcast_to(np.arange(S), (len(samples), S)))
 
 
