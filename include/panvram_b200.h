@@ -115,6 +115,9 @@ typedef struct pv_dev_cohort {
     const pv_ckpt* ckpt;         /* [pooled blocks << (log2 Q - ckpt_shift)] */
     uint32_t ckpt_shift;         /* log2 of the stride S (8 <= ckpt_shift <= log2 Q) */
     uint32_t pad2;
+    /* per pooled block, its assembly's first lower-case run (index from the assembly's low_base) that ends after the
+     * block's start (pv_index_build), or NULL: then the window kernels binary-search the runs */
+    const uint32_t* brun;
 } pv_dev_cohort;
 
 /* Block table word 0 of a block served from pv_dev_cohort.cache: cache slot | PV_BLOCK_CACHED << 40 (the payload
@@ -307,8 +310,10 @@ int pv_windows_noalloc(const pv_dev_cohort* cohort, const int64_t* asm_index, co
 size_t pv_index_bytes(uint32_t Q, uint64_t nblocks, uint32_t ckpt_shift);
 /* Decode every block of the cohort once on the device (blocks served from the block cache are skipped) and write its
  * checkpoints into out (pv_index_bytes bytes, 16-byte aligned, device). cohort->ckpt is ignored. *nbad (device uint64,
- * zeroed by the caller, or NULL) counts the blocks that failed. Asynchronous on `stream`. */
-int pv_index_build(const pv_dev_cohort* cohort, uint64_t nblocks, uint32_t ckpt_shift, pv_ckpt* out, uint64_t* nbad, void* stream);
+ * zeroed by the caller, or NULL) counts the blocks that failed. brun (device uint32 [nblocks], or NULL) receives the
+ * blocks' first lower-case runs (pv_dev_cohort.brun). Asynchronous on `stream`. */
+int pv_index_build(const pv_dev_cohort* cohort, uint64_t nblocks, uint32_t ckpt_shift, pv_ckpt* out, uint64_t* nbad, uint32_t* brun,
+                   void* stream);
 
 /* ---- device: the whole-assembly checks (Cohort.check_full / fasta, panvram/cohort.py:224-234, whose FASTA rebuild
  * and XXH3 run on the host in the reference, pv_core.cpp:138-176) ---- */

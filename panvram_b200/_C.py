@@ -38,7 +38,7 @@ class DevCohort(ctypes.Structure):
                 ("pref", ctypes.c_void_p), ("pruns", ctypes.c_void_p), ("pidx", ctypes.c_void_p), ("pnruns", ctypes.c_uint64),
                 ("groups", ctypes.c_void_p), ("btab", ctypes.c_void_p), ("bexc", ctypes.c_void_p),
                 ("packed", ctypes.c_uint32), ("compact", ctypes.c_uint32),
-                ("ckpt", ctypes.c_void_p), ("ckpt_shift", ctypes.c_uint32), ("pad2", ctypes.c_uint32)]
+                ("ckpt", ctypes.c_void_p), ("ckpt_shift", ctypes.c_uint32), ("pad2", ctypes.c_uint32), ("brun", ctypes.c_void_p)]
 
 
 class HostPools(ctypes.Structure):
@@ -108,7 +108,7 @@ for _name, _res, _args in (
         ("pv_index_bytes", _SZ, [_U32, _U64, _U32]),
         ("pv_windows_items", _SZ, [ctypes.POINTER(DevCohort), _I64, _I64]),
         ("pv_windows_trace", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _U32, _P, _P, _P, _SZ, _P, _SZ, _P]),
-        ("pv_index_build", _I32, [ctypes.POINTER(DevCohort), _U64, _U32, _P, _P, _P])):
+        ("pv_index_build", _I32, [ctypes.POINTER(DevCohort), _U64, _U32, _P, _P, _P, _P])):
     _f = getattr(_lib, _name)
     _f.restype, _f.argtypes = _res, _args
 
@@ -508,19 +508,21 @@ def trace_summary(trace):
 
 def index_build(dev, nblocks, ckpt_shift, device):
     """The cohort's checkpoint index on `device` (pv_index_build: every block decoded once on the device; blocks in the
-    block cache skipped) -> (uint8 tensor of pv_ckpt records, number of blocks that failed to decode). Waits for it."""
+    block cache skipped) -> (uint8 tensor of pv_ckpt records, int32 tensor of each block's first lower-case run, number
+    of blocks that failed to decode). Waits for it."""
     nbytes = int(_lib.pv_index_bytes(int(dev.Q), int(nblocks), int(ckpt_shift)))
     if not nbytes:
         raise ValueError(f"checkpoint stride 2^{ckpt_shift}: a power of two from 256 to the block size {dev.Q}")
     out = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    brun = torch.empty(max(1, int(nblocks)), dtype=torch.int32, device=device)
     nbad = torch.zeros(1, dtype=torch.int64, device=device)
     with torch.cuda.device(device):
-        code = _lib.pv_index_build(ctypes.byref(dev), int(nblocks), int(ckpt_shift), out.data_ptr(), nbad.data_ptr(),
+        code = _lib.pv_index_build(ctypes.byref(dev), int(nblocks), int(ckpt_shift), out.data_ptr(), nbad.data_ptr(), brun.data_ptr(),
                                    torch.cuda.current_stream(device).cuda_stream)
         if code:
             raise RuntimeError("panvram_b200 index: " + (_lib.pv_kernels_last_error() or b"").decode())
         torch.cuda.current_stream(device).synchronize()
-    return out, int(nbad.item())
+    return out, brun, int(nbad.item())
 
 
 def read_status(status):

@@ -115,14 +115,15 @@ class Cohort:
         then cover one stride each: each decodes from its checkpoint to the end of its range only, so a window's serial
         chains are about a stride long instead of a block, and the blocks outside the window's span are not decoded.
         Decoding every block here also validates it: a block that fails is marked, and windows touching it report
-        status 1 exactly as when they decoded it in full."""
+        status 1 exactly as when they decoded it in full. Alongside, each block's first lower-case run (4 bytes per
+        block), so an item finds its runs in a step or two instead of a binary search of the assembly's runs."""
         if stride & (stride - 1) or not 256 <= stride <= self._core.Q:
             raise ValueError(f"checkpoint_stride: a power of two from 256 to the block size ({self._core.Q}), or 0")
         shift = stride.bit_length() - 1
         asms = self._dev["asms"].cpu().numpy().view(np.uint64).reshape(-1, 8)
         nblocks = int(asms[:, 2].sum())
-        self._ckpt, self.bad_blocks = _C.index_build(self._devc, nblocks, shift, self.device)
-        self._devc.ckpt, self._devc.ckpt_shift = self._ckpt.data_ptr(), shift
+        self._ckpt, self._brun, self.bad_blocks = _C.index_build(self._devc, nblocks, shift, self.device)
+        self._devc.ckpt, self._devc.ckpt_shift, self._devc.brun = self._ckpt.data_ptr(), shift, self._brun.data_ptr()
         self.checkpoint_stride = stride
 
     @property
@@ -281,7 +282,7 @@ class Cohort:
         r = {"P": nb("payload"), "blocks": nb("blocks", "groups", "btab", "bexc"), "tab": nb("tabs"), "low": nb("low"),
              "ref": nb("ref_padded", "pref", "pruns", "pidx"), "asm": nb("asms"),
              "cache": self._cache.numel() if self._cache is not None else 0,
-             "index": self._ckpt.numel() if self._ckpt is not None else 0}
+             "index": (self._ckpt.numel() + 4 * self._brun.numel()) if self._ckpt is not None else 0}
         r["total"] = sum(r.values())
         return r
 

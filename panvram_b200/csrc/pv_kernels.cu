@@ -81,10 +81,14 @@ struct __align__(16) Item {
     uint32_t jc, wx0, wx1;  // its cell of the block; the window's bytes in the block [wx0, wx1)
     uint4 landing;          // 16 bytes a bulk copy may target (the expired-wait test's completing copy)
     uint64_t idx;           // its index in the call (the trace record it writes)
-    Op ops[OPS_CAP];
-    uint8_t lits[LIT_CAP];
-    int32_t runs[2 * RUN_CAP];   // window-relative [start, end), clipped to the item's range
+    alignas(16) int32_t runs[2 * RUN_CAP];   // window-relative [start, end), clipped to the item's range
+    alignas(16) Op ops[OPS_CAP];
+    alignas(16) uint8_t lits[LIT_CAP];
 };
+// an Item is copied in 16-byte words: the part up to its ops (header and runs), then only the ops and literal bytes it
+// holds
+constexpr uint32_t ITEM_HEAD16 = (uint32_t)(offsetof(Item, ops) / 16), ITEM_LITS16 = (uint32_t)(offsetof(Item, lits) / 16);
+static_assert(offsetof(Item, ops) % 16 == 0 && offsetof(Item, lits) % 16 == 0 && sizeof(Item) % 16 == 0, "Item layout");
 
 struct Params {
     pv_dev_cohort C;
@@ -840,6 +844,7 @@ __device__ __forceinline__ RefView slot_ref(const Params& P, uint8_t* slot) {
 // intersected); false when there is nothing to decode
 __device__ bool item_locate(const Params& P, uint64_t item, Item* it) {
     it->state = ST_IDLE;
+    it->nops = 0; it->nlits = 0;
     if (item >= P.total) return false;
     it->idx = item;
     const uint64_t w = item < 0xFFFFFFFFull ? (uint64_t)((uint32_t)item / (uint32_t)P.bpw) : item / P.bpw, j = item - w * P.bpw;
@@ -905,8 +910,14 @@ __device__ void item_runs(const Params& P, Item* it) {
     if (!(P.apply_case && !P.tokens && R.low_cnt)) return;
     const uint64_t x0 = it->bst + it->ox0, x1 = it->bst + it->ox1, s = it->s;
     const uint64_t* low = C.low + 2 * R.low_base;
-    uint64_t lo = 0, hi = R.low_cnt;
-    while (lo < hi) { const uint64_t m = (lo + hi) >> 1; if (__ldg(low + 2 * m + 1) <= x0) lo = m + 1; else hi = m; }
+    uint64_t lo = 0;
+    if (C.brun) {                                   // from the block's first run, a step or two
+        lo = __ldg(C.brun + it->gblk);
+        while (lo < R.low_cnt && __ldg(low + 2 * lo + 1) <= x0) lo++;
+    } else {
+        uint64_t hi = R.low_cnt;
+        while (lo < hi) { const uint64_t m = (lo + hi) >> 1; if (__ldg(low + 2 * m + 1) <= x0) lo = m + 1; else hi = m; }
+    }
     uint64_t e = lo;
     while (e < R.low_cnt && __ldg(low + 2 * e) < x1) e++;
     it->run_first = (uint32_t)(R.low_base + lo); it->run_cnt = (uint32_t)(e - lo);
@@ -1281,7 +1292,13 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
         if (lane == 0) trace_at(P, item, 4);
         const uint4* src = (const uint4*)(plan + item);
         uint4* dst = (uint4*)it;
-        for (uint32_t k = lane; k < sizeof(Item) / 16; k += 32) dst[k] = src[k];
+        const Item* pi = plan + item;
+        const uint32_t nops = min((uint32_t)__ldg(&pi->nops), (uint32_t)OPS_CAP), nlits = min((uint32_t)__ldg(&pi->nlits), (uint32_t)LIT_CAP);
+        const uint32_t no16 = (nops * (uint32_t)sizeof(Op) + 15) / 16, nl16 = (nlits + 15) / 16;
+        for (uint32_t k = lane; k < ITEM_HEAD16 + no16 + nl16; k += 32) {
+            const uint32_t q = k < ITEM_HEAD16 + no16 ? k : ITEM_LITS16 + (k - ITEM_HEAD16 - no16);
+            dst[q] = __ldg(src + q);
+        }
     } else if (lane == 0) {
         it->state = ST_IDLE;
     }
@@ -1346,7 +1363,7 @@ struct CkptSink {
 
 template <bool PK, bool CP>
 __global__ void __launch_bounds__(128) pv_index_kernel(const pv_dev_cohort C, uint64_t nblk, uint32_t cs, uint32_t qs, uint4* out,
-                                                       unsigned long long* nbad) {
+                                                       unsigned long long* nbad, uint32_t* brun) {
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= nblk) return;
     int64_t lo = 0, hi = C.nasm;                    // the assembly: the last one whose first block is at or before i
@@ -1356,6 +1373,12 @@ __global__ void __launch_bounds__(128) pv_index_kernel(const pv_dev_cohort C, ui
     const uint32_t blen = (uint32_t)(nbases - bst < (1ull << qs) ? nbases - bst : (1ull << qs));
     const uint32_t ncell = 1u << (qs - cs);
     uint4* o = out + 2 * (i << (qs - cs));
+    if (brun) {                                     // the block's first lower-case run: the first to end after bst
+        const uint64_t* low = C.low + 2 * __ldg(&R.low_base);
+        uint64_t lo = 0, hi = __ldg(&R.low_cnt);
+        while (lo < hi) { const uint64_t m = (lo + hi) >> 1; if (__ldg(low + 2 * m + 1) <= bst) lo = m + 1; else hi = m; }
+        brun[i] = (uint32_t)lo;
+    }
     const BlockRec r = block_rec<CP>(C, i, __ldg(&R.grp_base), b);
     if (r.cache) return;                            // served from the block cache: never decoded by windows
     int res = DEC_ERR;
@@ -1839,7 +1862,7 @@ extern "C" size_t pv_index_bytes(uint32_t Q, uint64_t nblocks, uint32_t ckpt_shi
 }
 
 extern "C" int pv_index_build(const pv_dev_cohort* cohort, uint64_t nblocks, uint32_t ckpt_shift, pv_ckpt* out, uint64_t* nbad,
-                              void* stream) {
+                              uint32_t* brun, void* stream) {
     static_assert(sizeof(pv_ckpt) == 32, "pv_ckpt is two 16-byte words");
     const uint32_t Q = cohort ? cohort->Q : 0;
     if (!cohort || !(Q == 1024 || Q == 2048 || Q == 4096 || Q == 16384) || !pv_index_bytes(Q, nblocks, ckpt_shift) || !out ||
@@ -1864,10 +1887,10 @@ extern "C" int pv_index_build(const pv_dev_cohort* cohort, uint64_t nblocks, uin
     unsigned long long* nb = (unsigned long long*)nbad;
     const int form = (cohort->packed ? 1 : 0) | (cohort->compact ? 2 : 0);
     switch (form) {
-    case 0: pv_index_kernel<false, false><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb); break;
-    case 1: pv_index_kernel<true, false><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb); break;
-    case 2: pv_index_kernel<false, true><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb); break;
-    default: pv_index_kernel<true, true><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb); break;
+    case 0: pv_index_kernel<false, false><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun); break;
+    case 1: pv_index_kernel<true, false><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun); break;
+    case 2: pv_index_kernel<false, true><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun); break;
+    default: pv_index_kernel<true, true><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun); break;
     }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
