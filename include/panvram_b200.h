@@ -197,8 +197,8 @@ int pv_sha256_file_bases(const char* path, char hex[65]);
  * tokens), reverse-complemented where rc[i] != 0 (rc may be NULL), then mapped to tokens A/a 0 C/c 1 G/g 2 T/t 3
  * else 4 when tokens. asm, start: int64 [n] device; out: uint8 [n * W] device; status: int32 device word that the
  * call ORs PV_STATUS_* bits into (the caller zeroes it); work: device scratch of at least pv_windows_work_bytes()
- * bytes, 16-byte aligned (the split form's plan and the general path's block buffers; calls running at the same time
- * need their own). Launches on `stream` (a cudaStream_t), asynchronous. Same argument checks as pv_cuda.cu:119-128:
+ * bytes, 16-byte aligned (the split form's work queue, plan of decoded items and general-path list, and block
+ * buffers; nothing in it needs to start at zero; calls running at the same time need their own). Launches on `stream` (a cudaStream_t), asynchronous. Same argument checks as pv_cuda.cu:119-128:
  * W in [0, 2^31), n >= 0. */
 int pv_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
                const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* work, size_t work_bytes,
@@ -212,9 +212,12 @@ size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W);
  * caller) receives the PV_STATUS_* bits of each window; the cohort's block cache is filled this way at open. */
 #define PV_WIN_BLOCK_PATH 1u
 /* The kernels a call runs: by default the one-kernel form (one warp per item decodes on one lane and emits) while the
- * call has fewer than 4,608 (window, block) items (3,072 at Q = 16,384; items = n x (ceil(W / Q) + 1)), else two launches (pv_decode_kernel: one item per lane, as many
- * per warp as keep about 3,072 decode warps busy, at most 32; pv_emit_kernel: one item per warp). PV_WIN_FUSED /
- * PV_WIN_SPLIT force one form; the output is the same. */
+ * call has fewer than 4,608 work items (3,072 when the item cell is 16,384 bases; items = n x (ceil(W / cell) + 1), the
+ * cell being the checkpoint stride of a cohort with an index, else its block size), else three launches
+ * (pv_decode_kernel: one item per lane, as many per warp as keep about 3,072 decode warps busy, at most 32;
+ * pv_emit_kernel: persistent, each warp taking the next decoded item from a queue and writing it; pv_heavy_kernel: the
+ * items that need the general path, usually none). PV_WIN_FUSED / PV_WIN_SPLIT force one form; the output is the
+ * same. */
 #define PV_WIN_FUSED 2u
 #define PV_WIN_SPLIT 4u
 /* For testing the expired-wait path (status 4) without a fault: every kernel's bounded wait on its shared-memory bulk
@@ -288,8 +291,8 @@ int pv_torch_draw_geometry(int64_t n, uint64_t total, int rc_mode, int sm_count,
  * Some callers cannot call cudaMalloc or hand over a scratch buffer: a data-loading hook inside a training framework
  * whose caching allocator already owns the device memory (a direct cudaMalloc there can fail or fragment its pool),
  * or code that must not stall the device (cudaMalloc / cudaFree can synchronise it). This variant takes the same
- * inputs and outputs as pv_windows but keeps its scratch - the split form's plan (the decode results of every item)
- * and the general path's block buffers - in a fixed array of PV_NOALLOC_SCRATCH_BYTES that the library places in
+ * inputs and outputs as pv_windows but keeps its scratch - the split form's work queue, its plan (the decode results
+ * of every item) and list of general-path items, and the block buffers - in a fixed array of PV_NOALLOC_SCRATCH_BYTES that the library places in
  * device memory; every GPU that loads the library holds its own copy of that array until the process exits. A call
  * that would need more scratch than that (pv_windows_work_bytes) returns PV_EARG (message in pv_kernels_last_error())
  * without launching; split it into smaller calls. The first call on a device looks up that device's array address
@@ -297,8 +300,8 @@ int pv_torch_draw_geometry(int64_t n, uint64_t total, int rc_mode, int sm_count,
  * CUDA stream capture; the kept address assumes the device's primary context lives as long as the process (after a
  * cudaDeviceReset, do not call this again). The calls on one device share its array: two calls on the same device
  * that run on the GPU at the same time (on different streams) race on it and must not overlap; calls on different
- * devices use different arrays and may. Nothing in it needs to start at zero: every byte of the plan and of a block
- * buffer is written before it is read. The call makes no cudaMalloc, cudaFree or other allocation. */
+ * devices use different arrays and may. Nothing in it needs to start at zero: the call's first kernel zeroes the
+ * queue, and every byte of the plan, the list and a block buffer is written before it is read. The call makes no cudaMalloc, cudaFree or other allocation. */
 #define PV_NOALLOC_SCRATCH_BYTES (16u << 20)
 int pv_windows_noalloc(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,
                        const uint8_t* rc, int tokens, int apply_case, uint8_t* out, int32_t* status, void* stream);
@@ -388,10 +391,11 @@ int pv_coords_from_host(const int64_t* asm_host, const int64_t* start_host, cons
  * previous batch's windows being copied to the host on another stream). */
 int pv_status_to_host(const int32_t* status, int32_t* host_word, void* stream);
 
-/* at most how many kernel launches one pv_windows call with these sizes makes (0 for an empty call) */
+/* at most how many kernel launches one pv_windows call with these sizes makes (0 for an empty call; 3 for the split
+ * form, 1 for the fused one) */
 int pv_windows_launches(int64_t n, int64_t W);
-/* the form a pv_windows_ex call with these sizes and flags takes: *launches 1 (pv_windows_kernel) or 2
- * (pv_decode_kernel + pv_emit_kernel; *dec_lanes items per decode warp), 0 for an empty call. cell: the cohort's item
+/* the form a pv_windows_ex call with these sizes and flags takes: *launches 1 (pv_windows_kernel) or 3
+ * (pv_decode_kernel + pv_emit_kernel + pv_heavy_kernel; *dec_lanes items per decode warp), 0 for an empty call. cell: the cohort's item
  * cell, its checkpoint stride (1 << ckpt_shift) when it has an index, else its block size Q. */
 int pv_windows_form(uint32_t cell, int64_t n, int64_t W, uint32_t flags, int* launches, uint32_t* dec_lanes);
 /* message of the calling thread's last pv_windows / pv_windows_ex argument or launch failure */

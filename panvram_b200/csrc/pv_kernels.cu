@@ -596,31 +596,6 @@ __device__ __forceinline__ void op_src16(const Item* it, const RefView& R, uint3
         lds16u(lits_sm + (uint32_t)((int64_t)o.src + (blo - first)), v);
     }
 }
-// any 16 bytes of an item's range: every op overlapping them, merged
-struct OpsGather {
-    const Item* it; RefView R; uint32_t lits_sm;
-    __device__ void operator()(int64_t blo, uint32_t r[4]) const {
-        r[0] = r[1] = r[2] = r[3] = 0;
-        const int64_t klo = blo > (int64_t)it->ox0 ? blo : (int64_t)it->ox0;
-        const int64_t khi = blo + 16 < (int64_t)it->ox1 ? blo + 16 : (int64_t)it->ox1;
-        if (klo >= khi) return;
-        int lo = 0, hi = it->nops;                 // first op ending after klo
-        while (lo < hi) {
-            const int m = (lo + hi) >> 1;
-            if ((int64_t)op_dst(it->ops[m]) + it->ops[m].len <= klo) lo = m + 1; else hi = m;
-        }
-        for (int k = lo; k < it->nops; k++) {
-            const Op o = it->ops[k];
-            const int64_t dst = op_dst(o), len = o.len;
-            if (dst >= khi) break;
-            const int64_t a = dst > klo ? dst : klo, e = dst + len < khi ? dst + len : khi;
-            if (a >= e) continue;
-            uint32_t v[4];
-            op_src16(it, R, lits_sm, o, blo, v);
-            merge16(r, v, (int)(a - blo), (int)(e - blo));
-        }
-    }
-};
 struct BufGather {
     const Item* it; const uint8_t* buf;
     __device__ void operator()(int64_t blo, uint32_t r[4]) const {
@@ -749,9 +724,12 @@ __device__ void emit(const Params& P, const Item* it, const Gather& gather, int 
 // kernels' instruction cache footprint)
 __device__ __noinline__ void emit_cached(const Params& P, const Item* it, int lane) { emit(P, it, CacheGather{it->cptr}, lane, 32); }
 
-// A decoded item's output: first every 16-byte output chunk that lies wholly inside one op (pass 1, chunk-major), then
-// each chunk that holds a boundary (an op start, or an end of the item's range, off a 16-byte boundary), assembled from
-// every op it overlaps by one lane (pass 2).
+// A decoded item's output, in one pass over the 16-byte chunks of the output row that its range [A, B) touches: lane i
+// takes every 32nd chunk, in the order of the block offsets they read (the output order reversed for a
+// reverse-complemented window), with a cursor into the ops that only moves forward. A chunk inside one op (most of
+// them) is that op's 16 source bytes; a chunk around op boundaries merges the bytes of each op it overlaps. Then case /
+// reverse complement / tokens in registers and one 16-byte store - or, for the chunks at the ends of [A, B), the bytes
+// inside it.
 __device__ void emit_ops(const Params& P, const Item* it, const RefView& R, int lane) {
     const OutRange g = out_range(P, it);
     const int64_t W = (int64_t)P.W;
@@ -759,33 +737,32 @@ __device__ void emit_ops(const Params& P, const Item* it, const RefView& R, int 
     const uint32_t lits_sm = smem_addr(it->lits);
     const int nops = it->nops;
     const int64_t ox0 = it->ox0, ox1 = it->ox1;
-    // pass 1, chunk-major: the 16-byte chunks wholly inside [A, B); lane i takes every 32nd, in the order of the block
-    // offsets they read (the output order reversed for a reverse-complemented window), with a cursor into the ops that
-    // only moves forward. A chunk inside one op is written here; one that holds an op boundary is left to pass 2.
-    const int64_t c0 = ((int64_t)g.A + 15) & ~(int64_t)15, c1 = (int64_t)g.B & ~(int64_t)15;
-    const int64_t nch = c1 > c0 ? (c1 - c0) >> 4 : 0;
+    const int64_t c0 = (int64_t)g.A & ~(int64_t)15, c1 = ((int64_t)g.B + 15) & ~(int64_t)15;
+    const int64_t nch = (c1 - c0) >> 4;
     int k = 0;
     for (int64_t i = lane; i < nch; i += 32) {
         const int64_t c = g.rcw ? c1 - 16 - 16 * i : c0 + 16 * i;
         const int64_t wpf = g.rcw ? W - 16 - (c - base) : c - base;
         const int64_t blo = wpf + g.delta;                  // block offset of the chunk's first forward byte
-        while (k < nops && (int64_t)op_dst(it->ops[k]) + it->ops[k].len <= blo) k++;
+        const int64_t klo = blo > ox0 ? blo : ox0, khi = blo + 16 < ox1 ? blo + 16 : ox1;
+        while (k < nops && (int64_t)op_dst(it->ops[k]) + it->ops[k].len <= klo) k++;
         if (k >= nops) break;
         const Op o = it->ops[k];
-        if ((int64_t)op_dst(o) > blo || (int64_t)op_dst(o) + o.len < blo + 16) continue;
         uint32_t v[4];
-        op_src16(it, R, lits_sm, o, blo, v);
-        put16(P, it, g, (uintptr_t)c, wpf, v, true);
-    }
-    const OpsGather gather{it, R, lits_sm};
-    for (int k = lane; k <= nops; k += 32) {
-        const int64_t b = k < nops ? (op_dst(it->ops[k]) > ox0 ? (int64_t)op_dst(it->ops[k]) : ox0) : ox1;
-        const int64_t p = base + (g.rcw ? W - (b - g.delta) : b - g.delta);     // the boundary's address in the row
-        if ((p & 15) == 0) continue;
-        const int64_t c = p & ~(int64_t)15;
-        const int64_t wpf = g.rcw ? W - 16 - (c - base) : c - base;
-        uint32_t v[4];
-        gather(wpf + g.delta, v);
+        if ((int64_t)op_dst(o) <= klo && (int64_t)op_dst(o) + o.len >= khi) {
+            op_src16(it, R, lits_sm, o, blo, v);          // one op covers every byte of the chunk the item writes
+        } else {
+            v[0] = v[1] = v[2] = v[3] = 0;
+            for (int kk = k; kk < nops; kk++) {
+                const Op q = it->ops[kk];
+                const int64_t dst = op_dst(q);
+                if (dst >= khi) break;
+                const int64_t a = dst > klo ? dst : klo, e = dst + q.len < khi ? dst + q.len : khi;
+                uint32_t u[4];
+                op_src16(it, R, lits_sm, q, blo, u);
+                merge16(v, u, (int)(a - blo), (int)(e - blo));
+            }
+        }
         put16(P, it, g, (uintptr_t)c, wpf, v, false);
     }
 }
@@ -1051,16 +1028,19 @@ __device__ void stage_span_packed(const Params& P, uint8_t* slot, int lane) {
 // bounded again, until the copies have landed: a CTA must not leave while a copy still targets its shared memory.
 // Under PV_WIN_TEST_WAIT the barrier expects 16 bytes that no copy brings, so the first wait expires for sure; a
 // 16-byte copy issued then completes them, and the second wait ends once every copy, that one included, has landed.
-__device__ bool slot_wait(const Params& P, Item* it, uint32_t bar) {
+enum { WAIT_OK = 0, WAIT_EXPIRED = 1, WAIT_STUCK = 2 };   // STUCK: a copy may still land in the slot; do not reuse it
+__device__ int slot_wait_ex(const Params& P, Item* it, uint32_t bar) {
     const uint32_t lim = P.test_wait ? TEST_WAIT_SPINS : WAIT_SPINS;
     for (uint32_t k = 0; k < lim; k++)
-        if (mbar_try(bar, 0)) return true;
+        if (mbar_try(bar, 0)) return WAIT_OK;
     report(P, it->w, PV_STATUS_WAIT);
     it->state = ST_ERR;
     if (P.test_wait) bulk_g2s(smem_addr(&it->landing), P.C.tabs, 16, bar);
-    for (uint32_t k = 0; k < DRAIN_SPINS && !mbar_try(bar, 0); k++) {}
-    return false;
+    for (uint32_t k = 0; k < DRAIN_SPINS; k++)
+        if (mbar_try(bar, 0)) return WAIT_EXPIRED;
+    return WAIT_STUCK;
 }
+__device__ bool slot_wait(const Params& P, Item* it, uint32_t bar) { return slot_wait_ex(P, it, bar) == WAIT_OK; }
 
 // lane 0 of the item's warp: wait (bounded) for the slot's copies, then decode the block keeping the window's ops
 template <bool PK>
@@ -1239,12 +1219,20 @@ __device__ void item_block_lane(const Params& P, Item* it) {
     else if (!CP && r.plen == (uint32_t)PV_BLEN_BAD) { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
 }
 
+// The split form's work queue, at the start of the call's scratch: pv_decode_kernel zeroes it (it runs first, and the
+// two kernels after it wait for it to finish); pv_emit_kernel's warps take items from `next` and list the items that
+// need the general path in `heavy`; pv_heavy_kernel's CTAs take those from `hnext`.
+struct WorkQueue { unsigned long long next, nheavy, hnext, pad[5]; };
+constexpr uint64_t QUEUE_BYTES = 256;
+constexpr unsigned HEAVY_CTAS = 148;             // pv_heavy_kernel's grid (each CTA a Q-byte block buffer in the scratch)
+
 constexpr int DEC_THREADS = 32;            // one warp per CTA: the few decode warps of a call spread over all SMs
 constexpr uint64_t DEC_WARPS = 3072;       // decode warps a split call aims for (148 SMs x ~21)
 template <bool PK, bool CP>
-__global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid_constant__ Params P, Item* plan) {
+__global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid_constant__ Params P, Item* plan, WorkQueue* q) {
     pdl_trigger();                                  // the emission kernel's CTAs may be placed now; they wait for this grid
     pdl_wait();
+    if (blockIdx.x == 0 && threadIdx.x == 0) { q->next = 0; q->nheavy = 0; q->hnext = 0; }
     if (threadIdx.x >= P.dec_lanes) return;
     const uint64_t i = (uint64_t)blockIdx.x * P.dec_lanes + threadIdx.x;
     if (i >= P.total) return;
@@ -1277,61 +1265,102 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
     else { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
 }
 
+// pv_emit_kernel: persistent - as many CTAs as are resident at once - and each WARP on its own takes the next item
+// from the queue, copies its decoded Item from the plan into its shared slot (the header, then only the ops and literal
+// bytes it holds), stages the reference span under its output range (TMA bulk copy, bounded wait), and writes it. A
+// warp that finishes takes the next item at once: no CTA-wide barrier, so a slow item holds up no other warp. Items
+// that need the general path are listed for pv_heavy_kernel.
 template <bool PK>
-__global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__ Params P, const Item* plan) {
+__global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__ Params P, const Item* plan, WorkQueue* q, uint64_t* heavy) {
     extern __shared__ uint4 smem_raw[];
     __shared__ __align__(8) uint64_t bars[WARPS];
-    __shared__ Op hops[HOPS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();                                  // pv_heavy_kernel's CTAs may be placed now; they wait for this grid
     pdl_wait();
     uint8_t* slot = (uint8_t*)smem_raw + (size_t)warp * P.slot_bytes;
     Item* it = slot_item(slot);
-    const uint64_t item = (uint64_t)blockIdx.x * WARPS + warp;
     const uint32_t bar = smem_addr(&bars[warp]);
-    if (item < P.total) {
+    const pv_dev_cohort& C = P.C;
+    for (uint64_t round = 0; round <= P.total; round++) {      // (bounded: every round takes an item or ends)
+        uint64_t item = 0;
+        if (lane == 0) item = atomicAdd(&q->next, 1ull);
+        item = __shfl_sync(0xffffffffu, item, 0);
+        if (item >= P.total) break;
         if (lane == 0) trace_at(P, item, 4);
-        const uint4* src = (const uint4*)(plan + item);
-        uint4* dst = (uint4*)it;
         const Item* pi = plan + item;
         const uint32_t nops = min((uint32_t)__ldg(&pi->nops), (uint32_t)OPS_CAP), nlits = min((uint32_t)__ldg(&pi->nlits), (uint32_t)LIT_CAP);
         const uint32_t no16 = (nops * (uint32_t)sizeof(Op) + 15) / 16, nl16 = (nlits + 15) / 16;
+        const uint4* src = (const uint4*)pi;
+        uint4* dst = (uint4*)it;
         for (uint32_t k = lane; k < ITEM_HEAD16 + no16 + nl16; k += 32) {
-            const uint32_t q = k < ITEM_HEAD16 + no16 ? k : ITEM_LITS16 + (k - ITEM_HEAD16 - no16);
-            dst[q] = __ldg(src + q);
-        }
-    } else if (lane == 0) {
-        it->state = ST_IDLE;
-    }
-    __syncwarp();
-    const int st0 = it->state;
-    if (st0 == ST_OK || st0 == ST_HEAVY) {
-        const pv_dev_cohort& C = P.C;
-        if (lane == 0) {
-            // the span the emission reads: the start diagonal under the item's output range only (the decode has
-            // finished; anything off it comes from global memory), so the slot holds min(W, Q) bases, not Q
-            item_span(P, it, true, P.span_cap);
-            const uint32_t span_tma = PK ? 0u : it->span_len;
-            mbar_init(bar);
-            mbar_expect(bar, span_tma + (P.test_wait ? 16u : 0u));
-            if (span_tma) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + it->span_lo, span_tma, bar);
+            const uint32_t w = k < ITEM_HEAD16 + no16 ? k : ITEM_LITS16 + (k - ITEM_HEAD16 - no16);
+            dst[w] = __ldg(src + w);
         }
         __syncwarp();
-        if (PK) stage_span_packed(P, slot, lane);
-        if (lane == 0 && slot_wait(P, it, bar)) trace_at(P, item, 5);
-    }
-    __syncwarp();
-    if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
-    else if (it->state == ST_CACHED) emit_cached(P, it, lane);
-    __syncwarp();
-    if (lane == 0 && item < P.total && it->state != ST_HEAVY && it->state != ST_IDLE) trace_done(P, it, 2);
-    __syncthreads();
-    uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
-    for (int t = 0; t < WARPS; t++) {
-        uint8_t* sl = (uint8_t*)smem_raw + (size_t)t * P.slot_bytes;
-        if (slot_item(sl)->state == ST_HEAVY) {
-            heavy_item<PK, true>(P, sl, buf, hops);
-            if (threadIdx.x == 0) trace_done(P, slot_item(sl), 2);
+        const int st0 = it->state;
+        if (st0 == ST_HEAVY) {
+            if (lane == 0) heavy[atomicAdd(&q->nheavy, 1ull)] = item;
+            __syncwarp();
+            continue;
         }
+        int wr = WAIT_OK;
+        if (st0 == ST_OK) {
+            if (lane == 0) {
+                // the span the emission reads: the decode's starting diagonal under the item's output range only
+                item_span(P, it, true, P.span_cap);
+                const uint32_t span_tma = PK ? 0u : it->span_len;
+                mbar_init(bar);
+                mbar_expect(bar, span_tma + (P.test_wait ? 16u : 0u));
+                if (span_tma) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + it->span_lo, span_tma, bar);
+            }
+            __syncwarp();
+            if (PK) stage_span_packed(P, slot, lane);
+            if (lane == 0) {
+                wr = slot_wait_ex(P, it, bar);
+                if (wr == WAIT_OK) trace_at(P, item, 5);
+            }
+            wr = __shfl_sync(0xffffffffu, wr, 0);
+        }
+        __syncwarp();
+        if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
+        else if (it->state == ST_CACHED) emit_cached(P, it, lane);
+        __syncwarp();
+        if (lane == 0 && it->state != ST_IDLE) trace_done(P, it, 2);
+        if (wr == WAIT_STUCK) break;               // a copy may still land in this slot: the warp takes no more items
+        __syncwarp();
+    }
+}
+
+// pv_heavy_kernel: the items listed by pv_emit_kernel (a self copy inside the window, more ops or literals than a
+// slot holds, a stream longer than a slot, or every item under PV_WIN_BLOCK_PATH), one per CTA at a time: the CTA
+// decodes the block from its start into its block buffer and emits the item's range (heavy_item). Usually there are
+// none, and each CTA finds the list empty and returns.
+template <bool PK>
+__global__ void __launch_bounds__(CTA) pv_heavy_kernel(const __grid_constant__ Params P, const Item* plan, WorkQueue* q, const uint64_t* heavy) {
+    extern __shared__ uint4 smem_raw[];
+    __shared__ Op hops[HOPS];
+    __shared__ uint64_t h_item;
+    pdl_wait();
+    uint8_t* slot = (uint8_t*)smem_raw;
+    Item* it = slot_item(slot);
+    uint8_t* buf = P.work + (uint64_t)blockIdx.x * P.C.Q;
+    const uint64_t nheavy = *(volatile unsigned long long*)&q->nheavy;
+    for (uint64_t round = 0; round <= nheavy; round++) {
+        if (threadIdx.x == 0) {
+            const unsigned long long h = atomicAdd(&q->hnext, 1ull);
+            h_item = h < nheavy ? heavy[h] : ~0ull;
+        }
+        __syncthreads();
+        const uint64_t item = h_item;
+        if (item == ~0ull) break;
+        const uint4* src = (const uint4*)(plan + item);
+        for (uint32_t k = threadIdx.x; k < sizeof(Item) / 16; k += CTA) ((uint4*)it)[k] = __ldg(src + k);
+        __syncthreads();
+        if (threadIdx.x == 0) { it->span_len = 0; it->span_lo = 0; }   // the reference from global memory
+        __syncthreads();
+        heavy_item<PK, true>(P, slot, buf, hops);
+        if (threadIdx.x == 0) trace_done(P, it, 2);
+        __syncthreads();
     }
 }
 
@@ -1531,7 +1560,7 @@ extern "C" {
 
 const char* pv_kernels_last_error(void) { return g_cuda_err; }
 
-int pv_windows_launches(int64_t n, int64_t W) { return (n > 0 && W > 0) ? 2 : 0; }   // (at most: 1 when fused)
+int pv_windows_launches(int64_t n, int64_t W) { return (n > 0 && W > 0) ? 3 : 0; }   // (at most: 1 when fused)
 
 int pv_coords_from_host(const int64_t* asm_host, const int64_t* start_host, const uint8_t* rc_host, int64_t n, int64_t* asm_index,
                         int64_t* start, uint8_t* rc, void* stream) {
@@ -1591,11 +1620,17 @@ static bool form_of(uint32_t cell, uint64_t total, uint32_t flags, uint32_t* lan
     return (flags & PV_WIN_FUSED) ? true : (flags & PV_WIN_SPLIT) ? false : total < split_min_items(cell);
 }
 static uint64_t plan_bytes(uint64_t total) { return (total * sizeof(Item) + 255) & ~255ull; }
+// A call's scratch. The split form: its work queue, the plan (one Item per item), the list of items for the general
+// path, and pv_heavy_kernel's Q-byte block buffers. The fused form: a Q-byte block buffer per CTA. Sized for either.
+static uint64_t split_scratch(uint64_t total, uint32_t Q) {
+    return QUEUE_BYTES + plan_bytes(total) + ((8 * total + 255) & ~255ull) + (uint64_t)HEAVY_CTAS * Q;
+}
+static uint64_t work_need(uint64_t total, uint64_t grid, uint32_t Q) { return std::max<uint64_t>(split_scratch(total, Q), grid * Q); }
 size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W) {
     if (n <= 0 || W <= 0) return 0;
     uint64_t total, bpw;
     const uint64_t grid = grid_of(cell_of(cohort), n, W, &total, &bpw);
-    return (size_t)(plan_bytes(total) + grid * cohort->Q);
+    return (size_t)work_need(total, grid, cohort->Q);
 }
 
 int pv_windows(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W, const uint8_t* rc,
@@ -1634,14 +1669,41 @@ static cudaError_t fused_form(uint64_t grid, size_t smem, cudaStream_t st, const
     if (e != cudaSuccess) return e;
     return launch_pdl(pv_windows_kernel<PK, CP>, (unsigned)grid, CTA, smem, st, P);
 }
+// CTAs of a kernel resident at once on the current device (its SM count x what fits on an SM), cached per kernel and size
+struct ResidentMemo { const void* fn; size_t smem; int dev; unsigned n; };
+static unsigned resident_ctas(const void* fn, int block, size_t smem) {
+    static thread_local ResidentMemo memo[16];
+    static thread_local int next = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    for (int i = 0; i < 16; i++)
+        if (memo[i].fn == fn && memo[i].smem == smem && memo[i].dev == dev) return memo[i].n;
+    int sms = 0, per = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, fn, block, smem) != cudaSuccess || per < 1) {
+        cudaGetLastError();
+        return 148;
+    }
+    const unsigned n = (unsigned)(sms * per);
+    memo[next] = ResidentMemo{fn, smem, dev, n};
+    next = (next + 1) % 16;
+    return n;
+}
+// decode kernel, then the persistent emission kernel (no more CTAs than are resident at once, nor than its items need),
+// then the general-path kernel
 template <bool PK, bool CP>
-static cudaError_t split_form(uint64_t total, uint64_t grid, size_t smem_e, cudaStream_t st, const Params& P, const Params& PE, Item* plan) {
-    const cudaError_t e = smem_attr((const void*)pv_emit_kernel<PK>, 4 + (PK ? 1 : 0), smem_e);
+static cudaError_t split_form(uint64_t total, size_t smem_e, cudaStream_t st, const Params& P, const Params& PE, const Params& PH, Item* plan,
+                              WorkQueue* q, uint64_t* heavy) {
+    cudaError_t e = smem_attr((const void*)pv_emit_kernel<PK>, 4 + (PK ? 1 : 0), smem_e);
     if (e != cudaSuccess) return e;
-    const cudaError_t d = launch_pdl(pv_decode_kernel<PK, CP>, (unsigned)((total + P.dec_lanes - 1) / P.dec_lanes), DEC_THREADS, 0, st,
-                                     P, plan);
-    if (d != cudaSuccess) return d;
-    return launch_pdl(pv_emit_kernel<PK>, (unsigned)grid, CTA, smem_e, st, PE, (const Item*)plan);
+    e = launch_pdl(pv_decode_kernel<PK, CP>, (unsigned)((total + P.dec_lanes - 1) / P.dec_lanes), DEC_THREADS, 0, st, P, plan, q);
+    if (e != cudaSuccess) return e;
+    const uint64_t want = (total + WARPS - 1) / WARPS;
+    const uint64_t resident = resident_ctas((const void*)pv_emit_kernel<PK>, CTA, smem_e);
+    const unsigned grid = (unsigned)(want < resident ? want : resident);
+    e = launch_pdl(pv_emit_kernel<PK>, grid, CTA, smem_e, st, PE, (const Item*)plan, q, heavy);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(pv_heavy_kernel<PK>, HEAVY_CTAS, CTA, sizeof(Item), st, PH, (const Item*)plan, q, (const uint64_t*)heavy);
 }
 static cudaError_t launch_fused(int form, uint64_t grid, size_t smem, cudaStream_t st, const Params& P) {
     switch (form) {
@@ -1651,13 +1713,13 @@ static cudaError_t launch_fused(int form, uint64_t grid, size_t smem, cudaStream
     default: return fused_form<true, true>(grid, smem, st, P);
     }
 }
-static cudaError_t launch_split(int form, uint64_t total, uint64_t grid, size_t smem_e, cudaStream_t st, const Params& P,
-                                const Params& PE, Item* plan) {
+static cudaError_t launch_split(int form, uint64_t total, size_t smem_e, cudaStream_t st, const Params& P, const Params& PE,
+                                const Params& PH, Item* plan, WorkQueue* q, uint64_t* heavy) {
     switch (form) {
-    case 0: return split_form<false, false>(total, grid, smem_e, st, P, PE, plan);
-    case 1: return split_form<true, false>(total, grid, smem_e, st, P, PE, plan);
-    case 2: return split_form<false, true>(total, grid, smem_e, st, P, PE, plan);
-    default: return split_form<true, true>(total, grid, smem_e, st, P, PE, plan);
+    case 0: return split_form<false, false>(total, smem_e, st, P, PE, PH, plan, q, heavy);
+    case 1: return split_form<true, false>(total, smem_e, st, P, PE, PH, plan, q, heavy);
+    case 2: return split_form<false, true>(total, smem_e, st, P, PE, PH, plan, q, heavy);
+    default: return split_form<true, true>(total, smem_e, st, P, PE, PH, plan, q, heavy);
     }
 }
 
@@ -1696,7 +1758,7 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     // emission pair beyond, where several chains per decode warp amortise the decode
     if (((flags >> PV_WIN_DEC_LANES_SHIFT) & 63u) > 32) { snprintf(g_cuda_err, sizeof g_cuda_err, "decode lanes per warp: 1 to 32"); return PV_EARG; }
     const bool fused = form_of(cell, P.total, flags, &P.dec_lanes);
-    const uint64_t need = plan_bytes(P.total) + grid * Q;
+    const uint64_t need = work_need(P.total, grid, Q);
     if (!work || work_bytes < need || ((uintptr_t)work & 15)) {
         snprintf(g_cuda_err, sizeof g_cuda_err, "work buffer: %llu bytes needed, 16-byte aligned", (unsigned long long)need);
         return PV_EARG;
@@ -1706,8 +1768,12 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
         return PV_EARG;
     }
     P.trace = trace;
-    Item* plan = (Item*)work;
-    P.work = (uint8_t*)work + plan_bytes(P.total);
+    // the split form's scratch: queue | plan | general-path list | block buffers; the fused form's: block buffers
+    WorkQueue* q = (WorkQueue*)work;
+    Item* plan = (Item*)((uint8_t*)work + QUEUE_BYTES);
+    uint64_t* heavy = (uint64_t*)((uint8_t*)plan + plan_bytes(P.total));
+    uint8_t* hbuf = (uint8_t*)heavy + ((8 * P.total + 255) & ~255ull);
+    P.work = (uint8_t*)work;
     P.tokens = tokens; P.apply_case = apply_case; P.force_block = (flags & PV_WIN_BLOCK_PATH) ? 1 : 0;
     P.test_wait = (flags & PV_WIN_TEST_WAIT) ? 1 : 0;
     P.qshift = qshift;
@@ -1730,9 +1796,11 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     PE.span_cap = P.span_cap;
     PE.slot_bytes = (uint32_t)sizeof(Item) + PE.span_cap;
     const size_t smem_e = (size_t)WARPS * PE.slot_bytes;
+    Params PH = PE;                                 // pv_heavy_kernel: its CTAs' block buffers after the list
+    PH.work = hbuf;
     const int form = (cohort->packed ? 1 : 0) | (cohort->compact ? 2 : 0);
     const cudaError_t le = fused ? launch_fused(form, grid, smem, (cudaStream_t)stream, P)
-                                 : launch_split(form, P.total, grid, smem_e, (cudaStream_t)stream, P, PE, plan);
+                                 : launch_split(form, P.total, smem_e, (cudaStream_t)stream, P, PE, PH, plan, q, heavy);
     if (le != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(le)); return PV_ECUDA; }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
@@ -1751,7 +1819,7 @@ int pv_windows_form(uint32_t cell, int64_t n, int64_t W, uint32_t flags, int* la
     const uint64_t total = (uint64_t)n * (((uint64_t)W + cell - 1) / cell + 1);
     uint32_t lanes;
     const bool fused = form_of(cell, total, flags, &lanes);
-    *launches = fused ? 1 : 2;
+    *launches = fused ? 1 : 3;
     *dec_lanes = fused ? 0 : lanes;
     return PV_OK;
 }

@@ -40,7 +40,7 @@ def test_last_error_without_gpu():
     lib.pv_windows_launches.restype = ctypes.c_int
     lib.pv_windows_launches.argtypes = [ctypes.c_int64, ctypes.c_int64]
     assert lib.pv_last_error() is not None
-    assert lib.pv_windows_launches(0, 10) == 0 and lib.pv_windows_launches(5, 0) == 0 and lib.pv_windows_launches(5, 10) == 2    # decode + emission
+    assert lib.pv_windows_launches(0, 10) == 0 and lib.pv_windows_launches(5, 0) == 0 and lib.pv_windows_launches(5, 10) == 3    # decode, emission, general path
 
 
 def test_sample_coords_refuses_bad_arguments_without_launching():
@@ -81,13 +81,13 @@ def test_windows_form_rule():
     beyond (4,608 items; 3,072 at Q = 16,384), with about 3,072 decode warps (at most 32 items per warp); flags pin it."""
     from panvram_b200 import _C
     assert _C.windows_form(4096, 1024, 8192) == (1, 0)              # config 1: 3,072 items
-    assert _C.windows_form(4096, 1536, 8192) == (2, 2)              # 4,608 items
+    assert _C.windows_form(4096, 1536, 8192) == (3, 2)              # 4,608 items
     assert _C.windows_form(16384, 1024, 8192) == (1, 0)             # 2,048 items
-    assert _C.windows_form(16384, 4096, 8192) == (2, 3)             # config 2: 8,192 items
-    assert _C.windows_form(4096, 131072, 512) == (2, 32)
-    assert _C.windows_form(4096, 1024, 8192, _C.PV_WIN_SPLIT) == (2, 1)
+    assert _C.windows_form(16384, 4096, 8192) == (3, 3)             # config 2: 8,192 items
+    assert _C.windows_form(4096, 131072, 512) == (3, 32)
+    assert _C.windows_form(4096, 1024, 8192, _C.PV_WIN_SPLIT) == (3, 1)
     assert _C.windows_form(16384, 4096, 8192, _C.PV_WIN_FUSED) == (1, 0)
-    assert _C.windows_form(4096, 9999, 8192, _C.PV_WIN_SPLIT | _C.PV_WIN_DEC_LANES(7)) == (2, 7)
+    assert _C.windows_form(4096, 9999, 8192, _C.PV_WIN_SPLIT | _C.PV_WIN_DEC_LANES(7)) == (3, 7)
     assert _C.windows_form(4096, 0, 8192) == (0, 0)
     import pytest
     with pytest.raises(ValueError):

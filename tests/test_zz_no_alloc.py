@@ -41,7 +41,7 @@ def test_noalloc_matches_windows_twice(golden, cuda):
     # decode results also lives in the fixed array)
     for call, (n, W, tokens) in enumerate(((600, 3000, False), (600, 777, True), (1500, 3000, False))):
         if call == 2:
-            assert _C.windows_form(c.item_cell, n, W)[0] == 2 and lib.pv_windows_work_bytes(ctypes.byref(c._devc), n, W) <= 16 << 20
+            assert _C.windows_form(c.item_cell, n, W)[0] == 3 and lib.pv_windows_work_bytes(ctypes.byref(c._devc), n, W) <= 16 << 20
         a = rng.integers(0, len(NAMES), n)
         s = np.array([rng.integers(0, nb[k] - W + 1) for k in a])
         asm = torch.from_numpy(a.astype(np.int64)).to(cuda)
