@@ -1029,18 +1029,20 @@ __device__ void stage_span_packed(const Params& P, uint8_t* slot, int lane) {
 // Under PV_WIN_TEST_WAIT the barrier expects 16 bytes that no copy brings, so the first wait expires for sure; a
 // 16-byte copy issued then completes them, and the second wait ends once every copy, that one included, has landed.
 enum { WAIT_OK = 0, WAIT_EXPIRED = 1, WAIT_STUCK = 2 };   // STUCK: a copy may still land in the slot; do not reuse it
-__device__ int slot_wait_ex(const Params& P, Item* it, uint32_t bar) {
+// (phase: the parity of the barrier phase the copies complete; a barrier initialised once and used for one item after
+// another alternates 0, 1, 0, ...)
+__device__ int slot_wait_ex(const Params& P, Item* it, uint32_t bar, uint32_t phase = 0) {
     const uint32_t lim = P.test_wait ? TEST_WAIT_SPINS : WAIT_SPINS;
     for (uint32_t k = 0; k < lim; k++)
-        if (mbar_try(bar, 0)) return WAIT_OK;
+        if (mbar_try(bar, phase)) return WAIT_OK;
     report(P, it->w, PV_STATUS_WAIT);
     it->state = ST_ERR;
     if (P.test_wait) bulk_g2s(smem_addr(&it->landing), P.C.tabs, 16, bar);
     for (uint32_t k = 0; k < DRAIN_SPINS; k++)
-        if (mbar_try(bar, 0)) return WAIT_EXPIRED;
+        if (mbar_try(bar, phase)) return WAIT_EXPIRED;
     return WAIT_STUCK;
 }
-__device__ bool slot_wait(const Params& P, Item* it, uint32_t bar) { return slot_wait_ex(P, it, bar) == WAIT_OK; }
+__device__ bool slot_wait(const Params& P, Item* it, uint32_t bar) { return slot_wait_ex(P, it, bar, 0) == WAIT_OK; }
 
 // lane 0 of the item's warp: wait (bounded) for the slot's copies, then decode the block keeping the window's ops
 template <bool PK>
@@ -1281,6 +1283,9 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
     Item* it = slot_item(slot);
     const uint32_t bar = smem_addr(&bars[warp]);
     const pv_dev_cohort& C = P.C;
+    if (lane == 0) mbar_init(bar);                  // once: the warp's items use its phases one after another
+    __syncwarp();
+    uint32_t phase = 0;
     for (uint64_t round = 0; round <= P.total; round++) {      // (bounded: every round takes an item or ends)
         uint64_t item = 0;
         if (lane == 0) item = atomicAdd(&q->next, 1ull);
@@ -1309,17 +1314,17 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
                 // the span the emission reads: the decode's starting diagonal under the item's output range only
                 item_span(P, it, true, P.span_cap);
                 const uint32_t span_tma = PK ? 0u : it->span_len;
-                mbar_init(bar);
                 mbar_expect(bar, span_tma + (P.test_wait ? 16u : 0u));
                 if (span_tma) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + it->span_lo, span_tma, bar);
             }
             __syncwarp();
             if (PK) stage_span_packed(P, slot, lane);
             if (lane == 0) {
-                wr = slot_wait_ex(P, it, bar);
+                wr = slot_wait_ex(P, it, bar, phase);
                 if (wr == WAIT_OK) trace_at(P, item, 5);
             }
             wr = __shfl_sync(0xffffffffu, wr, 0);
+            phase ^= 1u;
         }
         __syncwarp();
         if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
