@@ -75,14 +75,16 @@ typedef struct pv_blk_group {
  * reference's decode of that block would. The diagonal cache entries are stored as c + PV_CKPT_BIAS in 39 bits. */
 typedef struct pv_ckpt {
     uint32_t xs;          /* rANS state (24 bits) | previous kind + 1 << 24 (3 bits) | diagonal count - 1 << 27 (2 bits) */
-    uint32_t p;           /* stream bytes consumed (from the block stream's first byte) */
+    uint32_t p;           /* bits 0..31 of the position in the pooled payload of the next stream byte to read (or, with
+                           * PV_CKPT_CACHED, the block's row in pv_dev_cohort.cache) */
     uint32_t clo[4];      /* diagonal k (most recent first): bits 0..31 of c + PV_CKPT_BIAS */
     uint8_t chi[4];       /* bits 32..38 of c + PV_CKPT_BIAS | strand << 7 */
     uint16_t o;           /* block offset of the event boundary */
-    uint16_t flags;       /* PV_CKPT_BAD */
+    uint16_t flags;       /* PV_CKPT_BAD, PV_CKPT_CACHED | bits 32..39 of the payload position << 8 */
 } pv_ckpt;
 #define PV_CKPT_BIAS (1ll << 20)
-#define PV_CKPT_BAD 1u
+#define PV_CKPT_BAD 1u        /* the block failed to decode */
+#define PV_CKPT_CACHED 2u     /* the block is served from the block cache (no decoder state) */
 
 /* The pooled cohort as the window kernel reads it (device addresses). Built on the host by pv_core_pools() and
  * uploaded by the caller; it replaces the reference's pooled tensors P, pay_base, off, st, tab, blk_base, nbases,

@@ -76,6 +76,7 @@ struct __align__(16) Item {
     uint32_t tab_bytes, span_len;   // span_len: bytes of the reference staged in the slot (from position span_lo)
     int64_t span_lo;
     uint64_t ck;            // its decode's starting checkpoint in the cohort's index, or NO_CK (the block's start)
+    uint64_t cpos;          // that checkpoint's stream position in the pooled payload
     int64_t cst;            // the current diagonal c << 1 | dir where the decode starts (the spans follow it)
     uint32_t co;            // the block offset where the decode starts
     uint32_t jc, wx0, wx1;  // its cell of the block; the window's bytes in the block [wx0, wx1)
@@ -342,13 +343,15 @@ __device__ __forceinline__ void dec_init(Dec<S>& d, const S& src, int64_t st) {
     d.st.skip(3);
 }
 
-// The decoder at a checkpoint of the cohort's index (include/panvram_b200.h pv_ckpt): st reads the block's stream from
-// its first byte; the checkpoint says how far it had been consumed.
+// The decoder at a checkpoint of the cohort's index (include/panvram_b200.h pv_ckpt): src reads the block's stream from
+// the byte the checkpoint had reached (ck_pos).
 __device__ __forceinline__ uint64_t ck_diag(uint32_t lo, uint32_t hi) { return (((uint64_t)(hi & 0x7Fu) << 32) | lo) - (uint64_t)PV_CKPT_BIAS; }
+// a checkpoint's stream position in the pooled payload: p, and bits 32..39 in its flags' high byte
+__device__ __forceinline__ uint64_t ck_pos(uint32_t p, uint32_t ow) { return ((uint64_t)(ow >> 24) << 32) | p; }
 template <class S>
 __device__ __forceinline__ void dec_init_ck(Dec<S>& d, const S& src, const pv_ckpt* ck) {
     const uint4 a = __ldg((const uint4*)ck), b = __ldg((const uint4*)ck + 1);
-    d.st = src; d.st.skip(a.y); d.bad = 0;
+    d.st = src; d.bad = 0;
     d.x = a.x & 0xFFFFFFu; d.pk = (a.x >> 24) & 7u; d.nc = (int)((a.x >> 27) & 3u) + 1;
     d.o = b.w & 0xFFFFu; d.li = 0;
     d.c0 = ck_diag(a.z, b.z); d.c1 = ck_diag(a.w, b.z >> 8); d.c2 = ck_diag(b.x, b.z >> 16); d.c3 = ck_diag(b.y, b.z >> 24);
@@ -863,7 +866,12 @@ __device__ void item_ckpt(const Params& P, Item* it) {
     const uint64_t k = (it->gblk << ncs) + it->jc;
     const pv_ckpt* ck = C.ckpt + k;
     const uint32_t ow = __ldg((const uint32_t*)ck + 7);            // o | flags << 16
-    if (ow >> 16) { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); return; }
+    if (ow & (PV_CKPT_BAD << 16)) { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); return; }
+    if (ow & (PV_CKPT_CACHED << 16)) {              // (reached when the block table was not read): the cell range
+        it->state = ST_CACHED;
+        it->cptr = C.cache + (uint64_t)__ldg((const uint32_t*)ck + 1) * C.Q;
+        return;
+    }
     const uint32_t o0 = ow & 0xFFFFu;
     const bool last = it->jc == ((it->wx1 - 1) >> P.cshift);
     uint32_t o1 = it->wx1;
@@ -875,6 +883,7 @@ __device__ void item_ckpt(const Params& P, Item* it) {
     it->ox1 = o1;
     if (it->ox0 >= it->ox1) { it->state = ST_IDLE; return; }
     it->ck = k; it->co = o0;
+    it->cpos = ck_pos(__ldg((const uint32_t*)ck + 1), ow);
     const uint4 b = __ldg((const uint4*)ck + 1);
     const uint32_t lo = __ldg((const uint32_t*)ck + 2);
     it->cst = (int64_t)(ck_diag(lo, b.z) << 1) | (int64_t)((b.z >> 7) & 1u);
@@ -1055,7 +1064,7 @@ __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
     const uint32_t sp = smem_addr(slot_pay(P, slot)) + (uint32_t)((uintptr_t)(P.C.payload + it->poff) & 15);
     Dec<SmemStream> d;
     uint32_t stop = it->blen;
-    if (it->ck != NO_CK) { dec_init_ck(d, SmemStream{sp, sp + it->plen}, P.C.ckpt + it->ck); stop = it->ox1; }
+    if (it->ck != NO_CK) { dec_init_ck(d, SmemStream{sp + (uint32_t)(it->cpos - it->poff), sp + it->plen}, P.C.ckpt + it->ck); stop = it->ox1; }
     else dec_init(d, SmemStream{sp, sp + it->plen}, it->pst);
     const int r = decode_events(d, SmemTab{smem_addr(slot_tab(P, slot))}, slot_ref<PK>(P, slot), it->blen, stop, sk);
     trace_at(P, it->idx, 3);
@@ -1241,30 +1250,42 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
     Item* it = plan + i;
     trace_at(P, i, 0);
     if (!item_locate(P, i, it)) return;
-    item_block_lane<CP>(P, it);
-    if (P.C.ckpt && it->state == ST_LOCATED) item_ckpt(P, it);
-    if (it->state == ST_LOCATED || it->state == ST_CACHED) item_runs(P, it);
+    const pv_dev_cohort& C = P.C;
+    // with a checkpoint index the item's checkpoint says everything the decode needs (block validated or not, served
+    // from the cache or not, its stream position); the block table is read only for the general path. The lower-case
+    // runs are found by the emission kernel, off this lane's serial chain.
+    if (C.ckpt) item_ckpt(P, it);
+    else item_block_lane<CP>(P, it);
     trace_at(P, i, 1);
     if (it->state != ST_LOCATED) return;
     item_span(P, it, false, ~0ull);              // (L2 only: any length)
-    const pv_dev_cohort& C = P.C;
     if (!PK && it->span_len)
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(C.ref + it->span_lo), "r"(it->span_len) : "memory");
-    if (P.force_block) { it->state = ST_HEAVY; return; }
-    const uint8_t* src = C.payload + it->poff;
-    WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
-    Dec<GlobalStream> d;
-    uint32_t stop = it->blen;
-    if (it->ck != NO_CK) { dec_init_ck(d, GlobalStream{src, src + it->plen}, C.ckpt + it->ck); stop = it->ox1; }
-    else dec_init(d, GlobalStream{src, src + it->plen}, it->pst);
-    const RefView R{C.ref, C.ref_n, 0, 0, 0, PK ? C.pref : nullptr, C.pruns, C.pidx};
-    trace_at(P, i, 2);
-    const int r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, stop, sk);
-    trace_at(P, i, 3);
-    it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
+    int r = DEC_ABORT;
+    if (!P.force_block) {
+        WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
+        Dec<GlobalStream> d;
+        uint32_t stop = it->blen;
+        if (it->ck != NO_CK) {
+            // a validated block decoded from its checkpoint to the item's end reads no further than its stream
+            const uint8_t* src = C.payload + it->cpos;
+            dec_init_ck(d, GlobalStream{src, src + (1u << 24)}, C.ckpt + it->ck);
+            stop = it->ox1;
+        } else {
+            const uint8_t* src = C.payload + it->poff;
+            dec_init(d, GlobalStream{src, src + it->plen}, it->pst);
+        }
+        const RefView R{C.ref, C.ref_n, 0, 0, 0, PK ? C.pref : nullptr, C.pruns, C.pidx};
+        trace_at(P, i, 2);
+        r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, stop, sk);
+        trace_at(P, i, 3);
+        it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
+    }
     if (r == DEC_DONE) it->state = ST_OK;
-    else if (r == DEC_ABORT) it->state = ST_HEAVY;
-    else { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
+    else if (r == DEC_ABORT) {                   // the general path decodes the block from its start: its record
+        if (C.ckpt) item_block_lane<CP>(P, it);
+        if (it->state == ST_LOCATED) it->state = ST_HEAVY;
+    } else { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
 }
 
 // pv_emit_kernel: persistent - as many CTAs as are resident at once - and each WARP on its own takes the next item
@@ -1316,6 +1337,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
                 const uint32_t span_tma = PK ? 0u : it->span_len;
                 mbar_expect(bar, span_tma + (P.test_wait ? 16u : 0u));
                 if (span_tma) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + it->span_lo, span_tma, bar);
+                item_runs(P, it);                       // (while the copy is in flight)
             }
             __syncwarp();
             if (PK) stage_span_packed(P, slot, lane);
@@ -1326,6 +1348,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
             wr = __shfl_sync(0xffffffffu, wr, 0);
             phase ^= 1u;
         }
+        else if (st0 == ST_CACHED && lane == 0) item_runs(P, it);
         __syncwarp();
         if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
         else if (it->state == ST_CACHED) emit_cached(P, it, lane);
@@ -1361,7 +1384,7 @@ __global__ void __launch_bounds__(CTA) pv_heavy_kernel(const __grid_constant__ P
         const uint4* src = (const uint4*)(plan + item);
         for (uint32_t k = threadIdx.x; k < sizeof(Item) / 16; k += CTA) ((uint4*)it)[k] = __ldg(src + k);
         __syncthreads();
-        if (threadIdx.x == 0) { it->span_len = 0; it->span_lo = 0; }   // the reference from global memory
+        if (threadIdx.x == 0) { it->span_len = 0; it->span_lo = 0; item_runs(P, it); }   // the reference from global memory
         __syncthreads();
         heavy_item<PK, true>(P, slot, buf, hops);
         if (threadIdx.x == 0) trace_done(P, it, 2);
@@ -1375,7 +1398,7 @@ __global__ void __launch_bounds__(CTA) pv_heavy_kernel(const __grid_constant__ P
 // dec_init_ck unpacks it).
 struct CkptSink {
     uint4* out;                  // the block's checkpoints, two uint4 each
-    const uint8_t* base;         // the block stream's first byte
+    const uint8_t* base;         // the pooled payload's first byte
     uint32_t cs, ncell, jn;      // stride shift, checkpoints per block, the next one to write
     uint4 sa, sb;                // the last event boundary's state
     __device__ __forceinline__ void put(uint32_t j) { out[2 * j] = sa; out[2 * j + 1] = sb; }
@@ -1384,11 +1407,12 @@ struct CkptSink {
         const uint64_t c[4] = {d.c0 + (uint64_t)PV_CKPT_BIAS, d.c1 + (uint64_t)PV_CKPT_BIAS, d.c2 + (uint64_t)PV_CKPT_BIAS,
                                d.c3 + (uint64_t)PV_CKPT_BIAS};
         sa.x = d.x | (d.pk << 24) | ((uint32_t)(d.nc - 1) << 27);
-        sa.y = (uint32_t)(d.st.p - base);
+        const uint64_t pos = (uint64_t)(d.st.p - base);
+        sa.y = (uint32_t)pos;
         sa.z = (uint32_t)c[0]; sa.w = (uint32_t)c[1]; sb.x = (uint32_t)c[2]; sb.y = (uint32_t)c[3];
         sb.z = ((uint32_t)(c[0] >> 32) & 0x7Fu) | (d.d0 << 7) | ((((uint32_t)(c[1] >> 32) & 0x7Fu) | (d.d1 << 7)) << 8) |
                ((((uint32_t)(c[2] >> 32) & 0x7Fu) | (d.d2 << 7)) << 16) | ((((uint32_t)(c[3] >> 32) & 0x7Fu) | (d.d3 << 7)) << 24);
-        sb.w = d.o;
+        sb.w = d.o | (uint32_t)(((pos >> 32) & 0xFFu) << 24);
     }
     __device__ bool more() const { return true; }
     __device__ bool lit(uint32_t, uint8_t) { return true; }
@@ -1414,11 +1438,15 @@ __global__ void __launch_bounds__(128) pv_index_kernel(const pv_dev_cohort C, ui
         brun[i] = (uint32_t)lo;
     }
     const BlockRec r = block_rec<CP>(C, i, __ldg(&R.grp_base), b);
-    if (r.cache) return;                            // served from the block cache: never decoded by windows
+    if (r.cache) {                                  // served from the block cache: its row, for every cell
+        const uint32_t slot = (uint32_t)((uint64_t)(r.cache - C.cache) >> qs);
+        for (uint32_t j = 0; j < ncell; j++) { o[2 * j] = make_uint4(0, slot, 0, 0); o[2 * j + 1] = make_uint4(0, 0, 0, PV_CKPT_CACHED << 16); }
+        return;
+    }
     int res = DEC_ERR;
     if (CP || r.plen != (uint32_t)PV_BLEN_BAD) {
         const uint8_t* src = C.payload + r.poff;
-        CkptSink sk{o, src, cs, ncell, 0, make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+        CkptSink sk{o, C.payload, cs, ncell, 0, make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
         Dec<GlobalStream> d;
         dec_init(d, GlobalStream{src, src + r.plen}, r.pst);
         const RefView V{C.ref, C.ref_n, 0, 0, 0, PK ? C.pref : nullptr, C.pruns, C.pidx};
