@@ -359,12 +359,15 @@ __device__ __forceinline__ void dec_init_ck(Dec<S>& d, const S& src, const pv_ck
 }
 
 // The event loop of refrel3.h:114-160, from the decoder's state (a block's start or a checkpoint) until the output
-// reaches `stop` (blen: the whole block, with the end-of-stream checks of refrel3.h:157; less: an item's range of a
-// block the cohort's index has validated, so the decode ends with the event that reaches `stop`). Sinks: at(d) sees
-// the state at each event boundary, more() is asked before each event (false pauses, resumable), lit()/op()
+// reaches `stop`. From a block's start with stop = blen it is the whole block, with the end-of-stream checks of
+// refrel3.h:157; from a checkpoint (validated: the cohort's index decoded the block in full at open) it is an item's
+// range, ending with the event that reaches `stop`, and the end-of-stream checks are not repeated (the stream's end
+// may not be known: a decode from a checkpoint can read the pooled payload with no end but its padding). Sinks: at(d)
+// sees the state at each event boundary, more() is asked before each event (false pauses, resumable), lit()/op()
 // returning false abort the decode (the caller takes another path). Returns DEC_*.
 template <class S, class Sink, class Tb>
-__device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefView& R, uint32_t blen, uint32_t stop, Sink& sk) {
+__device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefView& R, uint32_t blen, uint32_t stop, Sink& sk,
+                                             bool validated = false) {
     const uint64_t ref_n = R.n;
     if (d.bad) return DEC_ERR;
     while (d.o < stop) {
@@ -433,7 +436,7 @@ __device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefVi
         if (!sk.op(okind, osrc, d.o, L)) return DEC_ABORT;
         d.o += L; d.pk = kind + 1;
     }
-    if (d.o < blen) return DEC_DONE;                 // stopped inside a validated block
+    if (d.o < blen || validated) return DEC_DONE;    // stopped inside a validated block, or at its end
     if (d.bad || d.x != RANS_L || d.st.left() != 0) return DEC_ERR;
     return DEC_DONE;
 }
@@ -1066,7 +1069,7 @@ __device__ void item_decode(const Params& P, uint8_t* slot, uint32_t bar) {
     uint32_t stop = it->blen;
     if (it->ck != NO_CK) { dec_init_ck(d, SmemStream{sp + (uint32_t)(it->cpos - it->poff), sp + it->plen}, P.C.ckpt + it->ck); stop = it->ox1; }
     else dec_init(d, SmemStream{sp, sp + it->plen}, it->pst);
-    const int r = decode_events(d, SmemTab{smem_addr(slot_tab(P, slot))}, slot_ref<PK>(P, slot), it->blen, stop, sk);
+    const int r = decode_events(d, SmemTab{smem_addr(slot_tab(P, slot))}, slot_ref<PK>(P, slot), it->blen, stop, sk, it->ck != NO_CK);
     trace_at(P, it->idx, 3);
     it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     if (r == DEC_DONE) it->state = ST_OK;
@@ -1277,7 +1280,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
         }
         const RefView R{C.ref, C.ref_n, 0, 0, 0, PK ? C.pref : nullptr, C.pruns, C.pidx};
         trace_at(P, i, 2);
-        r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, stop, sk);
+        r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, stop, sk, it->ck != NO_CK);
         trace_at(P, i, 3);
         it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     }
