@@ -26,10 +26,18 @@ def test_expired_wait_reports_status_4(golden, cuda, oracle, oracle_cohorts, for
     asm, start = torch.from_numpy(a.astype(np.int64)).to(cuda), torch.from_numpy(s.astype(np.int64)).to(cuda)
     ws = torch.zeros((n + 3) // 4 * 4, dtype=torch.uint8, device=cuda)
     with torch.cuda.device(cuda):
-        _, st = _C.windows_cuda(c._devc, asm, start, W, None, False, True, flags=flags | _C.PV_WIN_TEST_WAIT, wstatus=ws)
+        x_t, st = _C.windows_cuda(c._devc, asm, start, W, None, False, True, flags=flags | _C.PV_WIN_TEST_WAIT, wstatus=ws)
         torch.cuda.synchronize(cuda)
     assert int(st.item()) == 4
-    assert (ws[:n].cpu().numpy() == 4).all()              # every window stages copies (no block cache): every one expired
+    want = oracle.windows(arcs, ref, a, s, W, threads=4)
+    got_ws = ws[:n].cpu().numpy()
+    # every item that stages copies (all of them without the block cache, but those the general path decodes: the split
+    # form's pv_heavy_kernel reads global memory and has no such wait) expired; a window none of whose items waited
+    # reports nothing and has its bytes
+    assert set(np.unique(got_ws)) <= {0, 4} and (got_ws == 4).mean() > 0.8
+    quiet = np.nonzero(got_ws == 0)[0]
+    if len(quiet):
+        assert np.array_equal(x_t.cpu().numpy()[quiet], want[quiet])
     x, st = c._launch(asm, start, W, None, False, True, flags=flags)
     assert int(st.item()) == 0
-    assert np.array_equal(x.cpu().numpy(), oracle.windows(arcs, ref, a, s, W, threads=4))
+    assert np.array_equal(x.cpu().numpy(), want)
