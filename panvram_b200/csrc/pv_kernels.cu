@@ -782,10 +782,13 @@ __device__ __forceinline__ void mbar_init(uint32_t bar) {
 __device__ __forceinline__ void mbar_expect(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
 }
+// one try: the thread is suspended until the phase completes or about WAIT_TRY_NS have passed (so a waiting lane
+// issues a handful of instructions per microsecond, not a spin loop's worth)
+constexpr uint32_t WAIT_TRY_NS = 1000;
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t phase) {
     uint32_t ok;
-    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-                 : "=r"(ok) : "r"(bar), "r"(phase) : "memory");
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(phase), "n"(WAIT_TRY_NS) : "memory");
     return ok != 0;
 }
 // global -> shared, 16-byte aligned addresses and a multiple of 16 bytes, completing on `bar`
@@ -793,9 +796,9 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
-constexpr uint32_t WAIT_SPINS = 1u << 22;   // bounded wait on a bulk copy (milliseconds); then status 4
-constexpr uint32_t TEST_WAIT_SPINS = 1u << 10;   // the same under PV_WIN_TEST_WAIT, so the test's wait expires soon
-constexpr uint32_t DRAIN_SPINS = 1u << 24;  // after an expired wait: the bound on waiting for the copies to land
+constexpr uint32_t WAIT_SPINS = 1u << 13;   // tries of a bounded wait on a bulk copy (milliseconds); then status 4
+constexpr uint32_t TEST_WAIT_SPINS = 1u << 6;   // the same under PV_WIN_TEST_WAIT, so the test's wait expires soon
+constexpr uint32_t DRAIN_SPINS = 1u << 20;  // after an expired wait: the bound on waiting for the copies to land (~1 s)
 
 // Programmatic dependent launch: the window kernels are launched so that their CTAs may be scheduled while the kernel
 // before them on the stream is still running; each waits here, before it reads anything that kernel wrote, until it
