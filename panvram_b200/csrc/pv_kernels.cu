@@ -513,9 +513,6 @@ __device__ __forceinline__ uint32_t bytes_mask(int k0, int k1, int i) {   // byt
     const uint32_t m = (hi - lo) == 4 ? 0xFFFFFFFFu : ((1u << (8 * (hi - lo))) - 1);
     return m << (8 * lo);
 }
-__device__ __forceinline__ void merge16(uint32_t r[4], const uint32_t v[4], int k0, int k1) {
-#pragma unroll
-    for (int i = 0; i < 4; i++) { const uint32_t m = bytes_mask(k0, k1, i); r[i] = (r[i] & ~m) | (v[i] & m); }
 }
 // 16 bytes from any address (16-byte aligned loads on both sides, funnel-shifted)
 __device__ __forceinline__ void ldg16u(const uint8_t* p, uint32_t v[4]) {
@@ -730,12 +727,23 @@ __device__ void emit(const Params& P, const Item* it, const Gather& gather, int 
 // kernels' instruction cache footprint)
 __device__ __noinline__ void emit_cached(const Params& P, const Item* it, int lane) { emit(P, it, CacheGather{it->cptr}, lane, 32); }
 
+// bytes j.. of 16 (j in 0..15) taken from u: the ops of an item tile its range in order, so each op that starts inside
+// a chunk overwrites it from its start on, and the next one overwrites from its own start
+__device__ __forceinline__ void merge_from(uint32_t v[4], const uint32_t u[4], int j) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int sh = j - 4 * i;
+        const uint32_t m = sh <= 0 ? 0xFFFFFFFFu : sh >= 4 ? 0u : 0xFFFFFFFFu << (8 * sh);
+        v[i] = (v[i] & ~m) | (u[i] & m);
+    }
+}
+
 // A decoded item's output, in one pass over the 16-byte chunks of the output row that its range [A, B) touches: lane i
 // takes every 32nd chunk, in the order of the block offsets they read (the output order reversed for a
-// reverse-complemented window), with a cursor into the ops that only moves forward. A chunk inside one op (most of
-// them) is that op's 16 source bytes; a chunk around op boundaries merges the bytes of each op it overlaps. Then case /
-// reverse complement / tokens in registers and one 16-byte store - or, for the chunks at the ends of [A, B), the bytes
-// inside it.
+// reverse-complemented window), with a cursor into the ops that only moves forward. A chunk is the 16 source bytes of
+// the op covering its first byte, overwritten from their starts by the bytes of any further ops that start inside it
+// (op boundaries: an SNV is a one-base literal between two copies). Then case / reverse complement / tokens in
+// registers and one 16-byte store - or, for the chunks at the ends of [A, B), the bytes inside it.
 __device__ void emit_ops(const Params& P, const Item* it, const RefView& R, int lane) {
     const OutRange g = out_range(P, it);
     const int64_t W = (int64_t)P.W;
@@ -753,21 +761,15 @@ __device__ void emit_ops(const Params& P, const Item* it, const RefView& R, int 
         const int64_t klo = blo > ox0 ? blo : ox0, khi = blo + 16 < ox1 ? blo + 16 : ox1;
         while (k < nops && (int64_t)op_dst(it->ops[k]) + it->ops[k].len <= klo) k++;
         if (k >= nops) break;
-        const Op o = it->ops[k];
         uint32_t v[4];
-        if ((int64_t)op_dst(o) <= klo && (int64_t)op_dst(o) + o.len >= khi) {
-            op_src16(it, R, lits_sm, o, blo, v);          // one op covers every byte of the chunk the item writes
-        } else {
-            v[0] = v[1] = v[2] = v[3] = 0;
-            for (int kk = k; kk < nops; kk++) {
-                const Op q = it->ops[kk];
-                const int64_t dst = op_dst(q);
-                if (dst >= khi) break;
-                const int64_t a = dst > klo ? dst : klo, e = dst + q.len < khi ? dst + q.len : khi;
-                uint32_t u[4];
-                op_src16(it, R, lits_sm, q, blo, u);
-                merge16(v, u, (int)(a - blo), (int)(e - blo));
-            }
+        op_src16(it, R, lits_sm, it->ops[k], blo, v);
+        for (int kk = k + 1; kk < nops; kk++) {
+            const Op q = it->ops[kk];
+            const int64_t dst = op_dst(q);
+            if (dst >= khi) break;
+            uint32_t u[4];
+            op_src16(it, R, lits_sm, q, blo, u);
+            merge_from(v, u, (int)(dst - blo));
         }
         put16(P, it, g, (uintptr_t)c, wpf, v, false);
     }
