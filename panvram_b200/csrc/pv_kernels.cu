@@ -513,7 +513,6 @@ __device__ __forceinline__ uint32_t bytes_mask(int k0, int k1, int i) {   // byt
     const uint32_t m = (hi - lo) == 4 ? 0xFFFFFFFFu : ((1u << (8 * (hi - lo))) - 1);
     return m << (8 * lo);
 }
-}
 // 16 bytes from any address (16-byte aligned loads on both sides, funnel-shifted)
 __device__ __forceinline__ void ldg16u(const uint8_t* p, uint32_t v[4]) {
     const uintptr_t a = (uintptr_t)p;
@@ -540,7 +539,6 @@ __device__ __forceinline__ void lds16u(uint32_t a, uint32_t v[4]) {
 #pragma unroll
     for (int i = 0; i < 4; i++) v[i] = __funnelshift_r(w[i], w[i + 1], sh);
 }
-// 16 reference bytes from position q: from the staged span when it holds all of them, else global memory
 // the four letters of four 2-bit codes (8 bits) as bytes
 __device__ __forceinline__ uint32_t letters4(uint32_t c8) {
     const uint32_t sel = (c8 & 3u) | ((c8 & 0xCu) << 2) | ((c8 & 0x30u) << 4) | ((c8 & 0xC0u) << 6);
@@ -573,9 +571,6 @@ __device__ __noinline__ uint4 packed16(const uint32_t* pw, const pv_ref_run* run
     }
     return make_uint4(v[0], v[1], v[2], v[3]);
 }
-__device__ __forceinline__ void ref16(const RefView& R, int64_t q, uint32_t v[4]) {
-    if (q >= R.lo && q - R.lo + 16 <= (int64_t)R.len) lds16u(R.sm + (uint32_t)(q - R.lo), v);
-    else if (R.pw) { const uint4 u = packed16(R.pw, R.runs, R.pidx, R.n, q); v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; }
     else ldg16u(R.g + q, v);
 }
 
@@ -584,19 +579,23 @@ __device__ __forceinline__ void ref16(const RefView& R, int64_t q, uint32_t v[4]
 // bytes the op does cover). Literal bytes come from the item's literal array in shared memory (lits_sm: its address;
 // the bytes around it are other fields of the slot, read but never used), reference bytes from the staged span or
 // global memory, reverse-complement copies byte-reversed and complemented.
+// (one load path for every kind, its address chosen by selects - the lanes of a pass often hold ops of different
+// kinds - then the byte reversal and complement of a reverse-complement copy)
 __device__ __forceinline__ void op_src16(const Item* it, const RefView& R, uint32_t lits_sm, const Op& o, int64_t blo, uint32_t v[4]) {
     const int64_t dst = op_dst(o), len = o.len;
     const uint32_t kind = op_kind(o);
-    if (kind == 1) {
-        ref16(R, (int64_t)o.src + (blo - dst), v);
-    } else if (kind == 3) {
-        ref16(R, (int64_t)o.src + len - 1 - (blo - dst) - 15, v);
+    const bool lit = kind == 0, rev = kind == 3;
+    const int64_t q = rev ? (int64_t)o.src + len - 16 - (blo - dst) : (int64_t)o.src + (blo - dst);   // a copy's first byte
+    const int64_t first = dst > (int64_t)it->ox0 ? dst : (int64_t)it->ox0;
+    const bool in_span = lit || (q >= R.lo && q - R.lo + 16 <= (int64_t)R.len);
+    const uint32_t sa = lit ? lits_sm + (uint32_t)((int64_t)o.src + (blo - first)) : R.sm + (uint32_t)(q - R.lo);
+    if (in_span) lds16u(sa, v);
+    else if (R.pw) { const uint4 u = packed16(R.pw, R.runs, R.pidx, R.n, q); v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; }
+    else ldg16u(R.g + q, v);
+    if (rev) {
         rev16(v);
 #pragma unroll
         for (int i = 0; i < 4; i++) v[i] = comp4(v[i]);
-    } else {
-        const int64_t first = dst > (int64_t)it->ox0 ? dst : (int64_t)it->ox0;
-        lds16u(lits_sm + (uint32_t)((int64_t)o.src + (blo - first)), v);
     }
 }
 struct BufGather {
@@ -701,10 +700,14 @@ __device__ __forceinline__ void put16(const Params& P, const Item* it, const Out
     }
     if (whole || (ca >= g.A && ca + 16 <= g.B)) {
         *(uint4*)ca = make_uint4(v[0], v[1], v[2], v[3]);
-    } else {
-        for (int k = 0; k < 16; k++) {
-            const uintptr_t q = ca + (uintptr_t)k;
-            if (q >= g.A && q < g.B) *(uint8_t*)q = (uint8_t)(v[k >> 2] >> (8 * (k & 3)));
+    } else {                                        // an end of the range: its bytes, whole words as words
+        const int lo = ca < g.A ? (int)(g.A - ca) : 0, hi = ca + 16 > g.B ? (int)(g.B - ca) : 16;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int a = lo > 4 * i ? lo : 4 * i, b = hi < 4 * i + 4 ? hi : 4 * i + 4;
+            if (a == 4 * i && b == 4 * i + 4) *(uint32_t*)(ca + 4 * i) = v[i];
+            else
+                for (int k = a; k < b; k++) *(uint8_t*)(ca + k) = (uint8_t)(v[i] >> (8 * (k - 4 * i)));
         }
     }
 }
