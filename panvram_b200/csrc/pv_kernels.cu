@@ -571,8 +571,6 @@ __device__ __noinline__ uint4 packed16(const uint32_t* pw, const pv_ref_run* run
     }
     return make_uint4(v[0], v[1], v[2], v[3]);
 }
-    else ldg16u(R.g + q, v);
-}
 
 // ---------------------------------------------------------------- gathers: raw block bytes [blo, blo + 16)
 // 16 source bytes of op o for block offsets [blo, blo + 16), as if the op covered all of them (the caller keeps the
