@@ -225,7 +225,8 @@ size_t pv_windows_work_bytes(const pv_dev_cohort* cohort, int64_t n, int64_t W);
 /* For testing the expired-wait path (status 4) without a fault: every kernel's bounded wait on its shared-memory bulk
  * copies is made to expire - its barrier expects 16 bytes that no copy brings, and the wait's bound is short - so each
  * item that stages copies reports PV_STATUS_WAIT and writes nothing; the kernel then completes the missing 16 bytes with
- * one more copy and waits until every copy has landed before it returns. The context stays usable. */
+ * one more copy and waits until every copy has landed before it returns. The context stays usable. Only the one-kernel
+ * form (pv_windows_kernel) stages copies; the split form's kernels wait on none, and there the flag changes nothing. */
 #define PV_WIN_TEST_WAIT 16u
 /* the split form's decode warps: PV_WIN_DEC_LANES(k) runs k items per warp (one per lane, k in 1..32) instead of
  * the size rule's choice; the output is the same */

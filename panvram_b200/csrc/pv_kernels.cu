@@ -577,19 +577,29 @@ __device__ __noinline__ uint4 packed16(const uint32_t* pw, const pv_ref_run* run
 // bytes the op does cover). Literal bytes come from the item's literal array in shared memory (lits_sm: its address;
 // the bytes around it are other fields of the slot, read but never used), reference bytes from the staged span or
 // global memory, reverse-complement copies byte-reversed and complemented.
+// Where an item's literal bytes are: in its shared slot (lits_sm, a shared address) or, for the emission kernel that
+// reads decoded items in place, in the plan in global memory (lits_g).
+struct LitSrc { uint32_t sm; const uint8_t* g; };
 // (one load path for every kind, its address chosen by selects - the lanes of a pass often hold ops of different
 // kinds - then the byte reversal and complement of a reverse-complement copy)
-__device__ __forceinline__ void op_src16(const Item* it, const RefView& R, uint32_t lits_sm, const Op& o, int64_t blo, uint32_t v[4]) {
+template <bool LG>
+__device__ __forceinline__ void op_src16(const Item* it, const RefView& R, const LitSrc& L, const Op& o, int64_t blo, uint32_t v[4]) {
     const int64_t dst = op_dst(o), len = o.len;
     const uint32_t kind = op_kind(o);
     const bool lit = kind == 0, rev = kind == 3;
     const int64_t q = rev ? (int64_t)o.src + len - 16 - (blo - dst) : (int64_t)o.src + (blo - dst);   // a copy's first byte
     const int64_t first = dst > (int64_t)it->ox0 ? dst : (int64_t)it->ox0;
-    const bool in_span = lit || (q >= R.lo && q - R.lo + 16 <= (int64_t)R.len);
-    const uint32_t sa = lit ? lits_sm + (uint32_t)((int64_t)o.src + (blo - first)) : R.sm + (uint32_t)(q - R.lo);
-    if (in_span) lds16u(sa, v);
-    else if (R.pw) { const uint4 u = packed16(R.pw, R.runs, R.pidx, R.n, q); v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; }
-    else ldg16u(R.g + q, v);
+    const int64_t li = (int64_t)o.src + (blo - first);                                                 // a literal's
+    if (LG) {                                       // no span: literals and the byte reference from global memory
+        if (lit || !R.pw) ldg16u(lit ? L.g + li : R.g + q, v);
+        else { const uint4 u = packed16(R.pw, R.runs, R.pidx, R.n, q); v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; }
+    } else {
+        const bool in_span = lit || (q >= R.lo && q - R.lo + 16 <= (int64_t)R.len);
+        const uint32_t sa = lit ? L.sm + (uint32_t)li : R.sm + (uint32_t)(q - R.lo);
+        if (in_span) lds16u(sa, v);
+        else if (R.pw) { const uint4 u = packed16(R.pw, R.runs, R.pidx, R.n, q); v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; }
+        else ldg16u(R.g + q, v);
+    }
     if (rev) {
         rev16(v);
 #pragma unroll
@@ -744,12 +754,13 @@ __device__ __forceinline__ void merge_from(uint32_t v[4], const uint32_t u[4], i
 // reverse-complemented window), with a cursor into the ops that only moves forward. A chunk is the 16 source bytes of
 // the op covering its first byte, overwritten from their starts by the bytes of any further ops that start inside it
 // (op boundaries: an SNV is a one-base literal between two copies). Then case / reverse complement / tokens in
-// registers and one 16-byte store - or, for the chunks at the ends of [A, B), the bytes inside it.
-__device__ void emit_ops(const Params& P, const Item* it, const RefView& R, int lane) {
+// registers and one 16-byte store - or, for the chunks at the ends of [A, B), the bytes inside it. it: the item's header
+// (shared slot); ops / literal bytes in the slot too, or (LG) read in place from the item's record in the plan.
+template <bool LG>
+__device__ void emit_ops(const Params& P, const Item* it, const Op* ops, const LitSrc& L, const RefView& R, int lane) {
     const OutRange g = out_range(P, it);
     const int64_t W = (int64_t)P.W;
     const int64_t base = (int64_t)(uintptr_t)g.row;    // chunks are 16-byte aligned in memory, not in the row
-    const uint32_t lits_sm = smem_addr(it->lits);
     const int nops = it->nops;
     const int64_t ox0 = it->ox0, ox1 = it->ox1;
     const int64_t c0 = (int64_t)g.A & ~(int64_t)15, c1 = ((int64_t)g.B + 15) & ~(int64_t)15;
@@ -760,16 +771,17 @@ __device__ void emit_ops(const Params& P, const Item* it, const RefView& R, int 
         const int64_t wpf = g.rcw ? W - 16 - (c - base) : c - base;
         const int64_t blo = wpf + g.delta;                  // block offset of the chunk's first forward byte
         const int64_t klo = blo > ox0 ? blo : ox0, khi = blo + 16 < ox1 ? blo + 16 : ox1;
-        while (k < nops && (int64_t)op_dst(it->ops[k]) + it->ops[k].len <= klo) k++;
+        Op o;
+        while (k < nops && (int64_t)op_dst(o = ops[k]) + o.len <= klo) k++;
         if (k >= nops) break;
         uint32_t v[4];
-        op_src16(it, R, lits_sm, it->ops[k], blo, v);
+        op_src16<LG>(it, R, L, o, blo, v);
         for (int kk = k + 1; kk < nops; kk++) {
-            const Op q = it->ops[kk];
+            const Op q = ops[kk];
             const int64_t dst = op_dst(q);
             if (dst >= khi) break;
             uint32_t u[4];
-            op_src16(it, R, lits_sm, q, blo, u);
+            op_src16<LG>(it, R, L, q, blo, u);
             merge_from(v, u, (int)(dst - blo));
         }
         put16(P, it, g, (uintptr_t)c, wpf, v, false);
@@ -1175,7 +1187,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constan
         }
     }
     __syncwarp();
-    if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
+    if (it->state == ST_OK) emit_ops<false>(P, it, it->ops, LitSrc{smem_addr(it->lits), nullptr}, slot_ref<PK>(P, slot), lane);
     else if (it->state == ST_CACHED) emit_cached(P, it, lane);
     __syncwarp();
     if (lane == 0 && item < P.total && it->state != ST_HEAVY) trace_done(P, it, 1);
@@ -1297,25 +1309,54 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
     } else { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
 }
 
-// pv_emit_kernel: persistent - as many CTAs as are resident at once - and each WARP on its own takes the next item
-// from the queue, copies its decoded Item from the plan into its shared slot (the header, then only the ops and literal
-// bytes it holds), stages the reference span under its output range (TMA bulk copy, bounded wait), and writes it. A
-// warp that finishes takes the next item at once: no CTA-wide barrier, so a slow item holds up no other warp. Items
-// that need the general path are listed for pv_heavy_kernel.
+// The warp: the lower-case runs overlapping an item's output range, as item_runs finds them, eight candidate runs per
+// step read by eight lanes at once (from the block's first run: usually one step).
+__device__ void item_runs_warp(const Params& P, Item* it, int lane) {
+    const pv_dev_cohort& C = P.C;
+    const pv_asm_rec& R = C.asms[it->a];
+    const uint64_t cnt = R.low_cnt;
+    if (!(P.apply_case && !P.tokens && cnt)) return;
+    if (!C.brun) { if (lane == 0) item_runs(P, it); __syncwarp(); return; }
+    const uint64_t x0 = it->bst + it->ox0, x1 = it->bst + it->ox1, s = it->s;
+    const uint64_t* low = C.low + 2 * R.low_base;
+    const uint64_t r0 = __ldg(C.brun + it->gblk);
+    uint64_t first = cnt, last = cnt;               // the runs [first, last) ending after x0 and starting before x1
+    for (uint64_t base = r0; base < cnt; base += 32) {
+        const uint64_t r = base + lane;
+        const bool have = r < cnt;
+        const uint64_t rs = have ? __ldg(low + 2 * r) : ~0ull, re = have ? __ldg(low + 2 * r + 1) : ~0ull;
+        const uint32_t after = __ballot_sync(0xffffffffu, have && re > x0);
+        const uint32_t past = __ballot_sync(0xffffffffu, !have || rs >= x1);
+        if (first == cnt && after) first = base + __ffs(after) - 1;
+        if (past) { last = base + __ffs(past) - 1; break; }
+    }
+    if (first > last) first = last;
+    if (lane == 0) { it->run_first = (uint32_t)(R.low_base + first); it->run_cnt = (uint32_t)(last - first); }
+    if (last - first <= (uint64_t)RUN_CAP && (uint64_t)lane < last - first) {
+        const uint64_t r = first + lane, rs = __ldg(low + 2 * r), re = __ldg(low + 2 * r + 1);
+        it->runs[2 * lane] = (int32_t)((rs > x0 ? rs : x0) - s);
+        it->runs[2 * lane + 1] = (int32_t)((re < x1 ? re : x1) - s);
+    }
+    __syncwarp();
+}
+
+// pv_emit_kernel: persistent - as many CTAs as are resident at once - and each WARP on its own takes the next decoded
+// item from the queue and writes it: the item's header is copied into the warp's small shared slot (its lower-case
+// runs are found there by the warp), its ops and literal bytes are read in place from the plan, and the reference
+// bytes from global memory, where the decode kernel has just warmed the item's span into L2 - no staging and no wait,
+// so a warp goes from one item to the next at once, and a slot is a few hundred bytes (many warps per SM). A warp
+// that finishes takes the next item: no CTA-wide barrier. Items that need the general path are listed for
+// pv_heavy_kernel.
+constexpr int EMIT_SLOT = ITEM_HEAD16 * 16;
 template <bool PK>
-__global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__ Params P, const Item* plan, WorkQueue* q, uint64_t* heavy) {
+__global__ void __launch_bounds__(CTA, 8) pv_emit_kernel(const __grid_constant__ Params P, const Item* plan, WorkQueue* q, uint64_t* heavy) {
     extern __shared__ uint4 smem_raw[];
-    __shared__ __align__(8) uint64_t bars[WARPS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_trigger();                                  // pv_heavy_kernel's CTAs may be placed now; they wait for this grid
     pdl_wait();
-    uint8_t* slot = (uint8_t*)smem_raw + (size_t)warp * P.slot_bytes;
-    Item* it = slot_item(slot);
-    const uint32_t bar = smem_addr(&bars[warp]);
+    Item* it = (Item*)((uint8_t*)smem_raw + (size_t)warp * EMIT_SLOT);   // (the header part of an Item only)
     const pv_dev_cohort& C = P.C;
-    if (lane == 0) mbar_init(bar);                  // once: the warp's items use its phases one after another
-    __syncwarp();
-    uint32_t phase = 0;
+    const RefView R{C.ref, C.ref_n, 0, 0, 0, PK ? C.pref : nullptr, C.pruns, C.pidx};
     for (uint64_t round = 0; round <= P.total; round++) {      // (bounded: every round takes an item or ends)
         uint64_t item = 0;
         if (lane == 0) item = atomicAdd(&q->next, 1ull);
@@ -1323,14 +1364,8 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
         if (item >= P.total) break;
         if (lane == 0) trace_at(P, item, 4);
         const Item* pi = plan + item;
-        const uint32_t nops = min((uint32_t)__ldg(&pi->nops), (uint32_t)OPS_CAP), nlits = min((uint32_t)__ldg(&pi->nlits), (uint32_t)LIT_CAP);
-        const uint32_t no16 = (nops * (uint32_t)sizeof(Op) + 15) / 16, nl16 = (nlits + 15) / 16;
         const uint4* src = (const uint4*)pi;
-        uint4* dst = (uint4*)it;
-        for (uint32_t k = lane; k < ITEM_HEAD16 + no16 + nl16; k += 32) {
-            const uint32_t w = k < ITEM_HEAD16 + no16 ? k : ITEM_LITS16 + (k - ITEM_HEAD16 - no16);
-            dst[w] = __ldg(src + w);
-        }
+        for (uint32_t k = lane; k < ITEM_HEAD16; k += 32) ((uint4*)it)[k] = __ldg(src + k);
         __syncwarp();
         const int st0 = it->state;
         if (st0 == ST_HEAVY) {
@@ -1338,32 +1373,14 @@ __global__ void __launch_bounds__(CTA, 6) pv_emit_kernel(const __grid_constant__
             __syncwarp();
             continue;
         }
-        int wr = WAIT_OK;
-        if (st0 == ST_OK) {
-            if (lane == 0) {
-                // the span the emission reads: the decode's starting diagonal under the item's output range only
-                item_span(P, it, true, P.span_cap);
-                const uint32_t span_tma = PK ? 0u : it->span_len;
-                mbar_expect(bar, span_tma + (P.test_wait ? 16u : 0u));
-                if (span_tma) bulk_g2s(smem_addr(slot_span(P, slot)), C.ref + it->span_lo, span_tma, bar);
-                item_runs(P, it);                       // (while the copy is in flight)
-            }
-            __syncwarp();
-            if (PK) stage_span_packed(P, slot, lane);
-            if (lane == 0) {
-                wr = slot_wait_ex(P, it, bar, phase);
-                if (wr == WAIT_OK) trace_at(P, item, 5);
-            }
-            wr = __shfl_sync(0xffffffffu, wr, 0);
-            phase ^= 1u;
+        if (st0 == ST_OK || st0 == ST_CACHED) {
+            item_runs_warp(P, it, lane);
+            if (lane == 0) trace_at(P, item, 5);
+            if (st0 == ST_OK) emit_ops<true>(P, it, pi->ops, LitSrc{0, pi->lits}, R, lane);
+            else emit_cached(P, it, lane);
         }
-        else if (st0 == ST_CACHED && lane == 0) item_runs(P, it);
         __syncwarp();
-        if (it->state == ST_OK) emit_ops(P, it, slot_ref<PK>(P, slot), lane);
-        else if (it->state == ST_CACHED) emit_cached(P, it, lane);
-        __syncwarp();
-        if (lane == 0 && it->state != ST_IDLE) trace_done(P, it, 2);
-        if (wr == WAIT_STUCK) break;               // a copy may still land in this slot: the warp takes no more items
+        if (lane == 0 && st0 != ST_IDLE) trace_done(P, it, 2);
         __syncwarp();
     }
 }
@@ -1830,14 +1847,14 @@ static int launch_windows(const pv_dev_cohort* cohort, const int64_t* asm_index,
     P.span_cap = (uint32_t)((span + 2 * SPAN_MARGIN + 64 + 15) & ~15ull);
     P.slot_bytes = (uint32_t)sizeof(Item) + P.tab_area + P.pay_cap + P.span_cap;
     const size_t smem = (size_t)WARPS * P.slot_bytes;
-    // the emission kernel's slot: no stream, no table (its general path reads it through L1), and a span of the output
-    // range's diagonal only (min(W, Q) + margins)
+    // the emission kernel's slot: an item's header only (its ops and literal bytes are read in place, the reference
+    // from global memory); pv_heavy_kernel's: a whole Item, no span (it reads the reference from global memory)
     Params PE = P;
     PE.pay_cap = 0;
     PE.tab_area = 0;
-    PE.span_cap = P.span_cap;
-    PE.slot_bytes = (uint32_t)sizeof(Item) + PE.span_cap;
-    const size_t smem_e = (size_t)WARPS * PE.slot_bytes;
+    PE.span_cap = 0;
+    PE.slot_bytes = (uint32_t)sizeof(Item);
+    const size_t smem_e = (size_t)WARPS * EMIT_SLOT;
     Params PH = PE;                                 // pv_heavy_kernel: its CTAs' block buffers after the list
     PH.work = hbuf;
     const int form = (cohort->packed ? 1 : 0) | (cohort->compact ? 2 : 0);

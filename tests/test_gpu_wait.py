@@ -1,7 +1,9 @@
 """Status bit 4, the bounded wait that expired (the reference's semantics: pv_cuda.cu:20,26,78), without a fault: with
 PV_WIN_TEST_WAIT every kernel's wait on its shared-memory bulk copies expects 16 bytes no copy brings, so it expires;
 each window reports 4, the kernel completes the missing bytes with one more copy and waits until every copy has landed,
-and returns. The process stays healthy: the next call on the same stream gives the oracle's windows."""
+and returns. The process stays healthy: the next call on the same stream gives the oracle's windows. Only the one-kernel
+form stages copies; the split form's kernels read global memory and wait on nothing, so there the flag changes nothing
+(status 0, the oracle's windows)."""
 import numpy as np
 import pytest
 import torch
@@ -28,16 +30,14 @@ def test_expired_wait_reports_status_4(golden, cuda, oracle, oracle_cohorts, for
     with torch.cuda.device(cuda):
         x_t, st = _C.windows_cuda(c._devc, asm, start, W, None, False, True, flags=flags | _C.PV_WIN_TEST_WAIT, wstatus=ws)
         torch.cuda.synchronize(cuda)
-    assert int(st.item()) == 4
     want = oracle.windows(arcs, ref, a, s, W, threads=4)
     got_ws = ws[:n].cpu().numpy()
-    # every item that stages copies (all of them without the block cache, but those the general path decodes: the split
-    # form's pv_heavy_kernel reads global memory and has no such wait) expired; a window none of whose items waited
-    # reports nothing and has its bytes
-    assert set(np.unique(got_ws)) <= {0, 4} and (got_ws == 4).mean() > 0.8
-    quiet = np.nonzero(got_ws == 0)[0]
-    if len(quiet):
-        assert np.array_equal(x_t.cpu().numpy()[quiet], want[quiet])
+    if form == "split":
+        assert int(st.item()) == 0 and (got_ws == 0).all() and np.array_equal(x_t.cpu().numpy(), want)
+    else:
+        # every item stages copies without the block cache (but those the general path decodes, after the wait):
+        # every window reports 4
+        assert int(st.item()) == 4 and (got_ws == 4).all()
     x, st = c._launch(asm, start, W, None, False, True, flags=flags)
     assert int(st.item()) == 0
     assert np.array_equal(x.cpu().numpy(), want)
