@@ -19,6 +19,15 @@ import torch
 from . import _C
 
 DATASETS = ("q4k", "q16k")
+# torch releases (major.minor) whose randint / rand CUDA kernels (launch geometry, Philox state per thread, element
+# order, transforms) the coordinate kernel's restatement of them was checked against bit for bit
+# (tests/test_gpu_coords.py). With any other torch, sample() and Cohort.sampler make the draws with torch's own calls:
+# the same coordinates, at the cost of their launches.
+TORCH_DRAWS_CHECKED = ("2.11",)
+
+
+def _native_draws():
+    return ".".join(torch.__version__.split("+")[0].split(".")[:2]) in TORCH_DRAWS_CHECKED
 STATUS_TEXT = "GPU decode failed (status {}: 1 corrupt block, 4 bounded wait expired, 8 window outside an assembly)"
 
 
@@ -392,7 +401,8 @@ class Cohort:
         mode, p = _strand_mode(reverse_complement)
         u = r = None
         gen = None
-        if rng is None and gdev.type == "cuda" and (gdev.index or 0) == (dev.index or 0) and not torch.cuda.is_current_stream_capturing():
+        if (rng is None and gdev.type == "cuda" and (gdev.index or 0) == (dev.index or 0) and not torch.cuda.is_current_stream_capturing()
+                and _native_draws()):
             # outside stream capture the draws are made in the coordinate kernel, from the generator's seed and offset,
             # exactly as torch.randint / torch.rand would make them; the generator is then advanced as they would
             gen = generator if generator is not None else torch.cuda.default_generators[dev.index or 0]
@@ -540,9 +550,10 @@ class Sampler:
     """A captured sample() call (Cohort.sampler): call k returns what the k-th eager sample() call with the same
     generator would (windows, coordinates, status), and advances the generator as that call would. The graph makes the
     draws itself (pv_sample_draw_coords: torch's randint / rand kernels restated in the coordinate kernel, from a device
-    copy of the generator's seed and offset that the graph advances), so a replay is two launches and needs no
-    generator bookkeeping on the device; if the generator is used or reseeded between calls, the next call reloads its
-    state."""
+    copy of the generator's seed and offset that the graph advances), so a replay needs no generator bookkeeping on the
+    device; if the generator is used or reseeded between calls, the next call reloads its state. With a torch release
+    that restatement was not checked against (TORCH_DRAWS_CHECKED), the graph captures torch's own randint / rand
+    instead, and torch advances the generator at each replay."""
 
     def __init__(self, cohort, n, W, generator, reverse_complement, tokens, return_coords):
         if generator is None or generator.device.type != "cuda":
@@ -564,15 +575,17 @@ class Sampler:
             props = torch.cuda.get_device_properties(dev)
             _, _, self._inc = _C.torch_draw_geometry(n, cohort._valid[W][2], mode, props.multi_processor_count,
                                                      getattr(props, "max_threads_per_multi_processor", 2048))
+            self.native = _native_draws()
             self._rng = torch.zeros(3, dtype=torch.int64, device=dev)
             self._seed = self._offset = None
-            self._load_rng()
+            if self.native:
+                self._load_rng()
             self.graph = torch.cuda.CUDAGraph()
             self._acc = torch.zeros(1, dtype=torch.int32, device=dev)
             events, cohort.kernel_events = cohort.kernel_events, None
             try:
                 with torch.cuda.graph(self.graph):
-                    self.x, self.coords, _ = cohort._draw(*args, status=self._acc, rng=self._rng)
+                    self.x, self.coords, _ = cohort._draw(*args, status=self._acc, rng=self._rng if self.native else None)
             finally:
                 cohort.kernel_events = events
 
@@ -586,6 +599,9 @@ class Sampler:
 
     def __call__(self):
         with torch.cuda.device(self.cohort.device):
+            if not self.native:                          # torch's draws in the graph: torch advances the generator
+                self.graph.replay()
+                return (self.x, self.coords) if self.return_coords else self.x
             self._load_rng()
             self.graph.replay()
         self._offset += self._inc
