@@ -581,6 +581,8 @@ class Sampler:
             if self.native:
                 self._load_rng()
             self.graph = torch.cuda.CUDAGraph()
+            if not self.native:                          # torch's draws captured: the graph advances this generator
+                self.graph.register_generator_state(generator)
             self._acc = torch.zeros(1, dtype=torch.int32, device=dev)
             events, cohort.kernel_events = cohort.kernel_events, None
             try:
