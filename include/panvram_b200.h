@@ -120,6 +120,9 @@ typedef struct pv_dev_cohort {
     /* per pooled block, its assembly's first lower-case run (index from the assembly's low_base) that ends after the
      * block's start (pv_index_build), or NULL: then the window kernels binary-search the runs */
     const uint32_t* brun;
+    /* the reference reverse-complemented (pv_rc_reference: rcref[i] = complement of ref[ref_n - 1 - i]), 64 readable
+     * bytes on each side, or NULL: with it a reverse-complement copy is read forward from it (byte form only) */
+    const uint8_t* rcref;
 } pv_dev_cohort;
 
 /* Block table word 0 of a block served from pv_dev_cohort.cache: cache slot | PV_BLOCK_CACHED << 40 (the payload
@@ -320,6 +323,11 @@ size_t pv_index_bytes(uint32_t Q, uint64_t nblocks, uint32_t ckpt_shift);
  * blocks' first lower-case runs (pv_dev_cohort.brun). Asynchronous on `stream`. */
 int pv_index_build(const pv_dev_cohort* cohort, uint64_t nblocks, uint32_t ckpt_shift, pv_ckpt* out, uint64_t* nbad, uint32_t* brun,
                    void* stream);
+
+/* out[i] = the complement of ref[n - 1 - i] (A <-> T, C <-> G, every other byte as it is), i < n: the reverse-complement
+ * reference of pv_dev_cohort.rcref (no counterpart in the reference, which reverses and complements each copied byte).
+ * Device pointers; asynchronous on `stream`. */
+int pv_rc_reference(const uint8_t* ref, uint64_t n, uint8_t* out, void* stream);
 
 /* ---- device: the whole-assembly checks (Cohort.check_full / fasta, panvram/cohort.py:224-234, whose FASTA rebuild
  * and XXH3 run on the host in the reference, pv_core.cpp:138-176) ---- */

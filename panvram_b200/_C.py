@@ -38,7 +38,8 @@ class DevCohort(ctypes.Structure):
                 ("pref", ctypes.c_void_p), ("pruns", ctypes.c_void_p), ("pidx", ctypes.c_void_p), ("pnruns", ctypes.c_uint64),
                 ("groups", ctypes.c_void_p), ("btab", ctypes.c_void_p), ("bexc", ctypes.c_void_p),
                 ("packed", ctypes.c_uint32), ("compact", ctypes.c_uint32),
-                ("ckpt", ctypes.c_void_p), ("ckpt_shift", ctypes.c_uint32), ("pad2", ctypes.c_uint32), ("brun", ctypes.c_void_p)]
+                ("ckpt", ctypes.c_void_p), ("ckpt_shift", ctypes.c_uint32), ("pad2", ctypes.c_uint32), ("brun", ctypes.c_void_p),
+                ("rcref", ctypes.c_void_p)]
 
 
 class HostPools(ctypes.Structure):
@@ -107,6 +108,7 @@ for _name, _res, _args in (
         ("pv_torch_draw_geometry", _I32, [_I64, _U64, _I32, _I32, _I32, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)]),
         ("pv_index_bytes", _SZ, [_U32, _U64, _U32]),
         ("pv_windows_items", _SZ, [ctypes.POINTER(DevCohort), _I64, _I64]),
+        ("pv_rc_reference", _I32, [_P, _U64, _P, _P]),
         ("pv_windows_trace", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _U32, _P, _P, _P, _SZ, _P, _SZ, _P]),
         ("pv_index_build", _I32, [ctypes.POINTER(DevCohort), _U64, _U32, _P, _P, _P, _P])):
     _f = getattr(_lib, _name)
@@ -523,6 +525,17 @@ def index_build(dev, nblocks, ckpt_shift, device):
             raise RuntimeError("panvram_b200 index: " + (_lib.pv_kernels_last_error() or b"").decode())
         torch.cuda.current_stream(device).synchronize()
     return out, brun, int(nbad.item())
+
+
+def rc_reference(ref_padded, n, device):
+    """The reverse-complement reference (pv_rc_reference) of a device reference (ref_padded: the uint8 tensor with 64
+    bytes before the first base), in a tensor with the same 64-byte padding on each side."""
+    out = torch.zeros(int(n) + 128, dtype=torch.uint8, device=device)
+    with torch.cuda.device(device):
+        code = _lib.pv_rc_reference(ref_padded.data_ptr() + 64, int(n), out.data_ptr() + 64, torch.cuda.current_stream(device).cuda_stream)
+    if code:
+        raise RuntimeError("panvram_b200 reverse-complement reference: " + (_lib.pv_kernels_last_error() or b"").decode())
+    return out
 
 
 def read_status(status):

@@ -117,6 +117,12 @@ class Cohort:
         stride = self.CHECKPOINT_STRIDE if checkpoint_stride is None else int(checkpoint_stride)
         if stride:
             self._build_index(min(stride, core.Q))
+        # the reference reverse-complemented, for the byte form: the split emission reads reverse-complement copies
+        # forward from it (one more copy of the reference, ref_n bytes)
+        self._rcref = None
+        if not packed:
+            self._rcref = _C.rc_reference(self._dev["ref_padded"], core.ref_bases, self.device)
+            self._devc.rcref = self._rcref.data_ptr() + 64
 
     def _build_index(self, stride):
         """The checkpoint index (pv_index_build): every block not in the block cache decoded once on the device, its
@@ -289,7 +295,7 @@ class Cohort:
         d = self._dev
         nb = lambda *ks: sum(d[k].numel() * d[k].element_size() for k in ks if k in d)
         r = {"P": nb("payload"), "blocks": nb("blocks", "groups", "btab", "bexc"), "tab": nb("tabs"), "low": nb("low"),
-             "ref": nb("ref_padded", "pref", "pruns", "pidx"), "asm": nb("asms"),
+             "ref": nb("ref_padded", "pref", "pruns", "pidx") + (self._rcref.numel() if self._rcref is not None else 0), "asm": nb("asms"),
              "cache": self._cache.numel() if self._cache is not None else 0,
              "index": (self._ckpt.numel() + 4 * self._brun.numel()) if self._ckpt is not None else 0}
         r["total"] = sum(r.values())

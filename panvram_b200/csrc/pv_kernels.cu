@@ -518,14 +518,14 @@ __device__ __forceinline__ void ldg16u(const uint8_t* p, uint32_t v[4]) {
     const uintptr_t a = (uintptr_t)p;
     const uint4* q = (const uint4*)(a & ~(uintptr_t)15);
     const uint32_t sh = (uint32_t)(a & 15);
-    const uint4 lo = __ldg(q);
-    if (sh == 0) { v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w; return; }
-    const uint4 hi = __ldg(q + 1);
+    const uint4 lo = __ldg(q), hi = __ldg(q + 1);  // (both, whatever the shift: no branch for the lanes to split on)
     const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
     const uint32_t j = sh >> 2, b = (sh & 3) * 8;
-    uint32_t x[5];
+    uint32_t y[6], x[5];                            // words j .. j + 4: shifted by two words, then by one
 #pragma unroll
-    for (int i = 0; i < 5; i++) x[i] = j == 0 ? w[i] : j == 1 ? w[i + 1] : j == 2 ? w[i + 2] : w[(i + 3) & 7];
+    for (int i = 0; i < 6; i++) y[i] = (j & 2) ? w[i + 2] : w[i];
+#pragma unroll
+    for (int i = 0; i < 5; i++) x[i] = (j & 1) ? y[i + 1] : y[i];
 #pragma unroll
     for (int i = 0; i < 4; i++) v[i] = __funnelshift_r(x[i], x[i + 1], b);
 }
@@ -579,7 +579,7 @@ __device__ __noinline__ uint4 packed16(const uint32_t* pw, const pv_ref_run* run
 // global memory, reverse-complement copies byte-reversed and complemented.
 // Where an item's literal bytes are: in its shared slot (lits_sm, a shared address) or, for the emission kernel that
 // reads decoded items in place, in the plan in global memory (lits_g).
-struct LitSrc { uint32_t sm; const uint8_t* g; };
+struct LitSrc { uint32_t sm; const uint8_t* g; const uint8_t* rc; };   // (rc: the cohort's reverse-complement reference, or NULL)
 // (one load path for every kind, its address chosen by selects - the lanes of a pass often hold ops of different
 // kinds - then the byte reversal and complement of a reverse-complement copy)
 template <bool LG>
@@ -591,6 +591,10 @@ __device__ __forceinline__ void op_src16(const Item* it, const RefView& R, const
     const int64_t first = dst > (int64_t)it->ox0 ? dst : (int64_t)it->ox0;
     const int64_t li = (int64_t)o.src + (blo - first);                                                 // a literal's
     if (LG) {                                       // no span: literals and the byte reference from global memory
+        if (rev && L.rc) {                          // read forward from the reverse-complement reference: done
+            ldg16u(L.rc + ((int64_t)R.n - (int64_t)o.src - len + (blo - dst)), v);
+            return;
+        }
         if (lit || !R.pw) ldg16u(lit ? L.g + li : R.g + q, v);
         else { const uint4 u = packed16(R.pw, R.runs, R.pidx, R.n, q); v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; }
     } else {
@@ -686,11 +690,13 @@ __device__ __noinline__ void store_ids(int64_t* out64, int64_t i0, int64_t i1, i
 __device__ __forceinline__ void put16(const Params& P, const Item* it, const OutRange& g, uintptr_t ca, int64_t wpf, uint32_t v[4], bool whole) {
     if (g.cased) {
         const uint32_t m = case_mask(it, P.C.low, wpf);
+        if (m) {
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint32_t m4 = (m >> (4 * i)) & 15u;
-            const uint32_t bm = (m4 & 1u) * 0xFFu | (m4 & 2u) * 0x7F80u | (m4 & 4u) * 0x3FC000u | (m4 & 8u) * 0x1FE00000u;
-            v[i] |= bm & 0x20202020u;
+            for (int i = 0; i < 4; i++) {
+                const uint32_t m4 = (m >> (4 * i)) & 15u;
+                const uint32_t bm = (m4 & 1u) * 0xFFu | (m4 & 2u) * 0x7F80u | (m4 & 4u) * 0x3FC000u | (m4 & 8u) * 0x1FE00000u;
+                v[i] |= bm & 0x20202020u;
+            }
         }
     }
     if (P.tokens) {
@@ -759,32 +765,36 @@ __device__ __forceinline__ void merge_from(uint32_t v[4], const uint32_t u[4], i
 template <bool LG>
 __device__ void emit_ops(const Params& P, const Item* it, const Op* ops, const LitSrc& L, const RefView& R, int lane) {
     const OutRange g = out_range(P, it);
-    const int64_t W = (int64_t)P.W;
-    const int64_t base = (int64_t)(uintptr_t)g.row;    // chunks are 16-byte aligned in memory, not in the row
+    // offsets inside a window and a block fit 32 bits (W < 2^31, blocks <= 2^14 bases): the loop's arithmetic is 32-bit,
+    // only the chunk addresses are 64-bit
+    const int32_t W = (int32_t)P.W, delta = (int32_t)g.delta, ox0 = (int32_t)it->ox0, ox1 = (int32_t)it->ox1;
+    const uintptr_t c0 = g.A & ~(uintptr_t)15, c1 = (g.B + 15) & ~(uintptr_t)15, row = (uintptr_t)g.row;
+    const int32_t nch = (int32_t)((c1 - c0) >> 4);
+    const int32_t r0 = (int32_t)((intptr_t)c0 - (intptr_t)row), r1 = (int32_t)((intptr_t)c1 - (intptr_t)row);   // row offsets
     const int nops = it->nops;
-    const int64_t ox0 = it->ox0, ox1 = it->ox1;
-    const int64_t c0 = (int64_t)g.A & ~(int64_t)15, c1 = ((int64_t)g.B + 15) & ~(int64_t)15;
-    const int64_t nch = (c1 - c0) >> 4;
     int k = 0;
-    for (int64_t i = lane; i < nch; i += 32) {
-        const int64_t c = g.rcw ? c1 - 16 - 16 * i : c0 + 16 * i;
-        const int64_t wpf = g.rcw ? W - 16 - (c - base) : c - base;
-        const int64_t blo = wpf + g.delta;                  // block offset of the chunk's first forward byte
-        const int64_t klo = blo > ox0 ? blo : ox0, khi = blo + 16 < ox1 ? blo + 16 : ox1;
+    for (int32_t i = lane; i < nch; i += 32) {
+        const int32_t ro = g.rcw ? r1 - 16 - 16 * i : r0 + 16 * i;       // the chunk's offset in the row
+        const int32_t wpf = g.rcw ? W - 16 - ro : ro;                    // window position of its first forward byte
+        const int32_t blo = wpf + delta;                                  // and block offset
+        const int32_t klo = blo > ox0 ? blo : ox0, khi = blo + 16 < ox1 ? blo + 16 : ox1;
         Op o;
-        while (k < nops && (int64_t)op_dst(o = ops[k]) + o.len <= klo) k++;
+        for (; k < nops; k++) {                     // the op covering the chunk's first byte the item writes
+            o = ops[k];
+            if ((int32_t)(op_dst(o) + o.len) > klo) break;
+        }
         if (k >= nops) break;
         uint32_t v[4];
         op_src16<LG>(it, R, L, o, blo, v);
         for (int kk = k + 1; kk < nops; kk++) {
             const Op q = ops[kk];
-            const int64_t dst = op_dst(q);
+            const int32_t dst = (int32_t)op_dst(q);
             if (dst >= khi) break;
             uint32_t u[4];
             op_src16<LG>(it, R, L, q, blo, u);
-            merge_from(v, u, (int)(dst - blo));
+            merge_from(v, u, dst - blo);
         }
-        put16(P, it, g, (uintptr_t)c, wpf, v, false);
+        put16(P, it, g, (uintptr_t)((intptr_t)row + ro), wpf, v, false);
     }
 }
 
@@ -1187,7 +1197,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constan
         }
     }
     __syncwarp();
-    if (it->state == ST_OK) emit_ops<false>(P, it, it->ops, LitSrc{smem_addr(it->lits), nullptr}, slot_ref<PK>(P, slot), lane);
+    if (it->state == ST_OK) emit_ops<false>(P, it, it->ops, LitSrc{smem_addr(it->lits), nullptr, nullptr}, slot_ref<PK>(P, slot), lane);
     else if (it->state == ST_CACHED) emit_cached(P, it, lane);
     __syncwarp();
     if (lane == 0 && item < P.total && it->state != ST_HEAVY) trace_done(P, it, 1);
@@ -1376,7 +1386,7 @@ __global__ void __launch_bounds__(CTA, 8) pv_emit_kernel(const __grid_constant__
         if (st0 == ST_OK || st0 == ST_CACHED) {
             item_runs_warp(P, it, lane);
             if (lane == 0) trace_at(P, item, 5);
-            if (st0 == ST_OK) emit_ops<true>(P, it, pi->ops, LitSrc{0, pi->lits}, R, lane);
+            if (st0 == ST_OK) emit_ops<true>(P, it, pi->ops, LitSrc{0, pi->lits, PK ? nullptr : C.rcref}, R, lane);
             else emit_cached(P, it, lane);
         }
         __syncwarp();
@@ -1979,6 +1989,22 @@ int pv_sample_draw_coords(const int64_t* cum, const int64_t* valid, const int64_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- the reverse-complement reference (pv_rc_reference)
+__global__ void __launch_bounds__(256) pv_rc_reference_kernel(const uint8_t* ref, uint64_t n, uint8_t* out) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = comp_up(ref[n - 1 - i]);
+}
+
+extern "C" int pv_rc_reference(const uint8_t* ref, uint64_t n, uint8_t* out, void* stream) {
+    if (n == 0) return PV_OK;
+    if (!ref || !out) { snprintf(g_cuda_err, sizeof g_cuda_err, "pv_rc_reference: arguments"); return PV_EARG; }
+    pv_rc_reference_kernel<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(ref, n, out);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
+    return PV_OK;
+}
 
 // ---------------------------------------------------------------- the checkpoint index: host side
 extern "C" size_t pv_index_bytes(uint32_t Q, uint64_t nblocks, uint32_t ckpt_shift) {
