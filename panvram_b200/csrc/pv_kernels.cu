@@ -591,9 +591,9 @@ __device__ __forceinline__ void op_src16(const Item* it, const RefView& R, const
     const int64_t first = dst > (int64_t)it->ox0 ? dst : (int64_t)it->ox0;
     const int64_t li = (int64_t)o.src + (blo - first);                                                 // a literal's
     if (LG) {                                       // no span: literals and the byte reference from global memory
-        if (rev && L.rc) {                          // read forward from the reverse-complement reference: done
-            ldg16u(L.rc + ((int64_t)R.n - (int64_t)o.src - len + (blo - dst)), v);
-            return;
+        if (L.rc) {                                 // (byte form) one load for every kind: a reverse-complement copy
+            ldg16u(lit ? L.g + li : rev ? L.rc + ((int64_t)R.n - (int64_t)o.src - len + (blo - dst)) : R.g + q, v);
+            return;                                 // reads forward from the reverse-complement reference: done
         }
         if (lit || !R.pw) ldg16u(lit ? L.g + li : R.g + q, v);
         else { const uint4 u = packed16(R.pw, R.runs, R.pidx, R.n, q); v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; }
@@ -755,37 +755,62 @@ __device__ __forceinline__ void merge_from(uint32_t v[4], const uint32_t u[4], i
     }
 }
 
-// A decoded item's output, in one pass over the 16-byte chunks of the output row that its range [A, B) touches: lane i
-// takes every 32nd chunk, in the order of the block offsets they read (the output order reversed for a
-// reverse-complemented window), with a cursor into the ops that only moves forward. A chunk is the 16 source bytes of
-// the op covering its first byte, overwritten from their starts by the bytes of any further ops that start inside it
-// (op boundaries: an SNV is a one-base literal between two copies). Then case / reverse complement / tokens in
-// registers and one 16-byte store - or, for the chunks at the ends of [A, B), the bytes inside it. it: the item's header
-// (shared slot); ops / literal bytes in the slot too, or (LG) read in place from the item's record in the plan.
+// A decoded item's output, op by op. The ops of an item tile its range [ox0, ox1) in order; in the output row each op
+// covers a run of bytes (reversed in place for a reverse-complemented window). First, for each op in turn (the same
+// op for the whole warp, so every lane takes the same load path), the 16-byte chunks of the row wholly inside the op's
+// bytes: the lanes share them, each chunk one 16-byte load of the op's source (the reference, the reverse-complement
+// reference, the staged span or the literal bytes) and one 16-byte store after case / reverse complement / tokens in
+// registers. Then the chunks the first pass left: those holding an op boundary, or an end of the item's range, off a
+// 16-byte boundary - one lane each, its bytes gathered from every op it overlaps (the op covering its first byte, then
+// each op starting inside it over it from its start). it: the item's header (shared slot); ops and literal bytes in the
+// slot too, or (LG) read in place from the item's record in the plan.
 template <bool LG>
 __device__ void emit_ops(const Params& P, const Item* it, const Op* ops, const LitSrc& L, const RefView& R, int lane) {
     const OutRange g = out_range(P, it);
-    // offsets inside a window and a block fit 32 bits (W < 2^31, blocks <= 2^14 bases): the loop's arithmetic is 32-bit,
-    // only the chunk addresses are 64-bit
+    // offsets inside a window and a block fit 32 bits (W < 2^31, blocks <= 2^14 bases): the arithmetic is 32-bit, only
+    // the chunk addresses are 64-bit
     const int32_t W = (int32_t)P.W, delta = (int32_t)g.delta, ox0 = (int32_t)it->ox0, ox1 = (int32_t)it->ox1;
-    const uintptr_t c0 = g.A & ~(uintptr_t)15, c1 = (g.B + 15) & ~(uintptr_t)15, row = (uintptr_t)g.row;
-    const int32_t nch = (int32_t)((c1 - c0) >> 4);
-    const int32_t r0 = (int32_t)((intptr_t)c0 - (intptr_t)row), r1 = (int32_t)((intptr_t)c1 - (intptr_t)row);   // row offsets
+    const intptr_t row = (intptr_t)(uintptr_t)g.row;
     const int nops = it->nops;
-    int k = 0;
-    for (int32_t i = lane; i < nch; i += 32) {
-        const int32_t ro = g.rcw ? r1 - 16 - 16 * i : r0 + 16 * i;       // the chunk's offset in the row
-        const int32_t wpf = g.rcw ? W - 16 - ro : ro;                    // window position of its first forward byte
-        const int32_t blo = wpf + delta;                                  // and block offset
-        const int32_t klo = blo > ox0 ? blo : ox0, khi = blo + 16 < ox1 ? blo + 16 : ox1;
-        Op o;
-        for (; k < nops; k++) {                     // the op covering the chunk's first byte the item writes
-            o = ops[k];
-            if ((int32_t)(op_dst(o) + o.len) > klo) break;
+    // pass 1: each op's interior chunks
+    for (int k = 0; k < nops; k++) {
+        const Op o = ops[k];
+        const int32_t d0 = (int32_t)op_dst(o) > ox0 ? (int32_t)op_dst(o) : ox0;
+        const int32_t d1 = (int32_t)(op_dst(o) + o.len) < ox1 ? (int32_t)(op_dst(o) + o.len) : ox1;
+        const int32_t lo = g.rcw ? W - (d1 - delta) : d0 - delta, hi = g.rcw ? W - (d0 - delta) : d1 - delta;   // its row bytes
+        const intptr_t a0 = (row + lo + 15) & ~(intptr_t)15, a1 = (row + hi) & ~(intptr_t)15;
+        for (intptr_t c = a0 + 16 * (intptr_t)lane; c < a1; c += 16 * 32) {
+            const int32_t ro = (int32_t)(c - row);
+            const int32_t wpf = g.rcw ? W - 16 - ro : ro;
+            uint32_t v[4];
+            op_src16<LG>(it, R, L, o, wpf + delta, v);
+            put16(P, it, g, (uintptr_t)c, wpf, v, true);
         }
-        if (k >= nops) break;
+    }
+    // pass 2: the chunks around op boundaries and the ends of the range. Boundary b (0 .. nops) is the row offset where
+    // op b starts (b = 0: the range's first byte in window order) or, b = nops, where the range ends; its chunk is
+    // handled unless the boundary is 16-byte aligned in memory or another boundary's lane already has that chunk.
+    for (int b = lane; b <= nops; b += 32) {
+        const int32_t wb = b == 0 ? ox0 - delta : b == nops ? ox1 - delta : (int32_t)op_dst(ops[b]) - delta;   // window position
+        const int32_t ob = g.rcw ? W - wb : wb;        // the boundary's row offset (a reversed row: its end there)
+        const intptr_t ab = row + ob;
+        const int32_t wprev = b == 0 ? 0 : b - 1 == 0 ? ox0 - delta : (int32_t)op_dst(ops[b - 1]) - delta;
+        const intptr_t aprev = row + (g.rcw ? W - wprev : wprev);
+        if ((ab & 15) == 0 || (b > 0 && (aprev & ~(intptr_t)15) == (ab & ~(intptr_t)15) && (aprev & 15) != 0)) continue;
+        const intptr_t c = ab & ~(intptr_t)15;
+        const int32_t ro = (int32_t)(c - row);
+        const int32_t wpf = g.rcw ? W - 16 - ro : ro;
+        const int32_t blo = wpf + delta;
+        const int32_t klo = blo > ox0 ? blo : ox0, khi = blo + 16 < ox1 ? blo + 16 : ox1;
+        if (klo >= khi) continue;
+        int k = 0, hk = nops;                       // the op covering klo: the first ending after it
+        while (k < hk) {
+            const int m = (k + hk) >> 1;
+            if ((int32_t)(op_dst(ops[m]) + ops[m].len) <= klo) k = m + 1; else hk = m;
+        }
+        if (k >= nops) continue;
         uint32_t v[4];
-        op_src16<LG>(it, R, L, o, blo, v);
+        op_src16<LG>(it, R, L, ops[k], blo, v);
         for (int kk = k + 1; kk < nops; kk++) {
             const Op q = ops[kk];
             const int32_t dst = (int32_t)op_dst(q);
@@ -794,7 +819,7 @@ __device__ void emit_ops(const Params& P, const Item* it, const Op* ops, const L
             op_src16<LG>(it, R, L, q, blo, u);
             merge_from(v, u, dst - blo);
         }
-        put16(P, it, g, (uintptr_t)((intptr_t)row + ro), wpf, v, false);
+        put16(P, it, g, (uintptr_t)c, wpf, v, false);
     }
 }
 
