@@ -164,6 +164,14 @@ struct GlobalStream {
     __device__ __forceinline__ uint32_t left() const { return (uint32_t)(e - p); }
     __device__ __forceinline__ void skip(uint32_t k) { p += k; }
 };
+// a validated block's stream read from a checkpoint: no end to check (the decode to the item's end reads no further
+// than the block's stream, plus the two bytes a step looks ahead, inside the pool's padding)
+struct OpenStream {
+    const uint8_t* p;
+    __device__ __forceinline__ uint32_t peek(uint32_t k) const { return (uint32_t)__ldg(p + k); }
+    __device__ __forceinline__ uint32_t left() const { return 1u << 30; }
+    __device__ __forceinline__ void skip(uint32_t k) { p += k; }
+};
 // The decoder state is all scalar - the four-entry diagonal cache as named registers, indexed by selects - so that,
 // inlined, the block's serial rANS chain stays in registers and never round-trips through local memory.
 template <class S>
@@ -1320,20 +1328,18 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
     int r = DEC_ABORT;
     if (!P.force_block) {
         WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
-        Dec<GlobalStream> d;
-        uint32_t stop = it->blen;
-        if (it->ck != NO_CK) {
-            // a validated block decoded from its checkpoint to the item's end reads no further than its stream
-            const uint8_t* src = C.payload + it->cpos;
-            dec_init_ck(d, GlobalStream{src, src + (1u << 24)}, C.ckpt + it->ck);
-            stop = it->ox1;
-        } else {
-            const uint8_t* src = C.payload + it->poff;
-            dec_init(d, GlobalStream{src, src + it->plen}, it->pst);
-        }
         const RefView R{C.ref, C.ref_n, 0, 0, 0, PK ? C.pref : nullptr, C.pruns, C.pidx};
         trace_at(P, i, 2);
-        r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, stop, sk, it->ck != NO_CK);
+        if (it->ck != NO_CK) {                   // from its checkpoint to the item's end
+            Dec<OpenStream> d;
+            dec_init_ck(d, OpenStream{C.payload + it->cpos}, C.ckpt + it->ck);
+            r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, it->ox1, sk, true);
+        } else {                                 // the whole block, from its start
+            Dec<GlobalStream> d;
+            const uint8_t* src = C.payload + it->poff;
+            dec_init(d, GlobalStream{src, src + it->plen}, it->pst);
+            r = decode_events(d, GlobalTab{C.tabs + it->tab_off}, R, it->blen, it->blen, sk);
+        }
         trace_at(P, i, 3);
         it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     }
