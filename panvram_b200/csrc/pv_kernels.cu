@@ -112,7 +112,7 @@ constexpr uint64_t NO_CK = ~0ull;
 
 // The trace (pv_windows_trace): per item, %globaltimer (ns) when it reaches each phase - 0 start, 1 located (block,
 // checkpoint, case runs), 2 its decode starts (the fused kernel: its slot's copies have landed), 3 decoded, 4 the
-// emission kernel takes it (split form), 5 its span is staged there, 6 emitted - and word 7: SM | state << 8 | form
+// emission kernel takes it (split form), 5 its lower-case runs are found there, 6 emitted - and word 7: SM | state << 8 | form
 // << 12 (1 fused, 2 split) | from a checkpoint << 14 | ops << 16 | literals << 32 | decoded bases << 48.
 __device__ __forceinline__ uint64_t gtime() { uint64_t t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); return t; }
 __device__ __forceinline__ void trace_at(const Params& P, uint64_t item, int k) { if (P.trace) P.trace[item * 8 + k] = gtime(); }
