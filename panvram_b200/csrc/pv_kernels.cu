@@ -51,7 +51,8 @@ constexpr int HOPS = 64;       // ops per chunk on the heavy path
 enum { ST_IDLE = 0, ST_OK = 1, ST_HEAVY = 2, ST_ERR = 3, ST_CACHED = 4, ST_LOCATED = 5 };
 enum { DEC_DONE = 1, DEC_PAUSE = 0, DEC_ERR = -1, DEC_ABORT = -2 };
 
-struct Op { uint32_t src; uint16_t dk; uint16_t len; };   // dk: block offset | kind << 14
+struct Op { uint32_t src; uint16_t dk; uint16_t len; };   // dk: block offset | kind << 14 (8 bytes: src, then dk | len << 16)
+static_assert(sizeof(Op) == 8, "Op is read as two words");
 __device__ __forceinline__ uint32_t op_dst(const Op& o) { return o.dk & 0x3FFFu; }
 __device__ __forceinline__ uint32_t op_kind(const Op& o) { return o.dk >> 14; }
 
@@ -315,14 +316,17 @@ struct RefView {
         return pw ? packed_byte(q) : (uint32_t)__ldg(g + q);
     }
 };
-// the reference base the diagonal predicts at block offset o: 0..3, 4 = none (refrel3.h:104-109)
-__device__ __forceinline__ int refbase(const RefView& R, uint64_t c, uint32_t dir, uint32_t o) {
-    const int64_t q = dir ? (int64_t)c - (int64_t)o : (int64_t)c + (int64_t)o;
-    if (q < 0 || (uint64_t)q >= R.n) return 4;
-    const uint32_t b = R.byte(q);
+// the reference base the diagonal predicts at block offset o: 0..3, 4 = none (refrel3.h:104-109); refcode maps the
+// reference byte b at that position
+__device__ __forceinline__ int refcode(uint32_t b, uint32_t dir) {
     const uint32_t k = ((b >> 1) ^ (b >> 2)) & 3u;                 // A 0, C 1, G 2, T 3 for those letters
     if (((0x54474341u >> (8 * k)) & 0xFFu) != b) return 4;         // not an upper-case A, C, G or T
     return (int)(dir ? k ^ 3u : k);                                // the complement's code on the reverse strand
+}
+__device__ __forceinline__ int refbase(const RefView& R, uint64_t c, uint32_t dir, uint32_t o) {
+    const int64_t q = dir ? (int64_t)c - (int64_t)o : (int64_t)c + (int64_t)o;
+    if (q < 0 || (uint64_t)q >= R.n) return 4;
+    return refcode(R.byte(q), dir);
 }
 template <class S>
 __device__ __forceinline__ void dget(const Dec<S>& d, int k, uint64_t& c, uint32_t& dir) {
@@ -381,6 +385,11 @@ __device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefVi
     while (d.o < stop) {
         sk.at(d);
         if (!sk.more()) return DEC_PAUSE;
+        // the reference byte a first literal's context reads (refbase at d.o), loaded before the LL symbol is decoded
+        // so that its latency overlaps the symbol's table lookups (the byte form; the packed form looks it up after)
+        const int64_t q0 = d.d0 ? (int64_t)d.c0 - (int64_t)d.o : (int64_t)d.c0 + (int64_t)d.o;
+        const bool in0 = q0 >= 0 && (uint64_t)q0 < ref_n;
+        const uint32_t b0 = R.pw ? 0u : R.byte(in0 ? q0 : 0);
         const uint32_t kc = kclass(d.pk);
         const uint32_t ll = dval_big(d, T, (int)kc);                         // LL x previous kind class
         if (d.bad || ll > blen - d.o) return DEC_ERR;
@@ -388,7 +397,8 @@ __device__ __forceinline__ int decode_events(Dec<S>& d, const Tb& T, const RefVi
             uint32_t p1 = 16, p2 = 16;
             for (uint32_t j = 0; j < ll; j++) {
                 int c;
-                if (ll <= 8) c = C_LITR + refbase(R, d.c0, d.d0, d.o + j) * 2 + (j == 0 ? 1 : 0);
+                if (ll <= 8) c = C_LITR + (j == 0 ? (!in0 ? 4 : R.pw ? refbase(R, d.c0, d.d0, d.o) : refcode(b0, d.d0)) * 2 + 1
+                                                  : refbase(R, d.c0, d.d0, d.o + j) * 2);
                 else c = C_LIT2 + (p1 == 16 ? 16 : (int)((p2 == 16 ? p1 : p2 * 4 + p1) % 16));
                 const uint32_t sy = dsym_small(d, T, c);
                 uint32_t byte = sy < 4 ? (0x54474341u >> (8 * sy)) & 0xFFu : (uint32_t)'N';   // A C G T, N
@@ -521,12 +531,22 @@ __device__ __forceinline__ uint32_t bytes_mask(int k0, int k1, int i) {   // byt
     const uint32_t m = (hi - lo) == 4 ? 0xFFFFFFFFu : ((1u << (8 * (hi - lo))) - 1);
     return m << (8 * lo);
 }
-// 16 bytes from any address (16-byte aligned loads on both sides, funnel-shifted)
-__device__ __forceinline__ void ldg16u(const uint8_t* p, uint32_t v[4]) {
+// L2 eviction priorities (createpolicy): evict_last for the reference spans the decode warms for the emission, so that
+// the call's output stores do not push them out first; evict_first for the bytes the emission has read.
+__device__ __forceinline__ uint64_t l2_evict_last() { uint64_t p; asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p)); return p; }
+__device__ __forceinline__ uint64_t l2_evict_first() { uint64_t p; asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p)); return p; }
+__device__ __forceinline__ uint4 ldg_hint(const uint4* q, uint64_t pol) {
+    uint4 v;
+    asm("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(q), "l"(pol));
+    return v;
+}
+// 16 bytes from any address (16-byte aligned loads on both sides, funnel-shifted); pol: an L2 policy for the loads,
+// or 0
+__device__ __forceinline__ void ldg16u(const uint8_t* p, uint32_t v[4], uint64_t pol = 0) {
     const uintptr_t a = (uintptr_t)p;
     const uint4* q = (const uint4*)(a & ~(uintptr_t)15);
     const uint32_t sh = (uint32_t)(a & 15);
-    const uint4 lo = __ldg(q), hi = __ldg(q + 1);  // (both, whatever the shift: no branch for the lanes to split on)
+    const uint4 lo = pol ? ldg_hint(q, pol) : __ldg(q), hi = pol ? ldg_hint(q + 1, pol) : __ldg(q + 1);   // (both, whatever the shift)
     const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
     const uint32_t j = sh >> 2, b = (sh & 3) * 8;
     uint32_t y[6], x[5];                            // words j .. j + 4: shifted by two words, then by one
@@ -587,7 +607,7 @@ __device__ __noinline__ uint4 packed16(const uint32_t* pw, const pv_ref_run* run
 // global memory, reverse-complement copies byte-reversed and complemented.
 // Where an item's literal bytes are: in its shared slot (lits_sm, a shared address) or, for the emission kernel that
 // reads decoded items in place, in the plan in global memory (lits_g).
-struct LitSrc { uint32_t sm; const uint8_t* g; const uint8_t* rc; };   // (rc: the cohort's reverse-complement reference, or NULL)
+struct LitSrc { uint32_t sm; const uint8_t* g; const uint8_t* rc; uint64_t pol; };   // (rc: the cohort's reverse-complement reference, or NULL; pol: an L2 policy for the loads, or 0)
 // (one load path for every kind, its address chosen by selects - the lanes of a pass often hold ops of different
 // kinds - then the byte reversal and complement of a reverse-complement copy)
 template <bool LG>
@@ -600,10 +620,10 @@ __device__ __forceinline__ void op_src16(const Item* it, const RefView& R, const
     const int64_t li = (int64_t)o.src + (blo - first);                                                 // a literal's
     if (LG) {                                       // no span: literals and the byte reference from global memory
         if (L.rc) {                                 // (byte form) one load for every kind: a reverse-complement copy
-            ldg16u(lit ? L.g + li : rev ? L.rc + ((int64_t)R.n - (int64_t)o.src - len + (blo - dst)) : R.g + q, v);
+            ldg16u(lit ? L.g + li : rev ? L.rc + ((int64_t)R.n - (int64_t)o.src - len + (blo - dst)) : R.g + q, v, L.pol);
             return;                                 // reads forward from the reverse-complement reference: done
         }
-        if (lit || !R.pw) ldg16u(lit ? L.g + li : R.g + q, v);
+        if (lit || !R.pw) ldg16u(lit ? L.g + li : R.g + q, v, L.pol);
         else { const uint4 u = packed16(R.pw, R.runs, R.pidx, R.n, q); v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; }
     } else {
         const bool in_span = lit || (q >= R.lo && q - R.lo + 16 <= (int64_t)R.len);
@@ -721,7 +741,7 @@ __device__ __forceinline__ void put16(const Params& P, const Item* it, const Out
         return;
     }
     if (whole || (ca >= g.A && ca + 16 <= g.B)) {
-        *(uint4*)ca = make_uint4(v[0], v[1], v[2], v[3]);
+        __stcs((uint4*)ca, make_uint4(v[0], v[1], v[2], v[3]));      // streaming: the windows are not read here again
     } else {                                        // an end of the range: its bytes, whole words as words
         const int lo = ca < g.A ? (int)(g.A - ca) : 0, hi = ca + 16 > g.B ? (int)(g.B - ca) : 16;
 #pragma unroll
@@ -764,25 +784,33 @@ __device__ __forceinline__ void merge_from(uint32_t v[4], const uint32_t u[4], i
 }
 
 // A decoded item's output, op by op. The ops of an item tile its range [ox0, ox1) in order; in the output row each op
-// covers a run of bytes (reversed in place for a reverse-complemented window). First, for each op in turn (the same
-// op for the whole warp, so every lane takes the same load path), the 16-byte chunks of the row wholly inside the op's
-// bytes: the lanes share them, each chunk one 16-byte load of the op's source (the reference, the reverse-complement
-// reference, the staged span or the literal bytes) and one 16-byte store after case / reverse complement / tokens in
-// registers. Then the chunks the first pass left: those holding an op boundary, or an end of the item's range, off a
-// 16-byte boundary - one lane each, its bytes gathered from every op it overlaps (the op covering its first byte, then
-// each op starting inside it over it from its start). it: the item's header (shared slot); ops and literal bytes in the
-// slot too, or (LG) read in place from the item's record in the plan.
+// covers a run of bytes (reversed in place for a reverse-complemented window). First (emit_op_chunks), for each op in
+// turn (the same op for the whole warp, so every lane takes the same load path), the 16-byte chunks of the row wholly
+// inside the op's bytes: the lanes share them, each chunk one 16-byte load of the op's source (the reference, the
+// reverse-complement reference, the staged span or the literal bytes) and one 16-byte store after case / reverse
+// complement / tokens in registers. Then (emit_boundary) the chunks the first pass left: those holding an op boundary,
+// or an end of the item's range, off a 16-byte boundary - one lane each, its bytes gathered from every op it overlaps
+// (the op covering its first byte, then each op starting inside it over it from its start). it: the item's header
+// (shared slot); ops and literal bytes in the slot too, or (LG) read in place from the item's record in the plan. cit:
+// the header whose lower-case runs cover the item (the item's own, or its group's); g = out_range(P, it).
 template <bool LG>
-__device__ void emit_ops(const Params& P, const Item* it, const Op* ops, const LitSrc& L, const RefView& R, int lane) {
-    const OutRange g = out_range(P, it);
+__device__ __forceinline__ void emit_op_chunks(const Params& P, const Item* it, const Item* cit, const OutRange& g, const Op* ops,
+                                               const LitSrc& L, const RefView& R, int lane) {
     // offsets inside a window and a block fit 32 bits (W < 2^31, blocks <= 2^14 bases): the arithmetic is 32-bit, only
     // the chunk addresses are 64-bit
     const int32_t W = (int32_t)P.W, delta = (int32_t)g.delta, ox0 = (int32_t)it->ox0, ox1 = (int32_t)it->ox1;
     const intptr_t row = (intptr_t)(uintptr_t)g.row;
     const int nops = it->nops;
-    // pass 1: each op's interior chunks
+    // the item's ops, loaded once by the warp (lane j: ops j and j + 32) and broadcast op by op, so that the pass does
+    // not wait on one dependent load per op
+    uint2 r0 = make_uint2(0u, 0u), r1 = make_uint2(0u, 0u);
+    if (lane < nops) r0 = *(const uint2*)(ops + lane);
+    if (lane + 32 < nops) r1 = *(const uint2*)(ops + lane + 32);
     for (int k = 0; k < nops; k++) {
-        const Op o = ops[k];
+        const uint32_t ox = __shfl_sync(0xffffffffu, k < 32 ? r0.x : r1.x, k & 31);
+        const uint32_t oy = __shfl_sync(0xffffffffu, k < 32 ? r0.y : r1.y, k & 31);
+        Op o;
+        o.src = ox; o.dk = (uint16_t)(oy & 0xFFFFu); o.len = (uint16_t)(oy >> 16);
         const int32_t d0 = (int32_t)op_dst(o) > ox0 ? (int32_t)op_dst(o) : ox0;
         const int32_t d1 = (int32_t)(op_dst(o) + o.len) < ox1 ? (int32_t)(op_dst(o) + o.len) : ox1;
         const int32_t lo = g.rcw ? W - (d1 - delta) : d0 - delta, hi = g.rcw ? W - (d0 - delta) : d1 - delta;   // its row bytes
@@ -792,43 +820,54 @@ __device__ void emit_ops(const Params& P, const Item* it, const Op* ops, const L
             const int32_t wpf = g.rcw ? W - 16 - ro : ro;
             uint32_t v[4];
             op_src16<LG>(it, R, L, o, wpf + delta, v);
-            put16(P, it, g, (uintptr_t)c, wpf, v, true);
+            put16(P, cit, g, (uintptr_t)c, wpf, v, true);
         }
     }
-    // pass 2: the chunks around op boundaries and the ends of the range. Boundary b (0 .. nops) is the row offset where
-    // op b starts (b = 0: the range's first byte in window order) or, b = nops, where the range ends; its chunk is
-    // handled unless the boundary is 16-byte aligned in memory or another boundary's lane already has that chunk.
-    for (int b = lane; b <= nops; b += 32) {
-        const int32_t wb = b == 0 ? ox0 - delta : b == nops ? ox1 - delta : (int32_t)op_dst(ops[b]) - delta;   // window position
-        const int32_t ob = g.rcw ? W - wb : wb;        // the boundary's row offset (a reversed row: its end there)
-        const intptr_t ab = row + ob;
-        const int32_t wprev = b == 0 ? 0 : b - 1 == 0 ? ox0 - delta : (int32_t)op_dst(ops[b - 1]) - delta;
-        const intptr_t aprev = row + (g.rcw ? W - wprev : wprev);
-        if ((ab & 15) == 0 || (b > 0 && (aprev & ~(intptr_t)15) == (ab & ~(intptr_t)15) && (aprev & 15) != 0)) continue;
-        const intptr_t c = ab & ~(intptr_t)15;
-        const int32_t ro = (int32_t)(c - row);
-        const int32_t wpf = g.rcw ? W - 16 - ro : ro;
-        const int32_t blo = wpf + delta;
-        const int32_t klo = blo > ox0 ? blo : ox0, khi = blo + 16 < ox1 ? blo + 16 : ox1;
-        if (klo >= khi) continue;
-        int k = 0, hk = nops;                       // the op covering klo: the first ending after it
-        while (k < hk) {
-            const int m = (k + hk) >> 1;
-            if ((int32_t)(op_dst(ops[m]) + ops[m].len) <= klo) k = m + 1; else hk = m;
-        }
-        if (k >= nops) continue;
-        uint32_t v[4];
-        op_src16<LG>(it, R, L, ops[k], blo, v);
-        for (int kk = k + 1; kk < nops; kk++) {
-            const Op q = ops[kk];
-            const int32_t dst = (int32_t)op_dst(q);
-            if (dst >= khi) break;
-            uint32_t u[4];
-            op_src16<LG>(it, R, L, q, blo, u);
-            merge_from(v, u, dst - blo);
-        }
-        put16(P, it, g, (uintptr_t)c, wpf, v, false);
+}
+// Boundary b (0 .. nops) is the row offset where op b starts (b = 0: the range's first byte in window order) or, b =
+// nops, where the range ends; its chunk is handled unless the boundary is 16-byte aligned in memory or the lane of
+// boundary b - 1 already has that chunk.
+template <bool LG>
+__device__ __forceinline__ void emit_boundary(const Params& P, const Item* it, const Item* cit, const OutRange& g, const Op* ops,
+                                              const LitSrc& L, const RefView& R, int b) {
+    const int32_t W = (int32_t)P.W, delta = (int32_t)g.delta, ox0 = (int32_t)it->ox0, ox1 = (int32_t)it->ox1;
+    const intptr_t row = (intptr_t)(uintptr_t)g.row;
+    const int nops = it->nops;
+    const int32_t wb = b == 0 ? ox0 - delta : b == nops ? ox1 - delta : (int32_t)op_dst(ops[b]) - delta;   // window position
+    const int32_t ob = g.rcw ? W - wb : wb;        // the boundary's row offset (a reversed row: its end there)
+    const intptr_t ab = row + ob;
+    const int32_t wprev = b == 0 ? 0 : b - 1 == 0 ? ox0 - delta : (int32_t)op_dst(ops[b - 1]) - delta;
+    const intptr_t aprev = row + (g.rcw ? W - wprev : wprev);
+    if ((ab & 15) == 0 || (b > 0 && (aprev & ~(intptr_t)15) == (ab & ~(intptr_t)15) && (aprev & 15) != 0)) return;
+    const intptr_t c = ab & ~(intptr_t)15;
+    const int32_t ro = (int32_t)(c - row);
+    const int32_t wpf = g.rcw ? W - 16 - ro : ro;
+    const int32_t blo = wpf + delta;
+    const int32_t klo = blo > ox0 ? blo : ox0, khi = blo + 16 < ox1 ? blo + 16 : ox1;
+    if (klo >= khi) return;
+    int k = 0, hk = nops;                       // the op covering klo: the first ending after it
+    while (k < hk) {
+        const int m = (k + hk) >> 1;
+        if ((int32_t)(op_dst(ops[m]) + ops[m].len) <= klo) k = m + 1; else hk = m;
     }
+    if (k >= nops) return;
+    uint32_t v[4];
+    op_src16<LG>(it, R, L, ops[k], blo, v);
+    for (int kk = k + 1; kk < nops; kk++) {
+        const Op q = ops[kk];
+        const int32_t dst = (int32_t)op_dst(q);
+        if (dst >= khi) break;
+        uint32_t u[4];
+        op_src16<LG>(it, R, L, q, blo, u);
+        merge_from(v, u, dst - blo);
+    }
+    put16(P, cit, g, (uintptr_t)c, wpf, v, false);
+}
+template <bool LG>
+__device__ void emit_ops(const Params& P, const Item* it, const Op* ops, const LitSrc& L, const RefView& R, int lane) {
+    const OutRange g = out_range(P, it);
+    emit_op_chunks<LG>(P, it, it, g, ops, L, R, lane);
+    for (int b = lane; b <= (int)it->nops; b += 32) emit_boundary<LG>(P, it, it, g, ops, L, R, b);
 }
 
 // ---------------------------------------------------------------- TMA bulk copies and the mbarrier they complete on
@@ -1230,7 +1269,7 @@ __global__ void __launch_bounds__(CTA, 6) pv_windows_kernel(const __grid_constan
         }
     }
     __syncwarp();
-    if (it->state == ST_OK) emit_ops<false>(P, it, it->ops, LitSrc{smem_addr(it->lits), nullptr, nullptr}, slot_ref<PK>(P, slot), lane);
+    if (it->state == ST_OK) emit_ops<false>(P, it, it->ops, LitSrc{smem_addr(it->lits), nullptr, nullptr, 0}, slot_ref<PK>(P, slot), lane);
     else if (it->state == ST_CACHED) emit_cached(P, it, lane);
     __syncwarp();
     if (lane == 0 && item < P.total && it->state != ST_HEAVY) trace_done(P, it, 1);
@@ -1323,8 +1362,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
     trace_at(P, i, 1);
     if (it->state != ST_LOCATED) return;
     item_span(P, it, false, ~0ull);              // (L2 only: any length)
-    if (!PK && it->span_len)
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(C.ref + it->span_lo), "r"(it->span_len) : "memory");
+    if (!PK && it->span_len)        // (evict-last: the call's output stores should not push it out before the emission reads it)
+        asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" :: "l"(C.ref + it->span_lo), "r"(it->span_len),
+                     "l"(l2_evict_last()) : "memory");
     int r = DEC_ABORT;
     if (!P.force_block) {
         WindowSink sk{it->ops, it->lits, it->ox0, it->ox1, 0, 0};
@@ -1417,7 +1457,7 @@ __global__ void __launch_bounds__(CTA, 8) pv_emit_kernel(const __grid_constant__
         if (st0 == ST_OK || st0 == ST_CACHED) {
             item_runs_warp(P, it, lane);
             if (lane == 0) trace_at(P, item, 5);
-            if (st0 == ST_OK) emit_ops<true>(P, it, pi->ops, LitSrc{0, pi->lits, PK ? nullptr : C.rcref}, R, lane);
+            if (st0 == ST_OK) emit_ops<true>(P, it, pi->ops, LitSrc{0, pi->lits, PK ? nullptr : C.rcref, l2_evict_first()}, R, lane);
             else emit_cached(P, it, lane);
         }
         __syncwarp();
