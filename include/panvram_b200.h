@@ -320,9 +320,12 @@ size_t pv_index_bytes(uint32_t Q, uint64_t nblocks, uint32_t ckpt_shift);
 /* Decode every block of the cohort once on the device (blocks served from the block cache are skipped) and write its
  * checkpoints into out (pv_index_bytes bytes, 16-byte aligned, device). cohort->ckpt is ignored. *nbad (device uint64,
  * zeroed by the caller, or NULL) counts the blocks that failed. brun (device uint32 [nblocks], or NULL) receives the
- * blocks' first lower-case runs (pv_dev_cohort.brun). Asynchronous on `stream`. */
+ * blocks' first lower-case runs (pv_dev_cohort.brun). cost (device uint16 [nblocks], or NULL) receives each block's
+ * decode cost: the largest, over its stride cells, of the events starting in the cell plus the literal bytes decoded
+ * in it (the serial work of the block's costliest window item; 0 for a cached or failed block, saturating at 65535).
+ * Asynchronous on `stream`. */
 int pv_index_build(const pv_dev_cohort* cohort, uint64_t nblocks, uint32_t ckpt_shift, pv_ckpt* out, uint64_t* nbad, uint32_t* brun,
-                   void* stream);
+                   uint16_t* cost, void* stream);
 
 /* out[i] = the complement of ref[n - 1 - i] (A <-> T, C <-> G, every other byte as it is), i < n: the reverse-complement
  * reference of pv_dev_cohort.rcref (no counterpart in the reference, which reverses and complements each copied byte).

@@ -110,7 +110,7 @@ for _name, _res, _args in (
         ("pv_windows_items", _SZ, [ctypes.POINTER(DevCohort), _I64, _I64]),
         ("pv_rc_reference", _I32, [_P, _U64, _P, _P]),
         ("pv_windows_trace", _I32, [ctypes.POINTER(DevCohort), _P, _P, _I64, _I64, _P, _I32, _I32, _U32, _P, _P, _P, _SZ, _P, _SZ, _P]),
-        ("pv_index_build", _I32, [ctypes.POINTER(DevCohort), _U64, _U32, _P, _P, _P, _P])):
+        ("pv_index_build", _I32, [ctypes.POINTER(DevCohort), _U64, _U32, _P, _P, _P, _P, _P])):
     _f = getattr(_lib, _name)
     _f.restype, _f.argtypes = _res, _args
 
@@ -450,6 +450,7 @@ def coords_from_host(asm, start, rc, device):
 
 
 PV_CKPT_BAD = 1
+PV_CKPT_CACHED = 2
 TRACE_PHASES = ("start", "located", "decode_start", "decoded", "emit_start", "runs_found", "emitted")
 
 
@@ -480,7 +481,13 @@ def trace_summary(trace):
     state = (info >> np.uint64(8)) & np.uint64(15)
     form = (info >> np.uint64(12)) & np.uint64(3)
     ok = (state == 1) & (t[:, 6] > 0)
-    r = {"items": int(len(t)), "decoded": int(ok.sum())}
+    r = {"items": int(len(t)), "decoded": int(ok.sum()),
+         "states": {int(k): int(v) for k, v in zip(*np.unique(state, return_counts=True))}}
+    hv = (state == 2) & (t[:, 6] > 0)               # the general path's items (pv_heavy_kernel): their whole time
+    if hv.any():
+        h0 = t[hv, 0]
+        r["heavy_ns"] = {"count": int(hv.sum()), "max_end": float((t[hv, 6] - t[:, 0][t[:, 0] > 0].min()).max()),
+                         "max_span": float((t[hv, 6] - h0).max())}
     if not ok.any():
         return r
     t, info, form = t[ok], info[ok], form[ok]
@@ -511,20 +518,22 @@ def trace_summary(trace):
 def index_build(dev, nblocks, ckpt_shift, device):
     """The cohort's checkpoint index on `device` (pv_index_build: every block decoded once on the device; blocks in the
     block cache skipped) -> (uint8 tensor of pv_ckpt records, int32 tensor of each block's first lower-case run, number
-    of blocks that failed to decode). Waits for it."""
+    of blocks that failed to decode, int32 tensor of each block's decode cost: events + literal bytes of its costliest
+    stride cell). Waits for it."""
     nbytes = int(_lib.pv_index_bytes(int(dev.Q), int(nblocks), int(ckpt_shift)))
     if not nbytes:
         raise ValueError(f"checkpoint stride 2^{ckpt_shift}: a power of two from 256 to the block size {dev.Q}")
     out = torch.empty(nbytes, dtype=torch.uint8, device=device)
     brun = torch.empty(max(1, int(nblocks)), dtype=torch.int32, device=device)
     nbad = torch.zeros(1, dtype=torch.int64, device=device)
+    cost = torch.zeros(max(1, int(nblocks)), dtype=torch.int16, device=device)
     with torch.cuda.device(device):
         code = _lib.pv_index_build(ctypes.byref(dev), int(nblocks), int(ckpt_shift), out.data_ptr(), nbad.data_ptr(), brun.data_ptr(),
-                                   torch.cuda.current_stream(device).cuda_stream)
+                                   cost.data_ptr(), torch.cuda.current_stream(device).cuda_stream)
         if code:
             raise RuntimeError("panvram_b200 index: " + (_lib.pv_kernels_last_error() or b"").decode())
         torch.cuda.current_stream(device).synchronize()
-    return out, brun, int(nbad.item())
+    return out, brun, int(nbad.item()), cost.to(torch.int32) & 0xFFFF
 
 
 def rc_reference(ref_padded, n, device):

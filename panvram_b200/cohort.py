@@ -111,12 +111,11 @@ class Cohort:
         # PV_WIN_* flags added to every window launch: _C.PV_WIN_FUSED / PV_WIN_SPLIT pin the kernel form (default: by
         # call size); the output is the same
         self.launch_flags = 0
-        if block_cache:
-            self._build_block_cache(pools)
         self._ckpt, self.checkpoint_stride, self.bad_blocks = None, 0, 0
         stride = self.CHECKPOINT_STRIDE if checkpoint_stride is None else int(checkpoint_stride)
-        if stride:
-            self._build_index(min(stride, core.Q))
+        cost = self._build_index(min(stride, core.Q)) if stride else None
+        if block_cache:
+            self._build_block_cache(pools, cost)
         # the reference reverse-complemented, for the byte form: the split emission reads reverse-complement copies
         # forward from it (one more copy of the reference, ref_n bytes)
         self._rcref = None
@@ -125,21 +124,23 @@ class Cohort:
             self._devc.rcref = self._rcref.data_ptr() + 64
 
     def _build_index(self, stride):
-        """The checkpoint index (pv_index_build): every block not in the block cache decoded once on the device, its
-        decoder state kept at the last event boundary at or before each multiple of `stride` in the block. Window items
-        then cover one stride each: each decodes from its checkpoint to the end of its range only, so a window's serial
-        chains are about a stride long instead of a block, and the blocks outside the window's span are not decoded.
-        Decoding every block here also validates it: a block that fails is marked, and windows touching it report
-        status 1 exactly as when they decoded it in full. Alongside, each block's first lower-case run (4 bytes per
-        block), so an item finds its runs in a step or two instead of a binary search of the assembly's runs."""
+        """The checkpoint index (pv_index_build): every block decoded once on the device, its decoder state kept at the
+        last event boundary at or before each multiple of `stride` in the block. Window items then cover one stride
+        each: each decodes from its checkpoint to the end of its range only, so a window's serial chains are about a
+        stride long instead of a block, and the blocks outside the window's span are not decoded. Decoding every block
+        here also validates it: a block that fails is marked, and windows touching it report status 1 exactly as when
+        they decoded it in full. Alongside, each block's first lower-case run (4 bytes per block), so an item finds its
+        runs in a step or two instead of a binary search of the assembly's runs. -> each block's decode cost (device
+        int32: the events and literal bytes of its costliest stride cell), which picks blocks for the block cache."""
         if stride & (stride - 1) or not 256 <= stride <= self._core.Q:
             raise ValueError(f"checkpoint_stride: a power of two from 256 to the block size ({self._core.Q}), or 0")
         shift = stride.bit_length() - 1
         asms = self._dev["asms"].cpu().numpy().view(np.uint64).reshape(-1, 8)
         nblocks = int(asms[:, 2].sum())
-        self._ckpt, self._brun, self.bad_blocks = _C.index_build(self._devc, nblocks, shift, self.device)
+        self._ckpt, self._brun, self.bad_blocks, cost = _C.index_build(self._devc, nblocks, shift, self.device)
         self._devc.ckpt, self._devc.ckpt_shift, self._devc.brun = self._ckpt.data_ptr(), shift, self._brun.data_ptr()
         self.checkpoint_stride = stride
+        return cost
 
     @property
     def item_cell(self):
@@ -148,24 +149,36 @@ class Cohort:
         return self.checkpoint_stride or self._core.Q
 
     CACHE_BYTES = 4 << 30
+    # with an index: also cache this fraction of the blocks, the costliest to decode (their costliest stride cell), so
+    # that no window item's serial chain is much longer than a typical one's (a call lasts as long as its longest chain)
+    CACHE_COSTLY = 0.002
 
-    def _build_block_cache(self, pools):
+    def _build_block_cache(self, pools, cost=None):
         """Decode once, into an HBM cache, the blocks whose rANS stream is at least Q/32 bytes - literal-heavy novel
-        sequence, whose serial decode is many times longer than a typical block's - and point their block-table entries
-        at the cache (PV_BLOCK_CACHED): windows then copy those bytes instead of decoding them. A block that fails to
-        decode stays uncached, so a window touching it still reports status 1. At most CACHE_BYTES (the longest
-        streams first)."""
+        sequence, whose serial decode is many times longer than a typical block's - and, given the index's block costs,
+        the CACHE_COSTLY fraction of blocks whose costliest stride cell costs the most; point their block-table entries
+        (and their checkpoints) at the cache: windows then copy those bytes instead of decoding them. A block that
+        fails to decode stays uncached, so a window touching it still reports status 1. At most CACHE_BYTES (the
+        costliest, else the longest streams, first)."""
         Q = self._core.Q
         compact = self._core.compact_blocks
         if compact:
             plen = (pools["btab"][: len(pools["btab"]) - _C.PV_BLK_GROUP] & np.uint32(0xFFFF)).astype(np.int64)
         else:
             plen = (pools["blocks"][0::2] >> np.uint64(40)).astype(np.int64)
-        cand = np.nonzero((plen >= max(64, Q // 32)) & (plen < _C.PV_BLOCK_CACHED))[0]
+        want = (plen >= max(64, Q // 32)) & (plen < _C.PV_BLOCK_CACHED)
+        score = plen
+        if cost is not None and len(cost) == len(plen) and self.CACHE_COSTLY > 0:
+            k = max(1, int(len(cost) * (1.0 - self.CACHE_COSTLY)))
+            cut = int(torch.kthvalue(cost.float(), k).values.item())
+            c = cost.cpu().numpy()
+            want |= (c > max(cut, 0)) & (plen < _C.PV_BLOCK_CACHED)
+            score = c
+        cand = np.nonzero(want)[0]
         if len(cand) == 0:
             return
         if len(cand) * Q > self.CACHE_BYTES:
-            cand = np.sort(cand[np.argsort(-plen[cand], kind="stable")[: self.CACHE_BYTES // Q]])
+            cand = np.sort(cand[np.argsort(-score[cand], kind="stable")[: self.CACHE_BYTES // Q]])
         asms = pools["asms"].view(np.uint64).reshape(-1, 8)
         base, nbases = asms[:, 1].astype(np.int64), asms[:, 0].astype(np.int64)
         a = np.searchsorted(base, cand, side="right") - 1
@@ -213,6 +226,16 @@ class Cohort:
                 blk = self._dev["blocks"].view(torch.int64)
                 vals = torch.from_numpy((np.arange(len(blocks), dtype=np.uint64) | np.uint64(_C.PV_BLOCK_CACHED << 40)).view(np.int64)).to(dev)
                 blk[torch.from_numpy(2 * blocks).to(dev)] = vals
+            if len(blocks) and self._ckpt is not None:
+                # their checkpoints: every cell of a cached block says so, with the block's cache row (as the index
+                # build writes them for blocks it finds cached)
+                ncell = Q // self.checkpoint_stride
+                rec = self._ckpt.view(torch.int32).view(-1, 8)
+                rows = (torch.from_numpy(blocks.astype(np.int64)).to(dev)[:, None] * ncell + torch.arange(ncell, device=dev)).reshape(-1)
+                new = torch.zeros((len(rows), 8), dtype=torch.int32, device=dev)
+                new[:, 1] = torch.arange(len(blocks), dtype=torch.int32, device=dev).repeat_interleave(ncell)
+                new[:, 7] = _C.PV_CKPT_CACHED << 16
+                rec[rows] = new
             torch.cuda.synchronize(dev)
         self._cache, self.cached_blocks = cache, int(len(keep))
         self._devc.cache = cache.data_ptr() + 64

@@ -1503,13 +1503,19 @@ __global__ void __launch_bounds__(CTA) pv_heavy_kernel(const __grid_constant__ P
 // A block decoded once, from its start, by one lane; at every event boundary the sink sees the decoder's state and
 // writes it into the checkpoints whose offsets j S it is the last boundary at or before (pv_ckpt, packed the same way
 // dec_init_ck unpacks it).
+// It also counts each cell's decode cost - the events that start in it and the literal bytes decoded in it - and keeps
+// the largest: the serial work of the block's costliest window item.
 struct CkptSink {
     uint4* out;                  // the block's checkpoints, two uint4 each
     const uint8_t* base;         // the pooled payload's first byte
     uint32_t cs, ncell, jn;      // stride shift, checkpoints per block, the next one to write
     uint4 sa, sb;                // the last event boundary's state
+    uint32_t cell, cost, worst;  // the current cell, its cost so far, the largest cost of a finished cell
     __device__ __forceinline__ void put(uint32_t j) { out[2 * j] = sa; out[2 * j + 1] = sb; }
     __device__ __forceinline__ void at(const Dec<GlobalStream>& d) {
+        const uint32_t cj = d.o >> cs;
+        if (cj != cell) { worst = cost > worst ? cost : worst; cost = 0; cell = cj; }
+        cost++;
         while (jn < ncell && (jn << cs) < d.o) put(jn++);
         const uint64_t c[4] = {d.c0 + (uint64_t)PV_CKPT_BIAS, d.c1 + (uint64_t)PV_CKPT_BIAS, d.c2 + (uint64_t)PV_CKPT_BIAS,
                                d.c3 + (uint64_t)PV_CKPT_BIAS};
@@ -1522,13 +1528,14 @@ struct CkptSink {
         sb.w = d.o | (uint32_t)(((pos >> 32) & 0xFFu) << 24);
     }
     __device__ bool more() const { return true; }
-    __device__ bool lit(uint32_t, uint8_t) { return true; }
+    __device__ bool lit(uint32_t, uint8_t) { cost++; return true; }
     __device__ bool op(uint32_t, uint64_t, uint32_t, uint32_t) { return true; }
+    __device__ uint32_t costliest() const { return cost > worst ? cost : worst; }
 };
 
 template <bool PK, bool CP>
 __global__ void __launch_bounds__(128) pv_index_kernel(const pv_dev_cohort C, uint64_t nblk, uint32_t cs, uint32_t qs, uint4* out,
-                                                       unsigned long long* nbad, uint32_t* brun) {
+                                                       unsigned long long* nbad, uint32_t* brun, uint16_t* cost) {
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= nblk) return;
     int64_t lo = 0, hi = C.nasm;                    // the assembly: the last one whose first block is at or before i
@@ -1548,18 +1555,22 @@ __global__ void __launch_bounds__(128) pv_index_kernel(const pv_dev_cohort C, ui
     if (r.cache) {                                  // served from the block cache: its row, for every cell
         const uint32_t slot = (uint32_t)((uint64_t)(r.cache - C.cache) >> qs);
         for (uint32_t j = 0; j < ncell; j++) { o[2 * j] = make_uint4(0, slot, 0, 0); o[2 * j + 1] = make_uint4(0, 0, 0, PV_CKPT_CACHED << 16); }
+        if (cost) cost[i] = 0;
         return;
     }
     int res = DEC_ERR;
+    uint32_t worst = 0;
     if (CP || r.plen != (uint32_t)PV_BLEN_BAD) {
         const uint8_t* src = C.payload + r.poff;
-        CkptSink sk{o, C.payload, cs, ncell, 0, make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+        CkptSink sk{o, C.payload, cs, ncell, 0, make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), 0, 0, 0};
         Dec<GlobalStream> d;
         dec_init(d, GlobalStream{src, src + r.plen}, r.pst);
         const RefView V{C.ref, C.ref_n, 0, 0, 0, PK ? C.pref : nullptr, C.pruns, C.pidx};
         res = decode_events(d, GlobalTab{C.tabs + __ldg(&R.tab_off)}, V, blen, blen, sk);
         if (res == DEC_DONE) while (sk.jn < ncell) sk.put(sk.jn++);   // the last boundary's state for the rest
+        worst = sk.costliest();
     }
+    if (cost) cost[i] = (uint16_t)(res == DEC_DONE ? (worst < 0xFFFFu ? worst : 0xFFFFu) : 0u);
     if (res != DEC_DONE) {
         for (uint32_t j = 0; j < ncell; j++) { o[2 * j] = make_uint4(0, 0, 0, 0); o[2 * j + 1] = make_uint4(0, 0, 0, PV_CKPT_BAD << 16); }
         if (nbad) atomicAdd(nbad, 1ull);
@@ -2086,7 +2097,7 @@ extern "C" size_t pv_index_bytes(uint32_t Q, uint64_t nblocks, uint32_t ckpt_shi
 }
 
 extern "C" int pv_index_build(const pv_dev_cohort* cohort, uint64_t nblocks, uint32_t ckpt_shift, pv_ckpt* out, uint64_t* nbad,
-                              uint32_t* brun, void* stream) {
+                              uint32_t* brun, uint16_t* cost, void* stream) {
     static_assert(sizeof(pv_ckpt) == 32, "pv_ckpt is two 16-byte words");
     const uint32_t Q = cohort ? cohort->Q : 0;
     if (!cohort || !(Q == 1024 || Q == 2048 || Q == 4096 || Q == 16384) || !pv_index_bytes(Q, nblocks, ckpt_shift) || !out ||
@@ -2111,10 +2122,10 @@ extern "C" int pv_index_build(const pv_dev_cohort* cohort, uint64_t nblocks, uin
     unsigned long long* nb = (unsigned long long*)nbad;
     const int form = (cohort->packed ? 1 : 0) | (cohort->compact ? 2 : 0);
     switch (form) {
-    case 0: pv_index_kernel<false, false><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun); break;
-    case 1: pv_index_kernel<true, false><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun); break;
-    case 2: pv_index_kernel<false, true><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun); break;
-    default: pv_index_kernel<true, true><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun); break;
+    case 0: pv_index_kernel<false, false><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun, cost); break;
+    case 1: pv_index_kernel<true, false><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun, cost); break;
+    case 2: pv_index_kernel<false, true><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun, cost); break;
+    default: pv_index_kernel<true, true><<<grid, 128, 0, st>>>(*cohort, nblocks, ckpt_shift, qs, (uint4*)out, nb, brun, cost); break;
     }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_cuda_err, sizeof g_cuda_err, "%s", cudaGetErrorString(e)); return PV_ECUDA; }
