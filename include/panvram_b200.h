@@ -254,8 +254,8 @@ size_t pv_windows_items(const pv_dev_cohort* cohort, int64_t n, int64_t W);
  * none; its logs time the decode ad hoc with clock64 / %globaltimer): trace (device uint64 [trace_records x 8],
  * trace_records >= pv_windows_items, zeroed by the caller) receives for item i the %globaltimer time (ns) at which it
  * reached each phase - word 0 start, 1 located (block, checkpoint, lower-case runs), 2 its decode starts (fused
- * kernel: after its staged copies landed), 3 decoded, 4 taken by the emission kernel (split form), 5 its lower-case
- * runs found there, 6 its bytes written - and in word 7: SM | item state << 8 | form << 12 (1 fused, 2 split) | decode
+ * kernel: after its staged copies landed), 3 decoded, 4 taken by the emission kernel (split form), 5 its header in
+ * the emission warp's slot, 6 its bytes written - and in word 7: SM | item state << 8 | form << 12 (1 fused, 2 split) | decode
  * from a checkpoint << 14 | ops << 16 | literal bytes << 32 | bases decoded << 48. A phase the item did not reach
  * stays 0. Same output as pv_windows_ex; the timer reads add a little time. */
 int pv_windows_trace(const pv_dev_cohort* cohort, const int64_t* asm_index, const int64_t* start, int64_t n, int64_t W,

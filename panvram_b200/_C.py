@@ -451,7 +451,7 @@ def coords_from_host(asm, start, rc, device):
 
 PV_CKPT_BAD = 1
 PV_CKPT_CACHED = 2
-TRACE_PHASES = ("start", "located", "decode_start", "decoded", "emit_start", "runs_found", "emitted")
+TRACE_PHASES = ("start", "located", "decode_start", "decoded", "emit_start", "header_copied", "emitted")
 
 
 def windows_trace(dev, wasm, wstart, W, rc=None, tokens=False, apply_case=True, flags=0):
@@ -504,7 +504,7 @@ def trace_summary(trace):
     r["emit_ns"] = stats(t[:, 6] - emit0)
     if split.any():
         r["emit_queue_ns"] = stats((t[:, 4] - t[:, 3])[split])
-        r["emit_runs_ns"] = stats((t[:, 5] - t[:, 4])[split])
+        r["emit_header_ns"] = stats((t[:, 5] - t[:, 4])[split])
     r["end_ns"] = stats(t[:, 6] - t0)
     r["call_ns"] = float(t[:, 6].max() - t0)
     r["bases_decoded"] = stats(info >> np.uint64(48))

@@ -1,27 +1,30 @@
 // pv_kernels.cu - the refrel3 v1 window decode on sm_100a (pv_windows of include/panvram_b200.h).
 //
 // Replaces the reference's three-kernel path (pv_queue_kernel -> pv_case_kernel -> pv_rc_tok_kernel,
-// pv_cuda.cu:38-147) with kernels that write every output byte once. Work item = (window, one block it touches).
+// pv_cuda.cu:38-147) with kernels that write every output byte once. Work item = (window, one stride cell of a block
+// it touches): with the cohort's checkpoint index (built at open by pv_index_kernel, which decodes every block once)
+// an item decodes from the checkpoint at or before its cell to the end of its output range; without an index the
+// cell is the whole block.
 //
 // The fused form, pv_windows_kernel (calls of few items: split_min_items), one item per warp, WARPS warps per CTA:
 //   * lane 0 stages into the warp's shared slot, with TMA bulk copies completing on one mbarrier (bounded wait:
-//     status 4), the assembly's compact decode table (pv_layout.h), the block's rANS stream and the reference span the
-//     block's start diagonal covers (for windows shorter than a block, only the span under the output range, the rest
-//     warmed in L2); then it decodes the stream in full (every validity check of refrel3.h:114-160, so a corrupt block
-//     reports status 1 exactly as the reference does) with the decoder state in registers, keeping only the ops and
-//     literal bytes that land inside the window. Each block's serial rANS chain runs in its own warp, so the chains'
-//     latencies overlap across warps.
-//   * the warp then writes the item's output range in 16-byte vector stores, chunks inside one op first (lane i
-//     every 32nd chunk; reference copies realigned with funnel shifts, reverse-complement copies byte-reversed,
-//     literals from the item's array), then the chunks around op boundaries, one lane each; lower-case runs, reverse
-//     complement and the token map (or the fused token-id map) are applied in registers before each store.
-//   * blocks in the cohort's block cache (decoded once at open) are copied from it like a reference span.
+//     status 4), the assembly's compact decode table (pv_layout.h), the item's rANS stream and the reference span
+//     its diagonal covers; then it decodes (every validity check of refrel3.h:114-160 on a block's full decode, so a
+//     corrupt block reports status 1 exactly as the reference does) with the decoder state in registers, keeping
+//     only the ops and literal bytes that land inside the item's range.
+//   * the warp then writes the item's output range in 16-byte vector stores (emit_ops): chunks inside one op first
+//     (lane i every 32nd chunk; reference copies realigned with funnel shifts, literals from the item's array), then
+//     the chunks around op boundaries, one lane each; lower-case runs, reverse complement and the token map (or the
+//     fused token-id map) are applied in registers before each store.
+//   * items from the cohort's block cache (decoded once at open) are copied from it.
 //   * items needing the general path (a self copy inside the window, or more ops / literals than a slot holds) are
 //     decoded again by the whole CTA into a Q-byte block buffer in the caller's scratch, ops executed in order, then
 //     emitted the same way.
-// The split form (larger calls): pv_decode_kernel decodes one item per lane (up to 32 chains per warp, as many as keep
-// about 3,072 decode warps in flight; tables through L1) into a plan in the caller's scratch, then pv_emit_kernel
-// emits one item per warp as above.
+// The split form (larger calls): pv_decode_kernel decodes one item per lane (as many per warp as keep about 3,072
+// decode warps in flight; tables through L1; the item's reference span warmed into L2) into a plan in the caller's
+// scratch, with the item's lower-case runs; pv_emit_kernel, persistent, emits one item per warp from a queue, reading
+// the plan in place (reverse-complement copies read forward from the reverse-complemented reference); pv_heavy_kernel
+// takes the general-path items.
 // Also here: pv_sample_coords_kernel, sample()'s coordinate arithmetic and (pv_sample_draw_coords) the draws torch's
 // randint / rand would make, restated on curand's Philox states; small kernels that move window coordinates from and
 // the status word to pinned host memory without a copy engine. The window kernels are launched with programmatic
@@ -113,8 +116,8 @@ constexpr uint64_t NO_CK = ~0ull;
 
 // The trace (pv_windows_trace): per item, %globaltimer (ns) when it reaches each phase - 0 start, 1 located (block,
 // checkpoint, case runs), 2 its decode starts (the fused kernel: its slot's copies have landed), 3 decoded, 4 the
-// emission kernel takes it (split form), 5 its lower-case runs are found there, 6 emitted - and word 7: SM | state << 8 | form
-// << 12 (1 fused, 2 split) | from a checkpoint << 14 | ops << 16 | literals << 32 | decoded bases << 48.
+// emission kernel takes it (split form), 5 its header is in the emission warp's slot, 6 emitted - and word 7: SM |
+// state << 8 | form << 12 (1 fused, 2 split) | from a checkpoint << 14 | ops << 16 | literals << 32 | decoded bases << 48.
 __device__ __forceinline__ uint64_t gtime() { uint64_t t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); return t; }
 __device__ __forceinline__ void trace_at(const Params& P, uint64_t item, int k) { if (P.trace) P.trace[item * 8 + k] = gtime(); }
 template <class It>
@@ -791,10 +794,10 @@ __device__ __forceinline__ void merge_from(uint32_t v[4], const uint32_t u[4], i
 // complement / tokens in registers. Then (emit_boundary) the chunks the first pass left: those holding an op boundary,
 // or an end of the item's range, off a 16-byte boundary - one lane each, its bytes gathered from every op it overlaps
 // (the op covering its first byte, then each op starting inside it over it from its start). it: the item's header
-// (shared slot); ops and literal bytes in the slot too, or (LG) read in place from the item's record in the plan. cit:
-// the header whose lower-case runs cover the item (the item's own, or its group's); g = out_range(P, it).
+// (shared slot); ops and literal bytes in the slot too, or (LG) read in place from the item's record in the plan;
+// g = out_range(P, it).
 template <bool LG>
-__device__ __forceinline__ void emit_op_chunks(const Params& P, const Item* it, const Item* cit, const OutRange& g, const Op* ops,
+__device__ __forceinline__ void emit_op_chunks(const Params& P, const Item* it, const OutRange& g, const Op* ops,
                                                const LitSrc& L, const RefView& R, int lane) {
     // offsets inside a window and a block fit 32 bits (W < 2^31, blocks <= 2^14 bases): the arithmetic is 32-bit, only
     // the chunk addresses are 64-bit
@@ -820,7 +823,7 @@ __device__ __forceinline__ void emit_op_chunks(const Params& P, const Item* it, 
             const int32_t wpf = g.rcw ? W - 16 - ro : ro;
             uint32_t v[4];
             op_src16<LG>(it, R, L, o, wpf + delta, v);
-            put16(P, cit, g, (uintptr_t)c, wpf, v, true);
+            put16(P, it, g, (uintptr_t)c, wpf, v, true);
         }
     }
 }
@@ -828,7 +831,7 @@ __device__ __forceinline__ void emit_op_chunks(const Params& P, const Item* it, 
 // nops, where the range ends; its chunk is handled unless the boundary is 16-byte aligned in memory or the lane of
 // boundary b - 1 already has that chunk.
 template <bool LG>
-__device__ __forceinline__ void emit_boundary(const Params& P, const Item* it, const Item* cit, const OutRange& g, const Op* ops,
+__device__ __forceinline__ void emit_boundary(const Params& P, const Item* it, const OutRange& g, const Op* ops,
                                               const LitSrc& L, const RefView& R, int b) {
     const int32_t W = (int32_t)P.W, delta = (int32_t)g.delta, ox0 = (int32_t)it->ox0, ox1 = (int32_t)it->ox1;
     const intptr_t row = (intptr_t)(uintptr_t)g.row;
@@ -861,13 +864,13 @@ __device__ __forceinline__ void emit_boundary(const Params& P, const Item* it, c
         op_src16<LG>(it, R, L, q, blo, u);
         merge_from(v, u, dst - blo);
     }
-    put16(P, cit, g, (uintptr_t)c, wpf, v, false);
+    put16(P, it, g, (uintptr_t)c, wpf, v, false);
 }
 template <bool LG>
 __device__ void emit_ops(const Params& P, const Item* it, const Op* ops, const LitSrc& L, const RefView& R, int lane) {
     const OutRange g = out_range(P, it);
-    emit_op_chunks<LG>(P, it, it, g, ops, L, R, lane);
-    for (int b = lane; b <= (int)it->nops; b += 32) emit_boundary<LG>(P, it, it, g, ops, L, R, b);
+    emit_op_chunks<LG>(P, it, g, ops, L, R, lane);
+    for (int b = lane; b <= (int)it->nops; b += 32) emit_boundary<LG>(P, it, g, ops, L, R, b);
 }
 
 // ---------------------------------------------------------------- TMA bulk copies and the mbarrier they complete on
@@ -992,6 +995,31 @@ __device__ void item_ckpt(const Params& P, Item* it) {
     it->cst = (int64_t)(ck_diag(lo, b.z) << 1) | (int64_t)((b.z >> 7) & 1u);
 }
 
+// one lane: the lower-case runs overlapping the item's output range, from r0, the block's first run (C.brun)
+__device__ __noinline__ void item_runs_from(const Params& P, Item* it, uint32_t r0) {
+    const pv_dev_cohort& C = P.C;
+    const pv_asm_rec& R = C.asms[it->a];
+    it->run_cnt = 0;
+    if (!(P.apply_case && !P.tokens && R.low_cnt)) return;
+    const uint64_t x0 = it->bst + it->ox0, x1 = it->bst + it->ox1, s = it->s;
+    const uint64_t* low = C.low + 2 * R.low_base;
+    uint64_t lo = r0;
+    if (!C.brun) {
+        uint64_t hi = R.low_cnt;
+        lo = 0;
+        while (lo < hi) { const uint64_t m = (lo + hi) >> 1; if (__ldg(low + 2 * m + 1) <= x0) lo = m + 1; else hi = m; }
+    }
+    while (lo < R.low_cnt && __ldg(low + 2 * lo + 1) <= x0) lo++;
+    uint64_t e = lo;
+    while (e < R.low_cnt && __ldg(low + 2 * e) < x1) e++;
+    it->run_first = (uint32_t)(R.low_base + lo); it->run_cnt = (uint32_t)(e - lo);
+    if (e - lo <= (uint64_t)RUN_CAP)
+        for (uint64_t r = lo; r < e; r++) {
+            const uint64_t rs = __ldg(low + 2 * r), re = __ldg(low + 2 * r + 1);
+            it->runs[2 * (r - lo)] = (int32_t)((rs > x0 ? rs : x0) - s);
+            it->runs[2 * (r - lo) + 1] = (int32_t)((re < x1 ? re : x1) - s);
+        }
+}
 // lane 0: the lower-case runs overlapping the item's output range (window-relative, clipped to it)
 __device__ void item_runs(const Params& P, Item* it) {
     const pv_dev_cohort& C = P.C;
@@ -1354,13 +1382,18 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
     trace_at(P, i, 0);
     if (!item_locate(P, i, it)) return;
     const pv_dev_cohort& C = P.C;
+    // the item's lower-case runs are found by this lane once its decode is done (the emission kernel then copies
+    // them with the item's header); the block's first run is loaded now, so that its latency overlaps the decode
+    const uint32_t brun0 = C.brun ? __ldg(C.brun + it->gblk) : 0u;
     // with a checkpoint index the item's checkpoint says everything the decode needs (block validated or not, served
-    // from the cache or not, its stream position); the block table is read only for the general path. The lower-case
-    // runs are found by the emission kernel, off this lane's serial chain.
+    // from the cache or not, its stream position); the block table is read only for the general path.
     if (C.ckpt) item_ckpt(P, it);
     else item_block_lane<CP>(P, it);
     trace_at(P, i, 1);
-    if (it->state != ST_LOCATED) return;
+    if (it->state != ST_LOCATED) {
+        if (it->state == ST_CACHED) item_runs_from(P, it, brun0);
+        return;
+    }
     item_span(P, it, false, ~0ull);              // (L2 only: any length)
     if (!PK && it->span_len)        // (evict-last: the call's output stores should not push it out before the emission reads it)
         asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" :: "l"(C.ref + it->span_lo), "r"(it->span_len),
@@ -1383,47 +1416,16 @@ __global__ void __launch_bounds__(DEC_THREADS, 24) pv_decode_kernel(const __grid
         trace_at(P, i, 3);
         it->nops = (uint16_t)sk.nops; it->nlits = (uint16_t)sk.nlits;
     }
-    if (r == DEC_DONE) it->state = ST_OK;
+    if (r == DEC_DONE) { it->state = ST_OK; item_runs_from(P, it, brun0); }
     else if (r == DEC_ABORT) {                   // the general path decodes the block from its start: its record
         if (C.ckpt) item_block_lane<CP>(P, it);
         if (it->state == ST_LOCATED) it->state = ST_HEAVY;
     } else { it->state = ST_ERR; report(P, it->w, PV_STATUS_DECODE); }
 }
 
-// The warp: the lower-case runs overlapping an item's output range, as item_runs finds them, eight candidate runs per
-// step read by eight lanes at once (from the block's first run: usually one step).
-__device__ void item_runs_warp(const Params& P, Item* it, int lane) {
-    const pv_dev_cohort& C = P.C;
-    const pv_asm_rec& R = C.asms[it->a];
-    const uint64_t cnt = R.low_cnt;
-    if (!(P.apply_case && !P.tokens && cnt)) return;
-    if (!C.brun) { if (lane == 0) item_runs(P, it); __syncwarp(); return; }
-    const uint64_t x0 = it->bst + it->ox0, x1 = it->bst + it->ox1, s = it->s;
-    const uint64_t* low = C.low + 2 * R.low_base;
-    const uint64_t r0 = __ldg(C.brun + it->gblk);
-    uint64_t first = cnt, last = cnt;               // the runs [first, last) ending after x0 and starting before x1
-    for (uint64_t base = r0; base < cnt; base += 32) {
-        const uint64_t r = base + lane;
-        const bool have = r < cnt;
-        const uint64_t rs = have ? __ldg(low + 2 * r) : ~0ull, re = have ? __ldg(low + 2 * r + 1) : ~0ull;
-        const uint32_t after = __ballot_sync(0xffffffffu, have && re > x0);
-        const uint32_t past = __ballot_sync(0xffffffffu, !have || rs >= x1);
-        if (first == cnt && after) first = base + __ffs(after) - 1;
-        if (past) { last = base + __ffs(past) - 1; break; }
-    }
-    if (first > last) first = last;
-    if (lane == 0) { it->run_first = (uint32_t)(R.low_base + first); it->run_cnt = (uint32_t)(last - first); }
-    if (last - first <= (uint64_t)RUN_CAP && (uint64_t)lane < last - first) {
-        const uint64_t r = first + lane, rs = __ldg(low + 2 * r), re = __ldg(low + 2 * r + 1);
-        it->runs[2 * lane] = (int32_t)((rs > x0 ? rs : x0) - s);
-        it->runs[2 * lane + 1] = (int32_t)((re < x1 ? re : x1) - s);
-    }
-    __syncwarp();
-}
-
 // pv_emit_kernel: persistent - as many CTAs as are resident at once - and each WARP on its own takes the next decoded
-// item from the queue and writes it: the item's header is copied into the warp's small shared slot (its lower-case
-// runs are found there by the warp), its ops and literal bytes are read in place from the plan, and the reference
+// item from the queue and writes it: the item's header (with the lower-case runs its decode lane found) is copied
+// into the warp's small shared slot, its ops and literal bytes are read in place from the plan, and the reference
 // bytes from global memory, where the decode kernel has just warmed the item's span into L2 - no staging and no wait,
 // so a warp goes from one item to the next at once, and a slot is a few hundred bytes (many warps per SM). A warp
 // that finishes takes the next item: no CTA-wide barrier. Items that need the general path are listed for
@@ -1454,8 +1456,7 @@ __global__ void __launch_bounds__(CTA, 8) pv_emit_kernel(const __grid_constant__
             __syncwarp();
             continue;
         }
-        if (st0 == ST_OK || st0 == ST_CACHED) {
-            item_runs_warp(P, it, lane);
+        if (st0 == ST_OK || st0 == ST_CACHED) {     // (the decode kernel found the item's runs)
             if (lane == 0) trace_at(P, item, 5);
             if (st0 == ST_OK) emit_ops<true>(P, it, pi->ops, LitSrc{0, pi->lits, PK ? nullptr : C.rcref, l2_evict_first()}, R, lane);
             else emit_cached(P, it, lane);
