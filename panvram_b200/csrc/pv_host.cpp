@@ -397,7 +397,7 @@ void pool(pv_core& C, const std::vector<std::string>& paths) {
     }
     C.low.assign(2 * std::max<uint64_t>(1, sl), 0);
     C.asms.assign(n, pv_asm_rec{});
-    C.tabs.assign(std::max<uint64_t>(16, st), 0);
+    C.tabs.assign(st + 16, 0);                            // (16 zero bytes after the last table: a lookup may read one entry ahead)
     C.ctg_asm.assign(sc, 0); C.ctg_local.assign(sc, 0); C.ctg_boff.assign(sc, 0); C.ctg_len.assign(sc, 0);
     std::mutex mu; std::string first;
     parallel_for(n, C.threads, [&](uint64_t i) {

@@ -182,7 +182,9 @@ def test_pools_padding(golden):
     assert not p["ref_padded"][:64].any() and not p["ref_padded"][-64:].any()
     assert not p["payload"][-64:].any()
     asms = p["asms"].view(np.uint64).reshape(-1, 8)
-    assert len(p["tabs"]) == int(asms[:, 6].sum()) and p["tab_max"] == int(asms[:, 6].max())
+    # the tables back to back, then 16 zero bytes (a dense-list lookup may read one entry ahead)
+    assert len(p["tabs"]) == int(asms[:, 6].sum()) + 16 and p["tab_max"] == int(asms[:, 6].max())
+    assert not p["tabs"][-16:].any()
 
 
 def test_cohort_is_gpu_only(golden):
