@@ -87,6 +87,49 @@ def test_block_cache_same_output(tmp_path_factory, oracle, cuda, Q):
                 assert int(st.item()) == 0 and np.array_equal(x.cpu().numpy(), want), (Q, W, tok, co.cached_blocks)
 
 
+@pytest.mark.parametrize("Q,stride", [(4096, None), (16384, 512)])
+def test_costly_blocks_cached(tmp_path_factory, oracle, cuda, monkeypatch, Q, stride):
+    """The block cache also takes the blocks whose costliest stride cell decodes longest (the index build's costs):
+    with a large fraction asked, blocks beyond the long-stream rule are cached, every checkpoint of a cached block
+    points at its cache row, and windows over them - both kernel forms - give the oracle's bytes."""
+    import panvram_b200 as P
+    from panvram_b200 import _C
+    d = str(tmp_path_factory.mktemp(f"costly{Q}"))
+    synth.make_cohort(d, "cfg1", Q=Q, nasm=3, scale=0.004)
+    ds = synth.dataset_of(Q)
+    monkeypatch.setattr(P.Cohort, "CACHE_COSTLY", 0.0)
+    c0 = P.Cohort.open(d, device=cuda, dataset=ds, checkpoint_stride=stride)
+    monkeypatch.setattr(P.Cohort, "CACHE_COSTLY", 0.3)
+    c = P.Cohort.open(d, device=cuda, dataset=ds, checkpoint_stride=stride)
+    assert c.cached_blocks > c0.cached_blocks > 0
+    blocks = c._dev["blocks"].cpu().numpy().view(np.uint64)
+    cached = np.nonzero((blocks[0::2] >> np.uint64(40)) == np.uint64(0xFFFFFE))[0]
+    assert len(cached) == c.cached_blocks
+    ncell = Q // c.checkpoint_stride
+    rec = c._ckpt.view(torch.int32).view(-1, 8).cpu().numpy()
+    slots = (blocks[0::2][cached] & np.uint64((1 << 40) - 1)).astype(np.int64)
+    for b, slot in zip(cached, slots):
+        r = rec[b * ncell:(b + 1) * ncell]
+        assert ((r[:, 7] >> 16) & _C.PV_CKPT_CACHED).all() and (r[:, 1] == slot).all()
+    ref = oracle.Reference(os.path.join(d, "reference.fa"))
+    arcs = [oracle.Archive(p, ref) for p in sorted(glob.glob(os.path.join(d, f"*.{ds}.rr3")))]
+    asms = c._core.pools()["asms"].view(np.uint64).reshape(-1, 8)
+    base = asms[:, 1].astype(np.int64)
+    rng = np.random.default_rng(Q + 1)
+    for W in (300, 2 * Q + 7):
+        asm, start = [], []
+        for g in rng.choice(cached, min(300, len(cached))):
+            a = int(np.searchsorted(base, g, side="right") - 1)
+            s = int((g - base[a]) * Q) + int(rng.integers(-W + 1, Q))
+            asm.append(a)
+            start.append(max(0, min(s, arcs[a].nbases - W)))
+        rcm = rng.random(len(asm)) < 0.5
+        want = oracle.windows(arcs, ref, np.array(asm), np.array(start), W, rc=rcm, threads=8)
+        for flags in (_C.PV_WIN_FUSED, _C.PV_WIN_SPLIT):
+            x, st = c._launch(torch.tensor(asm), torch.tensor(start), W, torch.from_numpy(rcm), False, True, flags=flags)
+            assert int(st.item()) == 0 and np.array_equal(x.cpu().numpy(), want), (Q, W, flags)
+
+
 @pytest.mark.parametrize("Q,stride", [(1024, None), (2048, None), (4096, None), (16384, None), (4096, 256), (16384, 512), (4096, 0),
                                       (16384, 0)])
 def test_synth_cohort_parity(tmp_path_factory, oracle, cuda, Q, stride):
