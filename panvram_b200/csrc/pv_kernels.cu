@@ -818,6 +818,24 @@ __device__ __forceinline__ void emit_op_chunks(const Params& P, const Item* it, 
         const int32_t d1 = (int32_t)(op_dst(o) + o.len) < ox1 ? (int32_t)(op_dst(o) + o.len) : ox1;
         const int32_t lo = g.rcw ? W - (d1 - delta) : d0 - delta, hi = g.rcw ? W - (d0 - delta) : d1 - delta;   // its row bytes
         const intptr_t a0 = (row + lo + 15) & ~(intptr_t)15, a1 = (row + hi) & ~(intptr_t)15;
+        if (LG && L.rc) {
+            // the byte form read in place: whatever the op's kind, a chunk's source is one address per op plus the
+            // chunk's window position - a literal's bytes in the plan, a copy's in the reference or, for a
+            // reverse-complement copy, read forward in the reverse-complemented reference (op_src16's addresses)
+            const uint32_t kind = op_kind(o);
+            const intptr_t dst = (intptr_t)op_dst(o), len = (intptr_t)o.len, src = (intptr_t)o.src;
+            const intptr_t base = kind == 0 ? (intptr_t)(uintptr_t)L.g + src - d0 + delta
+                                : kind == 3 ? (intptr_t)(uintptr_t)L.rc + (intptr_t)R.n - src - len - dst + delta
+                                            : (intptr_t)(uintptr_t)R.g + src - dst + delta;
+            for (intptr_t c = a0 + 16 * (intptr_t)lane; c < a1; c += 16 * 32) {
+                const int32_t ro = (int32_t)(c - row);
+                const int32_t wpf = g.rcw ? W - 16 - ro : ro;
+                uint32_t v[4];
+                ldg16u((const uint8_t*)(uintptr_t)(base + wpf), v, L.pol);
+                put16(P, it, g, (uintptr_t)c, wpf, v, true);
+            }
+            continue;
+        }
         for (intptr_t c = a0 + 16 * (intptr_t)lane; c < a1; c += 16 * 32) {
             const int32_t ro = (int32_t)(c - row);
             const int32_t wpf = g.rcw ? W - 16 - ro : ro;
