@@ -536,8 +536,16 @@ __device__ __forceinline__ uint32_t bytes_mask(int k0, int k1, int i) {   // byt
 }
 // L2 eviction priorities (createpolicy): evict_last for the reference spans the decode warms for the emission, so that
 // the call's output stores do not push them out first; evict_first for the bytes the emission has read.
-__device__ __forceinline__ uint64_t l2_evict_last() { uint64_t p; asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p)); return p; }
-__device__ __forceinline__ uint64_t l2_evict_first() { uint64_t p; asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p)); return p; }
+__device__ __forceinline__ uint64_t l2_evict_last() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
 __device__ __forceinline__ uint4 ldg_hint(const uint4* q, uint64_t pol) {
     uint4 v;
     asm("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(q), "l"(pol));
@@ -610,7 +618,8 @@ __device__ __noinline__ uint4 packed16(const uint32_t* pw, const pv_ref_run* run
 // global memory, reverse-complement copies byte-reversed and complemented.
 // Where an item's literal bytes are: in its shared slot (lits_sm, a shared address) or, for the emission kernel that
 // reads decoded items in place, in the plan in global memory (lits_g).
-struct LitSrc { uint32_t sm; const uint8_t* g; const uint8_t* rc; uint64_t pol; };   // (rc: the cohort's reverse-complement reference, or NULL; pol: an L2 policy for the loads, or 0)
+// (rc: the cohort's reverse-complement reference, or NULL; pol: an L2 policy for the loads, or 0)
+struct LitSrc { uint32_t sm; const uint8_t* g; const uint8_t* rc; uint64_t pol; };
 // (one load path for every kind, its address chosen by selects - the lanes of a pass often hold ops of different
 // kinds - then the byte reversal and complement of a reverse-complement copy)
 template <bool LG>
