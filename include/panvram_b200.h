@@ -175,6 +175,11 @@ uint32_t pv_core_q(const pv_core* c);                   /* Core.Q (:205) */
 uint64_t pv_core_ref_bases(const pv_core* c);           /* Core.ref_bases (:209) */
 void pv_core_ref_sha256(const pv_core* c, char hex[65]); /* Core.ref_sha256 (:210) */
 int pv_core_pools(const pv_core* c, pv_host_pools* out);/* Core.pools (pv_core.cpp:177-182) */
+/* Free the host copies of the reference and of the pooled payload (plain and packed forms), once the caller has
+ * copied them to its device: they are read for nothing else. pv_core_pools then reports them empty (earlier views of
+ * them dangle); the rest of the core - block table, lower-case runs, contigs, decode tables, every archive's
+ * metadata - stays. No counterpart in the reference, whose Core keeps them. */
+void pv_core_release_uploaded(pv_core* c);
 int pv_core_info(const pv_core* c, int64_t asm_index, pv_asm_info* out);   /* Core.info (pv_core.cpp:161-163) */
 /* reference name and path strings of Core.info; NUL-terminated, truncated to cap */
 int pv_core_info_strings(const pv_core* c, int64_t asm_index, char* path, size_t path_cap, char* refname, size_t ref_cap);

@@ -77,6 +77,7 @@ for _name, _res, _args in (
         ("pv_core_n", _I64, [_P]), ("pv_core_q", _U32, [_P]), ("pv_core_ref_bases", _U64, [_P]),
         ("pv_core_ref_sha256", None, [_P, ctypes.c_char_p]),
         ("pv_core_pools", _I32, [_P, ctypes.POINTER(HostPools)]),
+        ("pv_core_release_uploaded", None, [_P]),
         ("pv_core_info", _I32, [_P, _I64, ctypes.POINTER(AsmInfo)]),
         ("pv_core_info_strings", _I32, [_P, _I64, ctypes.c_char_p, _SZ, ctypes.c_char_p, _SZ]),
         ("pv_core_ncontigs", _I64, [_P, _I64]),
@@ -162,6 +163,11 @@ class Core:
         b = ctypes.create_string_buffer(65)
         _lib.pv_core_ref_sha256(self._h, b)
         return b.value.decode()
+
+    def release_uploaded(self):
+        """Free the host copies of the reference and the pooled payload once they are on the device (pools() then
+        gives them empty; views taken before dangle)."""
+        _lib.pv_core_release_uploaded(self._h)
 
     def pools(self):
         """Host arrays in the device layout (numpy views of the core's memory), keyed by component."""

@@ -122,6 +122,11 @@ class Cohort:
         if not packed:
             self._rcref = _C.rc_reference(self._dev["ref_padded"], core.ref_bases, self.device)
             self._devc.rcref = self._rcref.data_ptr() + 64
+        # the host copies of the reference and the payload are on the device now and read for nothing else: free them
+        # (at config 2 that is ~12 GB of host memory per process, per GPU)
+        torch.cuda.synchronize(self.device)
+        del pools
+        core.release_uploaded()
 
     def _build_index(self, stride):
         """The checkpoint index (pv_index_build): every block decoded once on the device, its decoder state kept at the

@@ -501,6 +501,13 @@ uint32_t pv_core_q(const pv_core* c) { return c->Q; }
 uint64_t pv_core_ref_bases(const pv_core* c) { return c->ref_n; }
 void pv_core_ref_sha256(const pv_core* c, char out[65]) { const std::string h = hex(c->ref_sha, 32); memcpy(out, h.c_str(), 65); }
 
+void pv_core_release_uploaded(pv_core* c) {
+    if (!c) return;
+    std::vector<uint8_t>().swap(c->ref);
+    std::vector<uint8_t>().swap(c->payload);
+    std::vector<uint32_t>().swap(c->pref);
+}
+
 int pv_core_pools(const pv_core* c, pv_host_pools* o) {
     o->ref_padded = c->ref.data(); o->ref_padded_bytes = c->ref.size();
     o->payload = c->payload.data(); o->payload_bytes = c->payload.size();
