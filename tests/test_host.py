@@ -187,6 +187,21 @@ def test_pools_padding(golden):
     assert not p["tabs"][-16:].any()
 
 
+def test_release_uploaded_keeps_the_rest(golden):
+    """After the cohort is on the device, the host copies of the reference and the payload are freed; the block table,
+    runs, tables, contigs and every archive's metadata stay, and the core still answers contigs / info."""
+    c = _C.Core(golden["ref"], paths(golden, "q4k"), 2)
+    before = c.pools()
+    kept = {k: before[k].copy() for k in ("blocks", "asms", "tabs", "low", "ctg_len")}
+    info0, ctg0 = c.info(0), c.contigs(0)
+    c.release_uploaded()
+    after = c.pools()
+    assert after["payload"].size == 0 and after["ref_padded"].size == 0
+    for k, v in kept.items():
+        assert np.array_equal(after[k], v), k
+    assert c.info(0) == info0 and c.contigs(0) == ctg0 and c.ref_bases > 0
+
+
 def test_cohort_is_gpu_only(golden):
     with pytest.raises(RuntimeError, match="GPU only"):
         P.Cohort.open(golden["dirs"]["q4k"], device="cpu", reference=golden["ref"])

@@ -1,6 +1,6 @@
 """The N>1 bench path's host logic on CPU ranks (gloo, world size 2): rank 0 generates the cohort while rank 1 waits
-for it; the job's time is its slowest rank's; the job's rate counts every rank's windows (replicas, weak scaling);
-global_batch gathers every rank's windows and coordinates in rank order."""
+for it; the ranks open it one after another; the job's time is its slowest rank's; the job's rate counts every rank's
+windows (replicas, weak scaling); global_batch gathers every rank's windows and coordinates in rank order."""
 import datetime
 import os
 import socket
@@ -34,8 +34,11 @@ def _rank(rank, world, port, data, q):
         co = torch.arange(12, dtype=torch.int64).view(3, 4) + 100 * rank
         X, Co = global_batch(x, co)
         gathered = (X[:, 0].tolist(), Co[:, 0].tolist())
+        # the ranks' cohort opens, one at a time: each turn starts after the previous rank's has ended
+        import time
+        (t_start, t_end), _ = bench.one_rank_at_a_time(rank, world, lambda: (time.time(), (time.sleep(0.3), time.time())[1]))
         dist.barrier()
-        q.put((rank, path, ds, ready, t, rate, gathered))
+        q.put((rank, path, ds, ready, t, rate, gathered, (t_start, t_end)))
     finally:
         dist.destroy_process_group()
 
@@ -51,7 +54,8 @@ def test_two_cpu_ranks(tmp_path):
     for p in procs:
         p.join(60)
         assert p.exitcode == 0
-    (r0, path0, ds0, ready0, t0, rate0, g0), (r1, path1, ds1, ready1, t1, rate1, g1) = got
+    (r0, path0, ds0, ready0, t0, rate0, g0, turn0), (r1, path1, ds1, ready1, t1, rate1, g1, turn1) = got
+    assert turn1[0] >= turn0[1]                                     # rank 1's open began after rank 0's ended
     assert (r0, r1) == (0, 1)
     assert path0 == path1 == os.path.join(str(tmp_path), "cfg0") and ds0 == ds1 == "q4k"
     assert ready0 and ready1
